@@ -1,0 +1,177 @@
+/*
+ * popkv_b200.h -- C ABI of the B200 (sm_100a) PopKV retrieval kernels.
+ *
+ * Every entry point takes plain device pointers, element counts and strides,
+ * a CUDA stream (cudaStream_t passed as void*, NULL = legacy default stream)
+ * and returns a status code (POPKV_OK on success).  On failure
+ * popkv_last_error() returns a message describing the most recent failing
+ * call on the calling host thread.  All work is enqueued asynchronously on
+ * the given stream; no entry point synchronises the device or allocates
+ * device memory.
+ *
+ * Each declaration names the reference interface it replaces (file:line in
+ * kw78999/PopKV).  The reference binds its kernels through pybind11 + torch
+ * (csrc/popkv_ext.cpp:39-52) and the Python wrappers in popkv_cuda.py and
+ * sparse_kernels.py; the Python package popkv_b200 keeps those Python
+ * signatures and calls these functions through ctypes.
+ *
+ * Layouts (token-major, as in the reference's PopKVCache.packed,
+ * popkv.py:89-96 and csrc/popkv_ext.cu:1166-1171):
+ *   k_sign, k_mag   int32  [kv_heads, capacity, W]    W = ceil(head_dim / 32)
+ *   k_low, k_delta  fp16   [kv_heads, capacity, R]    R = ceil(head_dim / G)
+ *   q_sign, q_mag   int32  [batch, q_heads, W]
+ *   q_low, q_delta  fp32   [batch, q_heads, R]
+ * Bit l of word w holds dimension 32*w + l.  G (dim_group_size) is 16, 32 or 64.
+ */
+#ifndef POPKV_B200_H
+#define POPKV_B200_H
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define POPKV_API __attribute__((visibility("default")))
+#else
+#define POPKV_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Element types of floating-point operands. */
+#define POPKV_DTYPE_F32 0
+#define POPKV_DTYPE_F16 1
+#define POPKV_DTYPE_BF16 2
+
+/* Status codes. */
+#define POPKV_OK 0
+#define POPKV_ERR_INVALID 1     /* an argument failed validation */
+#define POPKV_ERR_CAPACITY 2    /* token_offset + tokens exceeds the planes' capacity */
+#define POPKV_ERR_UNSUPPORTED 3 /* a valid request this build does not implement */
+#define POPKV_ERR_CUDA 4        /* the CUDA runtime reported an error */
+
+#define POPKV_ABI_VERSION 1
+
+/* Message of the last failing call on this host thread ("" if none). */
+POPKV_API const char* popkv_last_error(void);
+
+/* POPKV_ABI_VERSION of the loaded library. */
+POPKV_API int popkv_abi_version(void);
+
+/*
+ * Key bit-planes and low/delta representatives for `tokens` keys, written to
+ * rows [token_offset, token_offset + tokens) of the planes.
+ *
+ * Replaces ext.pack / ext.pack_dim (prepack; csrc/popkv_ext.cu:1058-1073,
+ * :1153-1175) and ext.pack_into / ext.pack_into_dim (append;
+ * csrc/popkv_ext.cu:1075-1092, :1177-1206), reached from popkv_cuda.pack_keys
+ * (popkv_cuda.py:53) and popkv_cuda.pack_keys_into (popkv_cuda.py:72).
+ * Token groups of `token_group_size` are counted from keys' first token.
+ * keys[h, t, d] is read at keys + h*key_head_stride + t*key_token_stride + d
+ * (strides in elements; d is contiguous).
+ */
+POPKV_API int popkv_pack(const void* keys, int keys_dtype, int64_t kv_heads, int64_t tokens,
+               int64_t head_dim, int64_t key_head_stride, int64_t key_token_stride,
+               int32_t* k_sign, int32_t* k_mag, uint16_t* k_low, uint16_t* k_delta,
+               int64_t capacity, int64_t token_offset, int64_t token_group_size,
+               int64_t dim_group_size, void* stream);
+
+/*
+ * Query bit-planes and representatives of `rows` = batch*q_heads queries
+ * [rows, head_dim] (contiguous).
+ *
+ * Replaces ext.query_encode_out (csrc/popkv_ext.cu:1315-1358), reached from
+ * popkv_cuda.query_encode (popkv_cuda.py:157).
+ */
+POPKV_API int popkv_query_encode(const void* queries, int queries_dtype, int64_t rows, int64_t head_dim,
+                       int64_t dim_group_size, int32_t* q_sign, int32_t* q_mag, float* q_low,
+                       float* q_delta, void* stream);
+
+/*
+ * Popcount scores of the first `tokens` cached keys against pre-encoded
+ * queries, for head_dim 128: scores fp16 [batch, q_heads, tokens].
+ * head_to_kv int64 [q_heads]; query heads that share a KV head must be
+ * consecutive (GQA layout arange(q_heads) // group).
+ *
+ * Replaces ext.score_encoded (csrc/popkv_ext.cu:1533-1593), reached from
+ * popkv_cuda.score_encoded (popkv_cuda.py:170).
+ */
+POPKV_API int popkv_score_encoded(const int32_t* q_sign, const int32_t* q_mag, const float* q_low,
+                        const float* q_delta, int64_t batch, int64_t q_heads,
+                        const int32_t* k_sign, const int32_t* k_mag, const uint16_t* k_low,
+                        const uint16_t* k_delta, int64_t kv_heads, int64_t capacity,
+                        const int64_t* head_to_kv, int64_t tokens, int64_t dim_group_size,
+                        uint16_t* scores, void* stream);
+
+/*
+ * Encode raw queries [batch, q_heads, head_dim] and score them.  For
+ * head_dim 128 the scores are fp16 (scores_dtype must be POPKV_DTYPE_F16);
+ * otherwise fp32 (POPKV_DTYPE_F32).
+ *
+ * Replaces ext.score and ext.score_dim (csrc/popkv_ext.cu:1208-1313), reached
+ * from popkv_cuda.score (popkv_cuda.py:190).
+ */
+POPKV_API int popkv_score(const void* queries, int queries_dtype, int64_t batch, int64_t q_heads,
+                int64_t head_dim, const int32_t* k_sign, const int32_t* k_mag,
+                const uint16_t* k_low, const uint16_t* k_delta, int64_t kv_heads,
+                int64_t capacity, const int64_t* head_to_kv, int64_t tokens,
+                int64_t dim_group_size, void* scores, int scores_dtype, void* stream);
+
+/*
+ * Per-row top-k with the current-token slot reserved.
+ *
+ * For each of `rows` rows of `tokens` scores (fp16 or fp32, row r at
+ * scores + r*row_stride elements) writes the k highest-scoring token indices
+ * in ascending index order to out[r*out_stride + 0 .. k-1] (int64).  Ties
+ * rank by lower token index; +0 and -0 are equal; NaN ranks highest.  When
+ * current_index >= 0 it is written to out[r*out_stride + k].
+ *
+ * Replaces torch.topk(scores, k, dim=-1, sorted=False).indices followed by
+ * _append_current (popkv.py:1094-1098, :287-291), whose order among equal
+ * scores is unspecified; also serves LlamaSparseDecoder.experimental_topk
+ * (popkv.py:1091-1093).
+ */
+POPKV_API int popkv_topk(const void* scores, int scores_dtype, int64_t rows, int64_t tokens,
+               int64_t row_stride, int64_t k, int64_t current_index, int64_t* out,
+               int64_t out_stride, void* stream);
+
+/*
+ * Split-token sparse attention partial states.
+ *
+ * queries [batch, q_heads, head_dim] (contiguous); prefix K/V element (b, h, t, d)
+ * at base + b*batch_stride + h*head_stride + t*token_stride + d; current K/V
+ * [batch, kv_heads, head_dim] (contiguous); indices int64 [batch, q_heads,
+ * selected]; valid uint8 [batch, q_heads, selected] or NULL; head_to_kv int64
+ * [q_heads].  Slot j of split s = j / split_tokens reads the current key/value
+ * when indices == prefix_tokens, else prefix row clamp(index, 0,
+ * prefix_tokens - 1); masked slots are skipped.  partials fp32
+ * [batch, q_heads, splits, head_dim + 2] = (max logit, sum exp, sum exp*v).
+ *
+ * Replaces sparse_kernels.indexed_attention_split_partial and its Triton
+ * kernel (sparse_kernels.py:321-364, :237-294), which are batch-1.
+ */
+POPKV_API int popkv_attn_partial(const void* queries, int queries_dtype, int64_t batch, int64_t q_heads,
+                       int64_t head_dim, const void* prefix_keys, const void* prefix_values,
+                       int kv_dtype, int64_t kv_heads, int64_t prefix_tokens,
+                       int64_t k_batch_stride, int64_t k_head_stride, int64_t k_token_stride,
+                       int64_t v_batch_stride, int64_t v_head_stride, int64_t v_token_stride,
+                       const void* current_keys, const void* current_values,
+                       const int64_t* indices, int64_t selected, const uint8_t* valid,
+                       const int64_t* head_to_kv, int64_t split_tokens, float* partials,
+                       void* stream);
+
+/*
+ * Log-sum-exp merge of split partial states into one output row per query
+ * head: out[r, d] = sum_s exp(m_s - M) acc_s[d] / sum_s exp(m_s - M) sum_s.
+ *
+ * Replaces sparse_kernels.indexed_attention_split_merge and its Triton kernel
+ * (sparse_kernels.py:367-387, :297-318).
+ */
+POPKV_API int popkv_attn_merge(const float* partials, int64_t rows, int64_t splits, int64_t head_dim,
+                     void* out, int out_dtype, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* POPKV_B200_H */

@@ -1,0 +1,451 @@
+// Split-token sparse attention over the selected cache rows (PopKV subsystem 4).
+//
+// Reference: sparse_kernels.py:237-294 (_indexed_attention_split_kernel) and
+// :297-318 (_indexed_attention_merge_kernel), launched from
+// indexed_attention_split_partial / _merge (sparse_kernels.py:321-387).
+//
+// Partial kernel, head_dim 128: one CTA per (batch*query head, split).  The
+// split's slots are processed in chunks of 256: the slot -> cache-row map is
+// staged in shared memory, then thread t (segment c = t % 16 of 8 dims, row
+// group g = t / 16) issues 16-byte loads of its 16 K rows and 16 V rows up front
+// (256 rows x 512 B per chunk in flight), reduces q.k across the 16 threads of
+// a row with shuffles, and folds the chunk into a running (max, sum, acc)
+// online-softmax state.  Arithmetic is fp32; the state is written as
+// [max, sum, acc[D]] per (row, split) exactly like the reference's partials.
+// A generic warp-per-split kernel covers other head dims.
+//
+// Slot semantics follow the reference: index == prefix_tokens selects the
+// current token's key/value, any other index reads prefix row
+// clamp(index, 0, prefix_tokens - 1); a masked slot contributes nothing.  A
+// split without a live slot keeps max = -inf, sum = 0, acc = 0 (the reference
+// produces NaN when a split's first 16-slot tile is fully masked).
+#include <cstdint>
+#include <type_traits>
+
+#include "common.cuh"
+
+namespace popkv {
+namespace {
+
+constexpr int kAttnThreads = 256;
+constexpr int kChunk = 256;
+constexpr int kSegThreads = 16;                            // threads per row (8 dims each)
+constexpr int kRowGroups = kAttnThreads / kSegThreads;     // 16
+constexpr int kRowsPerThread = kChunk / kRowGroups;        // 16
+constexpr int kSlotMasked = -2;
+constexpr int kSlotCurrent = -1;
+
+struct Raw8 {
+    uint4 a, b;  // b used only for fp32 elements
+};
+
+template <typename T>
+__device__ __forceinline__ Raw8 load_raw8(const T* p) {
+    Raw8 r;
+    r.a = __ldg(reinterpret_cast<const uint4*>(p));
+    if constexpr (sizeof(T) == 4) r.b = __ldg(reinterpret_cast<const uint4*>(p) + 1);
+    else r.b = make_uint4(0, 0, 0, 0);
+    return r;
+}
+
+template <typename T>
+__device__ __forceinline__ void unpack8(const Raw8& r, float* f) {
+    if constexpr (sizeof(T) == 4) {
+        f[0] = __uint_as_float(r.a.x); f[1] = __uint_as_float(r.a.y);
+        f[2] = __uint_as_float(r.a.z); f[3] = __uint_as_float(r.a.w);
+        f[4] = __uint_as_float(r.b.x); f[5] = __uint_as_float(r.b.y);
+        f[6] = __uint_as_float(r.b.z); f[7] = __uint_as_float(r.b.w);
+    } else if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+        const uint32_t w[4] = {r.a.x, r.a.y, r.a.z, r.a.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            f[2 * j] = bf16_lo(w[j]);
+            f[2 * j + 1] = bf16_hi(w[j]);
+        }
+    } else {
+        const uint32_t w[4] = {r.a.x, r.a.y, r.a.z, r.a.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const float2 v = __half22float2(*reinterpret_cast<const __half2*>(&w[j]));
+            f[2 * j] = v.x;
+            f[2 * j + 1] = v.y;
+        }
+    }
+}
+
+template <typename QT, typename KT>
+__global__ void __launch_bounds__(kAttnThreads, 1) attn_partial128_kernel(
+    const QT* __restrict__ queries, const KT* __restrict__ prefix_k, const KT* __restrict__ prefix_v,
+    const KT* __restrict__ cur_k, const KT* __restrict__ cur_v, const int64_t* __restrict__ indices,
+    const uint8_t* __restrict__ valid, const int64_t* __restrict__ head_to_kv,
+    float* __restrict__ partials, int q_heads, int kv_heads, int64_t prefix_tokens,
+    int64_t kbs, int64_t khs, int64_t kts, int64_t vbs, int64_t vhs, int64_t vts,
+    int64_t selected, int64_t split_tokens, int splits, float scale) {
+    __shared__ int s_row[kChunk];
+    __shared__ float s_red[kAttnThreads / 32];
+    __shared__ float s_acc[kAttnThreads / 32][kSegThreads][8];
+    __shared__ float s_sum[kAttnThreads / 32];
+
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int c = tid & (kSegThreads - 1), g = tid / kSegThreads;
+    const int64_t row = blockIdx.y;
+    const int64_t b = row / q_heads;
+    const int qh = static_cast<int>(row % q_heads);
+    const int64_t kvh = head_to_kv[qh];
+    const int split = blockIdx.x;
+    const int64_t slot0 = static_cast<int64_t>(split) * split_tokens;
+    const int64_t slot_end = min(slot0 + split_tokens, selected);
+
+    float q8[8];
+    {
+        const QT* qp = queries + row * 128 + 8 * c;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) q8[j] = load_float(qp + j);
+    }
+    const KT* kbase = prefix_k + b * kbs + kvh * khs + 8 * c;
+    const KT* vbase = prefix_v + b * vbs + kvh * vhs + 8 * c;
+    const KT* ckp = cur_k + (b * kv_heads + kvh) * 128 + 8 * c;
+    const KT* cvp = cur_v + (b * kv_heads + kvh) * 128 + 8 * c;
+    const int64_t* idx_row = indices + row * selected;
+    const uint8_t* valid_row = valid ? valid + row * selected : nullptr;
+
+    float run_max = -INFINITY, run_sum = 0.0f;
+    float acc[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[j] = 0.0f;
+
+    for (int64_t chunk0 = slot0; chunk0 < slot_end; chunk0 += kChunk) {
+        {
+            const int64_t slot = chunk0 + tid;
+            int r = kSlotMasked;
+            if (slot < slot_end && (!valid_row || valid_row[slot])) {
+                const int64_t idx = idx_row[slot];
+                r = idx == prefix_tokens ? kSlotCurrent
+                                         : static_cast<int>(idx < 0 ? 0 : (idx > prefix_tokens - 1 ? prefix_tokens - 1 : idx));
+            }
+            s_row[tid] = r;
+        }
+        __syncthreads();
+
+        // 16-bit K/V: issue the K and V loads of all 16 rows before any math
+        // (16 x 2 x 16 B in flight per thread).  fp32 K/V would need twice the
+        // registers, so its V loads follow the logits.
+        constexpr bool kEarlyV = sizeof(KT) == 2;
+        Raw8 kraw[kRowsPerThread], vraw[kRowsPerThread];
+        int rid[kRowsPerThread];
+#pragma unroll
+        for (int i = 0; i < kRowsPerThread; ++i) {
+            rid[i] = s_row[g + kRowGroups * i];
+            if (rid[i] >= 0) {
+                kraw[i] = load_raw8(kbase + static_cast<int64_t>(rid[i]) * kts);
+                if constexpr (kEarlyV) vraw[i] = load_raw8(vbase + static_cast<int64_t>(rid[i]) * vts);
+            } else if (rid[i] == kSlotCurrent) {
+                kraw[i] = load_raw8(ckp);
+                if constexpr (kEarlyV) vraw[i] = load_raw8(cvp);
+            } else {
+                kraw[i].a = kraw[i].b = make_uint4(0, 0, 0, 0);
+                if constexpr (kEarlyV) vraw[i].a = vraw[i].b = make_uint4(0, 0, 0, 0);
+            }
+        }
+
+        float logit[kRowsPerThread];
+        float chunk_max = -INFINITY;
+#pragma unroll
+        for (int i = 0; i < kRowsPerThread; ++i) {
+            float kf[8];
+            unpack8<KT>(kraw[i], kf);
+            float dot = 0.0f;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) dot = __fmaf_rn(kf[j], q8[j], dot);
+#pragma unroll
+            for (int o = kSegThreads / 2; o > 0; o >>= 1) dot += __shfl_xor_sync(0xFFFFFFFFu, dot, o);
+            logit[i] = rid[i] == kSlotMasked ? -INFINITY : dot * scale;
+            chunk_max = fmaxf(chunk_max, logit[i]);
+        }
+        if constexpr (!kEarlyV) {
+#pragma unroll
+            for (int i = 0; i < kRowsPerThread; ++i) {
+                if (rid[i] >= 0) vraw[i] = load_raw8(vbase + static_cast<int64_t>(rid[i]) * vts);
+                else if (rid[i] == kSlotCurrent) vraw[i] = load_raw8(cvp);
+                else vraw[i].a = vraw[i].b = make_uint4(0, 0, 0, 0);
+            }
+        }
+        chunk_max = fmaxf(chunk_max, __shfl_xor_sync(0xFFFFFFFFu, chunk_max, 16));
+        if (lane == 0) s_red[warp] = chunk_max;
+        __syncthreads();
+        chunk_max = s_red[0];
+#pragma unroll
+        for (int w = 1; w < kAttnThreads / 32; ++w) chunk_max = fmaxf(chunk_max, s_red[w]);
+
+        const float new_max = fmaxf(run_max, chunk_max);
+        if (new_max != -INFINITY) {
+            const float alpha = run_max == -INFINITY ? 0.0f : expf(run_max - new_max);
+            run_sum *= alpha;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) acc[j] *= alpha;
+#pragma unroll
+            for (int i = 0; i < kRowsPerThread; ++i) {
+                const float p = rid[i] == kSlotMasked ? 0.0f : expf(logit[i] - new_max);
+                run_sum += p;
+                float vf[8];
+                unpack8<KT>(vraw[i], vf);
+#pragma unroll
+                for (int j = 0; j < 8; ++j) acc[j] = __fmaf_rn(p, vf[j], acc[j]);
+            }
+            run_max = new_max;
+        }
+        __syncthreads();  // s_row / s_red reuse
+    }
+
+    // Combine the 16 row groups: lanes g and g^1 share a warp, then 8 warps via smem.
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[j] += __shfl_xor_sync(0xFFFFFFFFu, acc[j], 16);
+    float sum = run_sum + __shfl_xor_sync(0xFFFFFFFFu, run_sum, 16);
+    if (lane < kSegThreads) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) s_acc[warp][lane][j] = acc[j];
+    }
+    if (lane == 0) s_sum[warp] = sum;
+    __syncthreads();
+    float* out = partials + (row * splits + split) * (128 + 2);
+    if (tid < 128) {
+        const int seg = tid / 8, j = tid % 8;
+        float a = 0.0f;
+#pragma unroll
+        for (int w = 0; w < kAttnThreads / 32; ++w) a += s_acc[w][seg][j];
+        out[2 + tid] = a;
+    }
+    if (tid == 0) {
+        float s = 0.0f;
+#pragma unroll
+        for (int w = 0; w < kAttnThreads / 32; ++w) s += s_sum[w];
+        out[0] = run_max;
+        out[1] = s;
+    }
+}
+
+// Generic head dims: one warp per (row, split), serial over slots.
+template <typename QT, typename KT>
+__global__ void attn_partial_generic_kernel(
+    const QT* __restrict__ queries, const KT* __restrict__ prefix_k, const KT* __restrict__ prefix_v,
+    const KT* __restrict__ cur_k, const KT* __restrict__ cur_v, const int64_t* __restrict__ indices,
+    const uint8_t* __restrict__ valid, const int64_t* __restrict__ head_to_kv,
+    float* __restrict__ partials, int q_heads, int kv_heads, int head_dim, int64_t prefix_tokens,
+    int64_t kbs, int64_t khs, int64_t kts, int64_t vbs, int64_t vhs, int64_t vts,
+    int64_t selected, int64_t split_tokens, int splits, float scale) {
+    constexpr int kMaxPerLane = 8;  // head_dim <= 256
+    const int lane = threadIdx.x & 31;
+    const int64_t row = blockIdx.y;
+    const int64_t b = row / q_heads;
+    const int qh = static_cast<int>(row % q_heads);
+    const int64_t kvh = head_to_kv[qh];
+    const int split = blockIdx.x;
+    const int64_t slot0 = static_cast<int64_t>(split) * split_tokens;
+    const int64_t slot_end = min(slot0 + split_tokens, selected);
+    float q[kMaxPerLane], acc[kMaxPerLane];
+#pragma unroll
+    for (int j = 0; j < kMaxPerLane; ++j) {
+        const int d = lane + 32 * j;
+        q[j] = d < head_dim ? load_float(queries + row * head_dim + d) : 0.0f;
+        acc[j] = 0.0f;
+    }
+    float run_max = -INFINITY, run_sum = 0.0f;
+    for (int64_t slot = slot0; slot < slot_end; ++slot) {
+        if (valid && !valid[row * selected + slot]) continue;
+        const int64_t idx = indices[row * selected + slot];
+        const KT *kp, *vp;
+        if (idx == prefix_tokens) {
+            kp = cur_k + (b * kv_heads + kvh) * head_dim;
+            vp = cur_v + (b * kv_heads + kvh) * head_dim;
+        } else {
+            const int64_t r = (idx < 0 ? int64_t(0) : (idx > prefix_tokens - 1 ? prefix_tokens - 1 : idx));
+            kp = prefix_k + b * kbs + kvh * khs + r * kts;
+            vp = prefix_v + b * vbs + kvh * vhs + r * vts;
+        }
+        float dot = 0.0f;
+#pragma unroll
+        for (int j = 0; j < kMaxPerLane; ++j) {
+            const int d = lane + 32 * j;
+            if (d < head_dim) dot = __fmaf_rn(load_float(kp + d), q[j], dot);
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) dot += __shfl_xor_sync(0xFFFFFFFFu, dot, o);
+        const float logit = dot * scale;
+        const float new_max = fmaxf(run_max, logit);
+        const float alpha = run_max == -INFINITY ? 0.0f : expf(run_max - new_max);
+        const float p = expf(logit - new_max);
+        run_sum = run_sum * alpha + p;
+#pragma unroll
+        for (int j = 0; j < kMaxPerLane; ++j) {
+            const int d = lane + 32 * j;
+            const float v = d < head_dim ? load_float(vp + d) : 0.0f;
+            acc[j] = __fmaf_rn(p, v, acc[j] * alpha);
+        }
+        run_max = new_max;
+    }
+    float* out = partials + (row * splits + split) * (head_dim + 2);
+#pragma unroll
+    for (int j = 0; j < kMaxPerLane; ++j) {
+        const int d = lane + 32 * j;
+        if (d < head_dim) out[2 + d] = acc[j];
+    }
+    if (lane == 0) {
+        out[0] = run_max;
+        out[1] = run_sum;
+    }
+}
+
+// Merge: one CTA per row; thread d owns output dim d.
+template <typename OT>
+__global__ void attn_merge_kernel(const float* __restrict__ partials, int64_t splits, int head_dim,
+                                  OT* __restrict__ out) {
+    const int64_t row = blockIdx.x;
+    const float* p = partials + row * splits * (head_dim + 2);
+    float gm = -INFINITY;
+    for (int64_t s = 0; s < splits; ++s) gm = fmaxf(gm, p[s * (head_dim + 2)]);
+    float den = 0.0f;
+    for (int64_t s = 0; s < splits; ++s)
+        den = __fmaf_rn(p[s * (head_dim + 2) + 1], expf(p[s * (head_dim + 2)] - gm), den);
+    for (int d = threadIdx.x; d < head_dim; d += blockDim.x) {
+        float num = 0.0f;
+        for (int64_t s = 0; s < splits; ++s)
+            num = __fmaf_rn(p[s * (head_dim + 2) + 2 + d], expf(p[s * (head_dim + 2)] - gm), num);
+        const float v = num / den;
+        if constexpr (std::is_same<OT, float>::value) out[row * head_dim + d] = v;
+        else if constexpr (std::is_same<OT, __half>::value) out[row * head_dim + d] = __float2half_rn(v);
+        else out[row * head_dim + d] = __float2bfloat16_rn(v);
+    }
+}
+
+template <typename QT, typename KT>
+int launch_partial(const void* queries, int64_t batch, int64_t q_heads, int64_t head_dim,
+                   const void* pk, const void* pv, int64_t kv_heads, int64_t prefix_tokens,
+                   int64_t kbs, int64_t khs, int64_t kts, int64_t vbs, int64_t vhs, int64_t vts,
+                   const void* ck, const void* cv, const int64_t* indices, int64_t selected,
+                   const uint8_t* valid, const int64_t* head_to_kv, int64_t split_tokens,
+                   float* partials, cudaStream_t stream) {
+    const int64_t splits = (selected + split_tokens - 1) / split_tokens;
+    dim3 grid(static_cast<unsigned>(splits), static_cast<unsigned>(batch * q_heads));
+    const float scale = score_scale_for(head_dim);
+    const size_t es = sizeof(KT);
+    const bool vec_ok = head_dim == 128 && aligned(pk, 16) && aligned(pv, 16) && aligned(ck, 16) &&
+                        aligned(cv, 16) && (kbs * es) % 16 == 0 && (khs * es) % 16 == 0 &&
+                        (kts * es) % 16 == 0 && (vbs * es) % 16 == 0 && (vhs * es) % 16 == 0 &&
+                        (vts * es) % 16 == 0;
+    if (vec_ok) {
+        attn_partial128_kernel<QT, KT><<<grid, kAttnThreads, 0, stream>>>(
+            static_cast<const QT*>(queries), static_cast<const KT*>(pk), static_cast<const KT*>(pv),
+            static_cast<const KT*>(ck), static_cast<const KT*>(cv), indices, valid, head_to_kv,
+            partials, static_cast<int>(q_heads), static_cast<int>(kv_heads), prefix_tokens, kbs,
+            khs, kts, vbs, vhs, vts, selected, split_tokens, static_cast<int>(splits), scale);
+    } else {
+        attn_partial_generic_kernel<QT, KT><<<grid, 32, 0, stream>>>(
+            static_cast<const QT*>(queries), static_cast<const KT*>(pk), static_cast<const KT*>(pv),
+            static_cast<const KT*>(ck), static_cast<const KT*>(cv), indices, valid, head_to_kv,
+            partials, static_cast<int>(q_heads), static_cast<int>(kv_heads),
+            static_cast<int>(head_dim), prefix_tokens, kbs, khs, kts, vbs, vhs, vts, selected,
+            split_tokens, static_cast<int>(splits), scale);
+    }
+    return check_launch("popkv_attn_partial");
+}
+
+template <typename QT>
+int dispatch_kv(int kv_dtype, const void* queries, int64_t batch, int64_t q_heads, int64_t head_dim,
+                const void* pk, const void* pv, int64_t kv_heads, int64_t prefix_tokens, int64_t kbs,
+                int64_t khs, int64_t kts, int64_t vbs, int64_t vhs, int64_t vts, const void* ck,
+                const void* cv, const int64_t* indices, int64_t selected, const uint8_t* valid,
+                const int64_t* head_to_kv, int64_t split_tokens, float* partials,
+                cudaStream_t stream) {
+    if (kv_dtype == POPKV_DTYPE_F32)
+        return launch_partial<QT, float>(queries, batch, q_heads, head_dim, pk, pv, kv_heads,
+                                         prefix_tokens, kbs, khs, kts, vbs, vhs, vts, ck, cv,
+                                         indices, selected, valid, head_to_kv, split_tokens,
+                                         partials, stream);
+    if (kv_dtype == POPKV_DTYPE_F16)
+        return launch_partial<QT, __half>(queries, batch, q_heads, head_dim, pk, pv, kv_heads,
+                                          prefix_tokens, kbs, khs, kts, vbs, vhs, vts, ck, cv,
+                                          indices, selected, valid, head_to_kv, split_tokens,
+                                          partials, stream);
+    return launch_partial<QT, __nv_bfloat16>(queries, batch, q_heads, head_dim, pk, pv, kv_heads,
+                                             prefix_tokens, kbs, khs, kts, vbs, vhs, vts, ck, cv,
+                                             indices, selected, valid, head_to_kv, split_tokens,
+                                             partials, stream);
+}
+
+}  // namespace
+}  // namespace popkv
+
+extern "C" int popkv_attn_partial(const void* queries, int queries_dtype, int64_t batch,
+                                  int64_t q_heads, int64_t head_dim, const void* prefix_keys,
+                                  const void* prefix_values, int kv_dtype, int64_t kv_heads,
+                                  int64_t prefix_tokens, int64_t k_batch_stride,
+                                  int64_t k_head_stride, int64_t k_token_stride,
+                                  int64_t v_batch_stride, int64_t v_head_stride,
+                                  int64_t v_token_stride, const void* current_keys,
+                                  const void* current_values, const int64_t* indices,
+                                  int64_t selected, const uint8_t* valid,
+                                  const int64_t* head_to_kv, int64_t split_tokens, float* partials,
+                                  void* stream) {
+    using namespace popkv;
+    if (!valid_dtype(queries_dtype) || !valid_dtype(kv_dtype))
+        return fail(POPKV_ERR_INVALID, "popkv_attn_partial: tensors must be fp32/fp16/bf16");
+    if (batch < 0 || q_heads <= 0 || kv_heads <= 0 || head_dim <= 0)
+        return fail(POPKV_ERR_INVALID, "invalid indexed-attention tensor ranks or K/V shapes");
+    if (prefix_tokens <= 0 || selected <= 0)
+        return fail(POPKV_ERR_INVALID, "indexed attention requires non-empty prefix and selection");
+    if (split_tokens <= 0 || split_tokens % 16)
+        return fail(POPKV_ERR_INVALID, "split_tokens must be a positive multiple of 16");
+    if (head_dim > 256)
+        return fail(POPKV_ERR_UNSUPPORTED, "popkv_attn_partial: head_dim %lld exceeds 256",
+                    static_cast<long long>(head_dim));
+    const int64_t splits = (selected + split_tokens - 1) / split_tokens;
+    if (splits > 0x7FFFFFFFll || batch * q_heads > 65535 || prefix_tokens >= 0x7FFFFFFFll)
+        return fail(POPKV_ERR_UNSUPPORTED, "popkv_attn_partial: grid too large");
+    if (batch == 0) return POPKV_OK;
+    if (!queries || !prefix_keys || !prefix_values || !current_keys || !current_values ||
+        !indices || !head_to_kv || !partials)
+        return fail(POPKV_ERR_INVALID, "popkv_attn_partial: null pointer");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (queries_dtype == POPKV_DTYPE_F32)
+        return dispatch_kv<float>(kv_dtype, queries, batch, q_heads, head_dim, prefix_keys,
+                                  prefix_values, kv_heads, prefix_tokens, k_batch_stride,
+                                  k_head_stride, k_token_stride, v_batch_stride, v_head_stride,
+                                  v_token_stride, current_keys, current_values, indices, selected,
+                                  valid, head_to_kv, split_tokens, partials, s);
+    if (queries_dtype == POPKV_DTYPE_F16)
+        return dispatch_kv<__half>(kv_dtype, queries, batch, q_heads, head_dim, prefix_keys,
+                                   prefix_values, kv_heads, prefix_tokens, k_batch_stride,
+                                   k_head_stride, k_token_stride, v_batch_stride, v_head_stride,
+                                   v_token_stride, current_keys, current_values, indices, selected,
+                                   valid, head_to_kv, split_tokens, partials, s);
+    return dispatch_kv<__nv_bfloat16>(kv_dtype, queries, batch, q_heads, head_dim, prefix_keys,
+                                      prefix_values, kv_heads, prefix_tokens, k_batch_stride,
+                                      k_head_stride, k_token_stride, v_batch_stride, v_head_stride,
+                                      v_token_stride, current_keys, current_values, indices,
+                                      selected, valid, head_to_kv, split_tokens, partials, s);
+}
+
+extern "C" int popkv_attn_merge(const float* partials, int64_t rows, int64_t splits,
+                                int64_t head_dim, void* out, int out_dtype, void* stream) {
+    using namespace popkv;
+    if (!valid_dtype(out_dtype))
+        return fail(POPKV_ERR_INVALID, "popkv_attn_merge: output must be fp32/fp16/bf16");
+    if (rows < 0 || splits <= 0 || head_dim <= 0)
+        return fail(POPKV_ERR_INVALID, "partial/output shape mismatch");
+    if (rows == 0) return POPKV_OK;
+    if (!partials || !out) return fail(POPKV_ERR_INVALID, "popkv_attn_merge: null pointer");
+    if (rows > 0x7FFFFFFFll) return fail(POPKV_ERR_UNSUPPORTED, "popkv_attn_merge: too many rows");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const unsigned threads = head_dim >= 128 ? 128 : 32 * static_cast<unsigned>((head_dim + 31) / 32);
+    const int d = static_cast<int>(head_dim);
+    if (out_dtype == POPKV_DTYPE_F32)
+        attn_merge_kernel<float><<<static_cast<unsigned>(rows), threads, 0, s>>>(partials, splits, d,
+                                                                                 static_cast<float*>(out));
+    else if (out_dtype == POPKV_DTYPE_F16)
+        attn_merge_kernel<__half><<<static_cast<unsigned>(rows), threads, 0, s>>>(partials, splits, d,
+                                                                                  static_cast<__half*>(out));
+    else
+        attn_merge_kernel<__nv_bfloat16><<<static_cast<unsigned>(rows), threads, 0, s>>>(
+            partials, splits, d, static_cast<__nv_bfloat16*>(out));
+    return check_launch("popkv_attn_merge");
+}

@@ -1,0 +1,263 @@
+// Key bit-plane prepack and per-token append (PopKV subsystem 1).
+//
+// Reference: csrc/popkv_ext.cu:381-500 (fused G16/G64 encoders),
+// :79-143 (G32 encoder), :284-374 (generic head dim), launched from
+// :1014-1206 and reached through popkv_cuda.pack_keys / pack_keys_into
+// (popkv_cuda.py:53-87).
+//
+// One CTA encodes one token group of one KV head:
+//   phase 1: per-dimension min/max over the group's tokens (coalesced loads,
+//            split across row slices, combined in shared memory), stored as the
+//            magnitude thresholds 0.5*max and 0.5*min;
+//   phase 2: one warp per token row, lane l owning dim 32*w + l of word w:
+//            two ballots give the sign and magnitude words, and the bucket sums
+//            of each representative group are reduced by a butterfly whose lane-0
+//            result equals the reference's shuffle-down tree
+//            (s[i] += s[i + o], o = 16, 8, 4, 2, 1; width 16 for G16).
+// Counts come from popcounts of the ballots, so only the two sums need shuffles.
+#include <cstdint>
+
+#include "common.cuh"
+
+namespace popkv {
+namespace {
+
+constexpr int kPackThreads = 256;
+constexpr int kMaxWords = 8;  // head_dim <= 256
+
+__device__ __forceinline__ float butterfly16(float x) {
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1) x = __fadd_rn(x, __shfl_xor_sync(0xFFFFFFFFu, x, o));
+    return x;
+}
+
+__device__ __forceinline__ float butterfly32(float x) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) x = __fadd_rn(x, __shfl_xor_sync(0xFFFFFFFFu, x, o));
+    return x;
+}
+
+template <typename T, int G, int W>
+__global__ void __launch_bounds__(kPackThreads) pack_kernel(
+    const T* __restrict__ keys, int64_t head_stride, int64_t token_stride, int64_t tokens,
+    int head_dim, int64_t token_group, int32_t* __restrict__ k_sign, int32_t* __restrict__ k_mag,
+    uint16_t* __restrict__ k_low, uint16_t* __restrict__ k_delta, int64_t capacity,
+    int64_t token_offset) {
+    extern __shared__ float smem[];
+    float* thr_hi = smem;                      // [head_dim]  0.5 * max
+    float* thr_lo = smem + head_dim;           // [head_dim]  0.5 * min
+    float* part = smem + 2 * head_dim;         // [slices][2][head_dim] partial extrema
+
+    const int64_t kvh = blockIdx.y;
+    const int64_t t0 = static_cast<int64_t>(blockIdx.x) * token_group;
+    const int64_t t1 = min(t0 + token_group, tokens);
+    const T* head = keys + kvh * head_stride;
+    const int tid = threadIdx.x;
+
+    // Phase 1: extrema.  `slices` row slices of head_dim threads each
+    // (head_dim <= 256 == kPackThreads, so every dim has a thread).
+    const int slices = max(1, kPackThreads / head_dim);
+    if (tid < slices * head_dim) {
+        const int d = tid % head_dim, s = tid / head_dim;
+        float mn = INFINITY, mx = -INFINITY;
+#pragma unroll 4
+        for (int64_t t = t0 + s; t < t1; t += slices) {
+            float v = load_float(head + t * token_stride + d);
+            mn = fminf(mn, v);
+            mx = fmaxf(mx, v);
+        }
+        part[(s * 2 + 0) * head_dim + d] = mn;
+        part[(s * 2 + 1) * head_dim + d] = mx;
+    }
+    __syncthreads();
+    for (int d = tid; d < head_dim; d += kPackThreads) {
+        float mn = part[d], mx = part[head_dim + d];
+        for (int s = 1; s < slices; ++s) {
+            mn = fminf(mn, part[(s * 2 + 0) * head_dim + d]);
+            mx = fmaxf(mx, part[(s * 2 + 1) * head_dim + d]);
+        }
+        thr_lo[d] = __fmul_rn(mn, 0.5f);
+        thr_hi[d] = __fmul_rn(mx, 0.5f);
+    }
+    __syncthreads();
+
+    // Phase 2: one warp per token row.
+    const int lane = tid & 31, warp = tid >> 5;
+    constexpr int kWarps = kPackThreads / 32;
+    const int reps = (head_dim + G - 1) / G;
+    for (int64_t t = t0 + warp; t < t1; t += kWarps) {
+        const T* row = head + t * token_stride;
+        const int64_t out_row = kvh * capacity + token_offset + t;
+        float a_low[W], a_high[W];
+        uint32_t sw[W], mw[W], vw[W];
+#pragma unroll
+        for (int w = 0; w < W; ++w) {
+            const int d = w * 32 + lane;
+            const bool valid = d < head_dim;
+            const float v = valid ? load_float(row + d) : 0.0f;
+            const bool sign = valid && v >= 0.0f;
+            const bool mag = valid && (sign ? (v > thr_hi[d]) : (v < thr_lo[d]));
+            sw[w] = __ballot_sync(0xFFFFFFFFu, sign);
+            mw[w] = __ballot_sync(0xFFFFFFFFu, mag);
+            vw[w] = __ballot_sync(0xFFFFFFFFu, valid);
+            const float a = fabsf(v);
+            a_low[w] = (valid && !mag) ? a : 0.0f;
+            a_high[w] = mag ? a : 0.0f;
+        }
+        if (lane == 0) {
+            if constexpr (W == 4) {
+                reinterpret_cast<uint4*>(k_sign)[out_row] = make_uint4(sw[0], sw[1], sw[2], sw[3]);
+                reinterpret_cast<uint4*>(k_mag)[out_row] = make_uint4(mw[0], mw[1], mw[2], mw[3]);
+            } else {
+#pragma unroll
+                for (int w = 0; w < W; ++w) {
+                    k_sign[out_row * W + w] = static_cast<int32_t>(sw[w]);
+                    k_mag[out_row * W + w] = static_cast<int32_t>(mw[w]);
+                }
+            }
+        }
+        if constexpr (G == 16) {
+#pragma unroll
+            for (int w = 0; w < W; ++w) {
+                const float lo = butterfly16(a_low[w]);
+                const float hi = butterfly16(a_high[w]);
+                const int half = lane >> 4;
+                const int rep = 2 * w + half;
+                if ((lane & 15) == 0 && rep < reps) {
+                    const uint32_t m = half ? 0xFFFF0000u : 0x0000FFFFu;
+                    const int low_count = __popc(vw[w] & ~mw[w] & m);
+                    const int high_count = __popc(mw[w] & m);
+                    float low, delta;
+                    bucket_means(lo, low_count, hi, high_count, low, delta);
+                    k_low[out_row * reps + rep] = float_to_half_bits(low);
+                    k_delta[out_row * reps + rep] = float_to_half_bits(delta);
+                }
+            }
+        } else if constexpr (G == 32) {
+#pragma unroll
+            for (int w = 0; w < W; ++w) {
+                const float lo = butterfly32(a_low[w]);
+                const float hi = butterfly32(a_high[w]);
+                if (lane == 0 && w < reps) {
+                    const int low_count = __popc(vw[w] & ~mw[w]);
+                    const int high_count = __popc(mw[w]);
+                    float low, delta;
+                    bucket_means(lo, low_count, hi, high_count, low, delta);
+                    k_low[out_row * reps + w] = float_to_half_bits(low);
+                    k_delta[out_row * reps + w] = float_to_half_bits(delta);
+                }
+            }
+        } else {
+#pragma unroll
+            for (int r = 0; r < (W + 1) / 2; ++r) {
+                const bool has_second = 2 * r + 1 < W;
+                const float x_lo = has_second ? __fadd_rn(a_low[2 * r], a_low[2 * r + 1]) : a_low[2 * r];
+                const float x_hi = has_second ? __fadd_rn(a_high[2 * r], a_high[2 * r + 1]) : a_high[2 * r];
+                const float lo = butterfly32(x_lo);
+                const float hi = butterfly32(x_hi);
+                if (lane == 0 && r < reps) {
+                    const uint32_t m1 = has_second ? mw[2 * r + 1] : 0u;
+                    const uint32_t v1 = has_second ? vw[2 * r + 1] : 0u;
+                    const int low_count = __popc(vw[2 * r] & ~mw[2 * r]) + __popc(v1 & ~m1);
+                    const int high_count = __popc(mw[2 * r]) + __popc(m1);
+                    float low, delta;
+                    bucket_means(lo, low_count, hi, high_count, low, delta);
+                    k_low[out_row * reps + r] = float_to_half_bits(low);
+                    k_delta[out_row * reps + r] = float_to_half_bits(delta);
+                }
+            }
+        }
+    }
+}
+
+template <typename T, int G>
+int launch_pack_g(const void* keys, int64_t kv_heads, int64_t tokens, int64_t head_dim,
+                  int64_t hs, int64_t ts, int32_t* k_sign, int32_t* k_mag, uint16_t* k_low,
+                  uint16_t* k_delta, int64_t capacity, int64_t token_offset, int64_t tg,
+                  cudaStream_t stream) {
+    const int64_t groups = (tokens + tg - 1) / tg;
+    const int words = static_cast<int>((head_dim + 31) / 32);
+    const int slices = head_dim >= kPackThreads ? 1 : kPackThreads / static_cast<int>(head_dim);
+    const size_t smem = sizeof(float) * static_cast<size_t>(head_dim) * (2 + 2 * slices);
+    dim3 grid(static_cast<unsigned>(groups), static_cast<unsigned>(kv_heads));
+    const T* k = static_cast<const T*>(keys);
+#define POPKV_PACK_CASE(NW)                                                                   \
+    case NW:                                                                                  \
+        pack_kernel<T, G, NW><<<grid, kPackThreads, smem, stream>>>(                          \
+            k, hs, ts, tokens, static_cast<int>(head_dim), tg, k_sign, k_mag, k_low, k_delta, \
+            capacity, token_offset);                                                          \
+        break;
+    switch (words) {
+        POPKV_PACK_CASE(1)
+        POPKV_PACK_CASE(2)
+        POPKV_PACK_CASE(3)
+        POPKV_PACK_CASE(4)
+        POPKV_PACK_CASE(5)
+        POPKV_PACK_CASE(6)
+        POPKV_PACK_CASE(7)
+        POPKV_PACK_CASE(8)
+        default:
+            return fail(POPKV_ERR_UNSUPPORTED, "popkv_pack: head_dim %lld exceeds 256",
+                        static_cast<long long>(head_dim));
+    }
+#undef POPKV_PACK_CASE
+    return check_launch("popkv_pack");
+}
+
+template <typename T>
+int launch_pack(const void* keys, int64_t kv_heads, int64_t tokens, int64_t head_dim, int64_t hs,
+                int64_t ts, int32_t* k_sign, int32_t* k_mag, uint16_t* k_low, uint16_t* k_delta,
+                int64_t capacity, int64_t token_offset, int64_t tg, int64_t g,
+                cudaStream_t stream) {
+    if (g == 16)
+        return launch_pack_g<T, 16>(keys, kv_heads, tokens, head_dim, hs, ts, k_sign, k_mag,
+                                    k_low, k_delta, capacity, token_offset, tg, stream);
+    if (g == 32)
+        return launch_pack_g<T, 32>(keys, kv_heads, tokens, head_dim, hs, ts, k_sign, k_mag,
+                                    k_low, k_delta, capacity, token_offset, tg, stream);
+    return launch_pack_g<T, 64>(keys, kv_heads, tokens, head_dim, hs, ts, k_sign, k_mag, k_low,
+                                k_delta, capacity, token_offset, tg, stream);
+}
+
+}  // namespace
+}  // namespace popkv
+
+extern "C" int popkv_pack(const void* keys, int keys_dtype, int64_t kv_heads, int64_t tokens,
+                          int64_t head_dim, int64_t key_head_stride, int64_t key_token_stride,
+                          int32_t* k_sign, int32_t* k_mag, uint16_t* k_low, uint16_t* k_delta,
+                          int64_t capacity, int64_t token_offset, int64_t token_group_size,
+                          int64_t dim_group_size, void* stream) {
+    using namespace popkv;
+    if (!valid_dtype(keys_dtype)) return fail(POPKV_ERR_INVALID, "popkv_pack: keys must be fp32/fp16/bf16");
+    if (kv_heads < 0 || tokens < 0 || head_dim <= 0)
+        return fail(POPKV_ERR_INVALID, "keys must be [KVH, T, D] with a non-empty head dim");
+    if (token_group_size < 1 || token_group_size > 4096)
+        return fail(POPKV_ERR_INVALID, "token_group_size must be between 1 and 4096");
+    if (dim_group_size != 16 && dim_group_size != 32 && dim_group_size != 64)
+        return fail(POPKV_ERR_INVALID, "dim_group_size must be 16, 32, or 64");
+    if (token_offset < 0 || token_offset + tokens > capacity)
+        return fail(POPKV_ERR_CAPACITY, "Pop-KV cache capacity exceeded");
+    if (kv_heads == 0 || tokens == 0) return POPKV_OK;
+    if (!keys || !k_sign || !k_mag || !k_low || !k_delta)
+        return fail(POPKV_ERR_INVALID, "popkv_pack: null pointer");
+    if ((head_dim + 31) / 32 == 4 && (!aligned(k_sign, 16) || !aligned(k_mag, 16)))
+        return fail(POPKV_ERR_INVALID, "popkv_pack: bit-planes must be 16-byte aligned");
+    if ((tokens + token_group_size - 1) / token_group_size > 0x7FFFFFFF || kv_heads > 65535)
+        return fail(POPKV_ERR_UNSUPPORTED, "popkv_pack: grid too large");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    switch (keys_dtype) {
+        case POPKV_DTYPE_F32:
+            return launch_pack<float>(keys, kv_heads, tokens, head_dim, key_head_stride,
+                                      key_token_stride, k_sign, k_mag, k_low, k_delta, capacity,
+                                      token_offset, token_group_size, dim_group_size, s);
+        case POPKV_DTYPE_F16:
+            return launch_pack<__half>(keys, kv_heads, tokens, head_dim, key_head_stride,
+                                       key_token_stride, k_sign, k_mag, k_low, k_delta, capacity,
+                                       token_offset, token_group_size, dim_group_size, s);
+        default:
+            return launch_pack<__nv_bfloat16>(keys, kv_heads, tokens, head_dim, key_head_stride,
+                                              key_token_stride, k_sign, k_mag, k_low, k_delta,
+                                              capacity, token_offset, token_group_size,
+                                              dim_group_size, s);
+    }
+}

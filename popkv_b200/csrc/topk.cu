@@ -1,0 +1,217 @@
+// Per-query-head top-k with the current-token slot reserved (PopKV subsystem 3).
+//
+// Replaces torch.topk(scores, k, dim=-1, sorted=False).indices followed by
+// _append_current (reference popkv.py:1094-1098, :287-291).  torch.topk leaves
+// the order among equal scores unspecified; this kernel fixes it: higher score
+// first, then lower token index, and the k winners are written in ascending
+// token order (the order the attention gather reads the cache in).
+//
+// Radix select on an order-preserving integer key of each score, one CTA per
+// row.  The row's keys are staged in shared memory when they fit.  Each pass
+// builds a shared-memory histogram of the next digit of the keys that still
+// match the threshold prefix (fp16: 11 + 5 bits; fp32: 11 + 11 + 10 bits) and
+// a block-wide scan picks the digit holding the k-th largest key.  The final
+// pass gives every thread a contiguous slice of the row: a block scan of its
+// (greater, equal) counts yields each winner's output position, taking equal
+// keys in index order until the quota is filled.
+#include <cstdint>
+#include <type_traits>
+
+#include "common.cuh"
+
+namespace popkv {
+namespace {
+
+constexpr int kTopkThreads = 1024;
+constexpr int kTopkWarps = kTopkThreads / 32;
+constexpr int kHistBins = 2048;
+constexpr size_t kStageBytes = 96 * 1024;
+
+__device__ __forceinline__ uint32_t key16(uint16_t h) {
+    if ((h & 0x7FFFu) == 0) h = 0;  // -0 == +0
+    if ((h & 0x7C00u) == 0x7C00u && (h & 0x3FFu)) return 0xFFFFu;  // NaN ranks highest
+    return (h & 0x8000u) ? (~static_cast<uint32_t>(h) & 0xFFFFu) : (static_cast<uint32_t>(h) | 0x8000u);
+}
+
+__device__ __forceinline__ uint32_t key32(uint32_t u) {
+    if ((u & 0x7FFFFFFFu) == 0) u = 0;
+    if ((u & 0x7F800000u) == 0x7F800000u && (u & 0x7FFFFFu)) return 0xFFFFFFFFu;
+    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+template <bool F32>
+__device__ __forceinline__ uint32_t load_key(const void* row, int64_t i) {
+    if constexpr (F32) return key32(static_cast<const uint32_t*>(row)[i]);
+    else return key16(static_cast<const uint16_t*>(row)[i]);
+}
+
+// Block-wide exclusive scan of one value per thread; `total` receives the sum.
+template <typename V>
+__device__ __forceinline__ V block_exclusive_scan(V x, V* warp_sums, V& total) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    V incl = x;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        V y = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+        if (lane >= o) incl += y;
+    }
+    if (lane == 31) warp_sums[warp] = incl;
+    __syncthreads();
+    if (warp == 0) {
+        V w = lane < kTopkWarps ? warp_sums[lane] : V(0);
+        V wi = w;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            V y = __shfl_up_sync(0xFFFFFFFFu, wi, o);
+            if (lane >= o) wi += y;
+        }
+        if (lane < kTopkWarps) warp_sums[lane] = wi - w;
+        if (lane == kTopkWarps - 1) warp_sums[kTopkWarps] = wi;
+    }
+    __syncthreads();
+    V result = warp_sums[warp] + incl - x;
+    total = warp_sums[kTopkWarps];
+    __syncthreads();
+    return result;
+}
+
+template <bool F32, bool STAGED>
+__global__ void __launch_bounds__(kTopkThreads) topk_kernel(
+    const void* __restrict__ scores, int64_t tokens, int64_t row_stride, int64_t k,
+    int64_t current_index, int64_t* __restrict__ out, int64_t out_stride) {
+    extern __shared__ __align__(16) unsigned char staged_raw[];
+    __shared__ uint32_t hist[kHistBins];
+    __shared__ unsigned long long scan_sums[kTopkWarps + 1];
+    __shared__ uint32_t sel_bin;
+    __shared__ unsigned long long sel_above;
+
+    using KeyT = typename std::conditional<F32, uint32_t, uint16_t>::type;
+    KeyT* staged = reinterpret_cast<KeyT*>(staged_raw);
+    const int64_t row = blockIdx.x;
+    const void* src = F32 ? static_cast<const void*>(static_cast<const float*>(scores) + row * row_stride)
+                          : static_cast<const void*>(static_cast<const uint16_t*>(scores) + row * row_stride);
+    int64_t* dst = out + row * out_stride;
+    const int tid = threadIdx.x;
+
+    if (current_index >= 0 && tid == 0) dst[k] = current_index;
+    if (k <= 0) return;
+
+    auto key_at = [&](int64_t i) -> uint32_t {
+        if constexpr (STAGED) return staged[i];
+        else return load_key<F32>(src, i);
+    };
+    if constexpr (STAGED) {
+        for (int64_t i = tid; i < tokens; i += kTopkThreads) staged[i] = static_cast<KeyT>(load_key<F32>(src, i));
+        __syncthreads();
+    }
+
+    // Radix passes: find the threshold key (the k-th largest).
+    constexpr int kPasses = F32 ? 3 : 2;
+    const int shifts[3] = {F32 ? 21 : 5, F32 ? 10 : 0, 0};
+    const int widths[3] = {11, F32 ? 11 : 5, 10};
+    uint32_t prefix = 0, prefix_mask = 0;
+    unsigned long long above = 0;  // keys strictly above the current prefix range
+#pragma unroll 1
+    for (int p = 0; p < kPasses; ++p) {
+        const int shift = shifts[p], width = widths[p];
+        const uint32_t nbins = 1u << width;
+        const uint32_t digit_mask = nbins - 1u;
+        for (uint32_t b = tid; b < nbins; b += kTopkThreads) hist[b] = 0;
+        __syncthreads();
+        for (int64_t i = tid; i < tokens; i += kTopkThreads) {
+            const uint32_t key = key_at(i);
+            if ((key & prefix_mask) == prefix) atomicAdd(&hist[(key >> shift) & digit_mask], 1u);
+        }
+        __syncthreads();
+        // Descending-digit scan: position j holds digit nbins - 1 - j.
+        const unsigned long long remaining = static_cast<unsigned long long>(k) - above;
+        const uint32_t per = (nbins + kTopkThreads - 1) / kTopkThreads;  // 1 or 2
+        unsigned long long local = 0;
+        for (uint32_t j = tid * per; j < min(nbins, (tid + 1) * per); ++j) local += hist[nbins - 1 - j];
+        unsigned long long total;
+        unsigned long long excl = block_exclusive_scan<unsigned long long>(local, scan_sums, total);
+        unsigned long long run = excl;
+        for (uint32_t j = tid * per; j < min(nbins, (tid + 1) * per); ++j) {
+            const uint32_t cnt = hist[nbins - 1 - j];
+            if (run < remaining && run + cnt >= remaining) {
+                sel_bin = nbins - 1 - j;
+                sel_above = run;
+            }
+            run += cnt;
+        }
+        __syncthreads();
+        prefix |= sel_bin << shift;
+        prefix_mask |= digit_mask << shift;
+        above += sel_above;
+        __syncthreads();
+    }
+    const uint32_t threshold = prefix;
+    const unsigned long long need = static_cast<unsigned long long>(k) - above;  // ties to take
+
+    // Compaction over contiguous slices, in token order.
+    const int64_t chunk = (tokens + kTopkThreads - 1) / kTopkThreads;
+    const int64_t lo = min(tokens, tid * chunk), hi = min(tokens, lo + chunk);
+    unsigned int gt = 0, eq = 0;
+    for (int64_t i = lo; i < hi; ++i) {
+        const uint32_t key = key_at(i);
+        gt += key > threshold;
+        eq += key == threshold;
+    }
+    unsigned long long packed = (static_cast<unsigned long long>(gt) << 32) | eq;
+    unsigned long long total;
+    unsigned long long excl = block_exclusive_scan<unsigned long long>(packed, scan_sums, total);
+    unsigned long long gt_before = excl >> 32, eq_before = excl & 0xFFFFFFFFull;
+    for (int64_t i = lo; i < hi; ++i) {
+        const uint32_t key = key_at(i);
+        if (key > threshold) {
+            dst[gt_before + min(eq_before, need)] = i;
+            ++gt_before;
+        } else if (key == threshold) {
+            if (eq_before < need) dst[gt_before + eq_before] = i;
+            ++eq_before;
+        }
+    }
+}
+
+template <bool F32>
+int launch_topk(const void* scores, int64_t rows, int64_t tokens, int64_t row_stride, int64_t k,
+                int64_t current_index, int64_t* out, int64_t out_stride, cudaStream_t stream) {
+    const size_t key_bytes = F32 ? 4 : 2;
+    const size_t stage = static_cast<size_t>(tokens) * key_bytes;
+    if (stage <= kStageBytes) {
+        auto kernel = topk_kernel<F32, true>;
+        cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(kStageBytes));
+        kernel<<<static_cast<unsigned>(rows), kTopkThreads, stage, stream>>>(
+            scores, tokens, row_stride, k, current_index, out, out_stride);
+    } else {
+        topk_kernel<F32, false><<<static_cast<unsigned>(rows), kTopkThreads, 0, stream>>>(
+            scores, tokens, row_stride, k, current_index, out, out_stride);
+    }
+    return check_launch("popkv_topk");
+}
+
+}  // namespace
+}  // namespace popkv
+
+extern "C" int popkv_topk(const void* scores, int scores_dtype, int64_t rows, int64_t tokens,
+                          int64_t row_stride, int64_t k, int64_t current_index, int64_t* out,
+                          int64_t out_stride, void* stream) {
+    using namespace popkv;
+    if (scores_dtype != POPKV_DTYPE_F16 && scores_dtype != POPKV_DTYPE_F32)
+        return fail(POPKV_ERR_INVALID, "popkv_topk: scores must be fp16 or fp32");
+    if (rows < 0 || tokens < 0) return fail(POPKV_ERR_INVALID, "popkv_topk: negative shape");
+    if (k < 0 || k > tokens)
+        return fail(POPKV_ERR_INVALID, "popkv_topk: k must be between 0 and the token count");
+    if (row_stride < tokens) return fail(POPKV_ERR_INVALID, "popkv_topk: row_stride < tokens");
+    const int64_t width = k + (current_index >= 0 ? 1 : 0);
+    if (out_stride < width) return fail(POPKV_ERR_INVALID, "popkv_topk: out_stride too small");
+    if (tokens > 0x7FFFFFFFll) return fail(POPKV_ERR_UNSUPPORTED, "popkv_topk: more than 2^31 tokens");
+    if (rows == 0 || width == 0) return POPKV_OK;
+    if (!out || (k > 0 && !scores)) return fail(POPKV_ERR_INVALID, "popkv_topk: null pointer");
+    if (rows > 0x7FFFFFFFll) return fail(POPKV_ERR_UNSUPPORTED, "popkv_topk: too many rows");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (scores_dtype == POPKV_DTYPE_F32)
+        return launch_topk<true>(scores, rows, tokens, row_stride, k, current_index, out, out_stride, s);
+    return launch_topk<false>(scores, rows, tokens, row_stride, k, current_index, out, out_stride, s);
+}
