@@ -224,6 +224,229 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_partial128_kernel(
     }
 }
 
+// ---------------------------------------------------------------------------
+// Pipelined partial kernel (head_dim 128, 16-bit K/V).
+//
+// Thread t owns row group r = t / 8 and 16-byte units c and c + 8 of the
+// head dim (dims 8c..8c+7 and 64+8c..64+8c+7).  The split is walked in
+// sub-chunks of 32 slots; for each, thread t copies exactly the K and V units
+// it will later read (cp.async, 16 B, L2-only) into a kPipeStages-deep ring of
+// shared-memory stages, so the copy -> compute hand-off is a per-thread
+// cp.async.wait_group with no block barrier.  The 8 threads of a row reduce
+// q.k with shuffles; each row group keeps its own online-softmax state and the
+// 32 states are combined once at the end.  Eight threads read one 256-byte row
+// per phase, which touches all 32 banks once: no conflicts.
+// ---------------------------------------------------------------------------
+constexpr int kPipeRows = 32;       // slots per sub-chunk
+constexpr int kPipeStages = 3;      // ring depth (2 sub-chunks in flight while computing)
+constexpr int kPipeMaxSub = 8;      // prefetched slot indices per thread (splits <= 256 slots)
+constexpr int kRowBytes = 256;      // 128 x 16-bit
+
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+    const uint32_t dst = static_cast<uint32_t>(__cvta_generic_to_shared(smem));
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(dst), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory"); }
+
+template <typename KT>
+__device__ __forceinline__ void unpack_unit(const uint4& u, float* f) {
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        if constexpr (std::is_same<KT, __nv_bfloat16>::value) {
+            f[2 * j] = bf16_lo(w[j]);
+            f[2 * j + 1] = bf16_hi(w[j]);
+        } else {
+            const float2 v = __half22float2(*reinterpret_cast<const __half2*>(&w[j]));
+            f[2 * j] = v.x;
+            f[2 * j + 1] = v.y;
+        }
+    }
+}
+
+struct SoftmaxState {
+    float m, s, acc[16];
+};
+
+template <typename QT, typename KT>
+__global__ void __launch_bounds__(kAttnThreads, 4) attn_partial_pipe_kernel(
+    const QT* __restrict__ queries, const KT* __restrict__ prefix_k, const KT* __restrict__ prefix_v,
+    const KT* __restrict__ cur_k, const KT* __restrict__ cur_v, const int64_t* __restrict__ indices,
+    const uint8_t* __restrict__ valid, const int64_t* __restrict__ head_to_kv,
+    float* __restrict__ partials, int q_heads, int kv_heads, int64_t prefix_tokens,
+    int64_t kbs, int64_t khs, int64_t kts, int64_t vbs, int64_t vhs, int64_t vts,
+    int64_t selected, int64_t split_tokens, int splits, float scale) {
+    extern __shared__ __align__(16) unsigned char ring[];  // [stage][K|V][32 rows][256 B]
+    __shared__ float s_m[kAttnThreads / 32], s_s[kAttnThreads / 32];
+    __shared__ float s_acc[kAttnThreads / 32][8][16];
+    __shared__ __align__(16) float s_q[128];
+
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int r = tid >> 3, c = tid & 7;
+    const int64_t row = blockIdx.y;
+    const int64_t b = row / q_heads;
+    const int qh = static_cast<int>(row % q_heads);
+    const int64_t kvh = head_to_kv[qh];
+    const int split = blockIdx.x;
+    const int64_t slot0 = static_cast<int64_t>(split) * split_tokens;
+    const int64_t slot_end = min(slot0 + split_tokens, selected);
+    const int nsub = static_cast<int>((slot_end - slot0 + kPipeRows - 1) / kPipeRows);
+
+    // Cache-row offsets (elements) of this thread's slots; -1 = masked.
+    const unsigned char* kb = reinterpret_cast<const unsigned char*>(prefix_k + b * kbs + kvh * khs);
+    const unsigned char* vb = reinterpret_cast<const unsigned char*>(prefix_v + b * vbs + kvh * vhs);
+    const unsigned char* ckb = reinterpret_cast<const unsigned char*>(cur_k + (b * kv_heads + kvh) * 128);
+    const unsigned char* cvb = reinterpret_cast<const unsigned char*>(cur_v + (b * kv_heads + kvh) * 128);
+    int rid[kPipeMaxSub];
+#pragma unroll
+    for (int i = 0; i < kPipeMaxSub; ++i) {
+        const int64_t slot = slot0 + static_cast<int64_t>(i) * kPipeRows + r;
+        int id = kSlotMasked;
+        if (i < nsub && slot < slot_end && (!valid || valid[row * selected + slot])) {
+            const int64_t idx = indices[row * selected + slot];
+            id = idx == prefix_tokens ? kSlotCurrent
+                                      : static_cast<int>(idx < 0 ? 0 : (idx > prefix_tokens - 1 ? prefix_tokens - 1 : idx));
+        }
+        rid[i] = id;
+    }
+
+    auto stage_k = [&](int st) { return ring + (st * 2 + 0) * kPipeRows * kRowBytes + r * kRowBytes; };
+    auto stage_v = [&](int st) { return ring + (st * 2 + 1) * kPipeRows * kRowBytes + r * kRowBytes; };
+    auto issue = [&](int i) {
+        if (i < nsub) {
+            const int id = rid[i];
+            if (id != kSlotMasked) {
+                const unsigned char* ks = id == kSlotCurrent ? ckb : kb + static_cast<int64_t>(id) * kts * 2;
+                const unsigned char* vs = id == kSlotCurrent ? cvb : vb + static_cast<int64_t>(id) * vts * 2;
+                const int st = i % kPipeStages;
+                cp_async16(stage_k(st) + c * 16, ks + c * 16);
+                cp_async16(stage_k(st) + (c + 8) * 16, ks + (c + 8) * 16);
+                cp_async16(stage_v(st) + c * 16, vs + c * 16);
+                cp_async16(stage_v(st) + (c + 8) * 16, vs + (c + 8) * 16);
+            }
+        }
+        cp_async_commit();
+    };
+
+    if (tid < 128) s_q[tid] = load_float(queries + row * 128 + tid);
+
+#pragma unroll
+    for (int i = 0; i < kPipeStages - 1; ++i) issue(i);
+    __syncthreads();  // s_q
+
+    SoftmaxState st;
+    st.m = -INFINITY;
+    st.s = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) st.acc[j] = 0.0f;
+
+#pragma unroll
+    for (int i = 0; i < kPipeMaxSub; ++i) {
+        if (i >= nsub) break;
+        issue(i + kPipeStages - 1);
+        cp_async_wait<kPipeStages - 1>();
+        const int id = rid[i];
+        // Every thread of the row group sees the same id, so the shuffles below
+        // are uniform across the 8 lanes that take part in them.
+        const int sidx = i % kPipeStages;
+        float kf[16];
+        if (id != kSlotMasked) {
+            unpack_unit<KT>(*reinterpret_cast<const uint4*>(stage_k(sidx) + c * 16), kf);
+            unpack_unit<KT>(*reinterpret_cast<const uint4*>(stage_k(sidx) + (c + 8) * 16), kf + 8);
+        } else {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) kf[j] = 0.0f;
+        }
+        float dot = 0.0f;
+        {
+            const float4* q0 = reinterpret_cast<const float4*>(s_q + 8 * c);
+            const float4* q1 = reinterpret_cast<const float4*>(s_q + 64 + 8 * c);
+            const float4 qa = q0[0], qb = q0[1], qc = q1[0], qd = q1[1];
+            const float qv[16] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w,
+                                  qc.x, qc.y, qc.z, qc.w, qd.x, qd.y, qd.z, qd.w};
+#pragma unroll
+            for (int j = 0; j < 16; ++j) dot = __fmaf_rn(kf[j], qv[j], dot);
+        }
+        dot += __shfl_xor_sync(0xFFFFFFFFu, dot, 4);
+        dot += __shfl_xor_sync(0xFFFFFFFFu, dot, 2);
+        dot += __shfl_xor_sync(0xFFFFFFFFu, dot, 1);
+        if (id != kSlotMasked) {
+            const float logit = dot * scale;
+            float vf[16];
+            unpack_unit<KT>(*reinterpret_cast<const uint4*>(stage_v(sidx) + c * 16), vf);
+            unpack_unit<KT>(*reinterpret_cast<const uint4*>(stage_v(sidx) + (c + 8) * 16), vf + 8);
+            if (st.m == -INFINITY) {
+                st.m = logit;
+                st.s = 1.0f;
+#pragma unroll
+                for (int j = 0; j < 16; ++j) st.acc[j] = vf[j];
+            } else {
+                const float m_new = fmaxf(st.m, logit);
+                const float alpha = expf(st.m - m_new);
+                const float p = expf(logit - m_new);
+                st.s = __fmaf_rn(st.s, alpha, p);
+#pragma unroll
+                for (int j = 0; j < 16; ++j) st.acc[j] = __fmaf_rn(p, vf[j], st.acc[j] * alpha);
+                st.m = m_new;
+            }
+        }
+    }
+    cp_async_wait<0>();
+
+    // Combine the 4 row groups of this warp (lanes with equal c), then the 8 warps.
+#pragma unroll
+    for (int o = 8; o <= 16; o <<= 1) {
+        const float m2 = __shfl_xor_sync(0xFFFFFFFFu, st.m, o);
+        const float s2 = __shfl_xor_sync(0xFFFFFFFFu, st.s, o);
+        const float M = fmaxf(st.m, m2);
+        const float f1 = st.m == -INFINITY ? 0.0f : expf(st.m - M);
+        const float f2 = m2 == -INFINITY ? 0.0f : expf(m2 - M);
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+            const float a2 = __shfl_xor_sync(0xFFFFFFFFu, st.acc[j], o);
+            st.acc[j] = st.acc[j] * f1 + a2 * f2;
+        }
+        st.s = st.s * f1 + s2 * f2;
+        st.m = M;
+    }
+    if (lane < 8) {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) s_acc[warp][lane][j] = st.acc[j];
+        if (lane == 0) {
+            s_m[warp] = st.m;
+            s_s[warp] = st.s;
+        }
+    }
+    __syncthreads();
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kAttnThreads / 32; ++w) M = fmaxf(M, s_m[w]);
+    float* out = partials + (row * splits + split) * (128 + 2);
+    if (tid < 128) {
+        const int d = tid;
+        const int cc = (d & 63) >> 3, j = (d & 7) + (d >= 64 ? 8 : 0);
+        float a = 0.0f;
+        if (M != -INFINITY) {
+#pragma unroll
+            for (int w = 0; w < kAttnThreads / 32; ++w)
+                if (s_m[w] != -INFINITY) a = __fmaf_rn(s_acc[w][cc][j], expf(s_m[w] - M), a);
+        }
+        out[2 + d] = a;
+    }
+    if (tid == 0) {
+        float ssum = 0.0f;
+        if (M != -INFINITY) {
+#pragma unroll
+            for (int w = 0; w < kAttnThreads / 32; ++w)
+                if (s_m[w] != -INFINITY) ssum = __fmaf_rn(s_s[w], expf(s_m[w] - M), ssum);
+        }
+        out[0] = M;
+        out[1] = ssum;
+    }
+}
+
 // Generic head dims: one warp per (row, split), serial over slots.
 template <typename QT, typename KT>
 __global__ void attn_partial_generic_kernel(
@@ -295,21 +518,50 @@ __global__ void attn_partial_generic_kernel(
     }
 }
 
-// Merge: one CTA per row; thread d owns output dim d.
+// Merge: one CTA per row; the split maxima/sums are staged in shared memory and
+// turned into weights once, then thread d reduces output dim d over the splits.
+constexpr int kMergeMaxSplits = 1024;
+
 template <typename OT>
 __global__ void attn_merge_kernel(const float* __restrict__ partials, int64_t splits, int head_dim,
                                   OT* __restrict__ out) {
+    __shared__ float s_w[kMergeMaxSplits];
+    __shared__ float s_red[32];
+    __shared__ float s_den;
     const int64_t row = blockIdx.x;
-    const float* p = partials + row * splits * (head_dim + 2);
+    const int64_t state = head_dim + 2;
+    const float* p = partials + row * splits * state;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarps = blockDim.x >> 5;
     float gm = -INFINITY;
-    for (int64_t s = 0; s < splits; ++s) gm = fmaxf(gm, p[s * (head_dim + 2)]);
+    for (int64_t sp = tid; sp < splits; sp += blockDim.x) gm = fmaxf(gm, p[sp * state]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) gm = fmaxf(gm, __shfl_xor_sync(0xFFFFFFFFu, gm, o));
+    if (lane == 0) s_red[warp] = gm;
+    __syncthreads();
+    gm = s_red[0];
+    for (int w = 1; w < nwarps; ++w) gm = fmaxf(gm, s_red[w]);
+    __syncthreads();
     float den = 0.0f;
-    for (int64_t s = 0; s < splits; ++s)
-        den = __fmaf_rn(p[s * (head_dim + 2) + 1], expf(p[s * (head_dim + 2)] - gm), den);
-    for (int d = threadIdx.x; d < head_dim; d += blockDim.x) {
+    for (int64_t sp = tid; sp < splits; sp += blockDim.x) {
+        const float w = expf(p[sp * state] - gm);
+        s_w[sp] = w;
+        den = __fmaf_rn(p[sp * state + 1], w, den);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) den += __shfl_xor_sync(0xFFFFFFFFu, den, o);
+    if (lane == 0) s_red[warp] = den;
+    __syncthreads();
+    if (tid == 0) {
+        float d = 0.0f;
+        for (int w = 0; w < nwarps; ++w) d += s_red[w];
+        s_den = d;
+    }
+    __syncthreads();
+    den = s_den;
+    for (int d = tid; d < head_dim; d += blockDim.x) {
         float num = 0.0f;
-        for (int64_t s = 0; s < splits; ++s)
-            num = __fmaf_rn(p[s * (head_dim + 2) + 2 + d], expf(p[s * (head_dim + 2)] - gm), num);
+#pragma unroll 4
+        for (int64_t sp = 0; sp < splits; ++sp) num = __fmaf_rn(p[sp * state + 2 + d], s_w[sp], num);
         const float v = num / den;
         if constexpr (std::is_same<OT, float>::value) out[row * head_dim + d] = v;
         else if constexpr (std::is_same<OT, __half>::value) out[row * head_dim + d] = __float2half_rn(v);
@@ -332,7 +584,14 @@ int launch_partial(const void* queries, int64_t batch, int64_t q_heads, int64_t 
                         aligned(cv, 16) && (kbs * es) % 16 == 0 && (khs * es) % 16 == 0 &&
                         (kts * es) % 16 == 0 && (vbs * es) % 16 == 0 && (vhs * es) % 16 == 0 &&
                         (vts * es) % 16 == 0;
-    if (vec_ok) {
+    if (vec_ok && sizeof(KT) == 2 && split_tokens <= kPipeRows * kPipeMaxSub) {
+        constexpr size_t ring_bytes = static_cast<size_t>(kPipeStages) * 2 * kPipeRows * kRowBytes;
+        attn_partial_pipe_kernel<QT, KT><<<grid, kAttnThreads, ring_bytes, stream>>>(
+            static_cast<const QT*>(queries), static_cast<const KT*>(pk), static_cast<const KT*>(pv),
+            static_cast<const KT*>(ck), static_cast<const KT*>(cv), indices, valid, head_to_kv,
+            partials, static_cast<int>(q_heads), static_cast<int>(kv_heads), prefix_tokens, kbs,
+            khs, kts, vbs, vhs, vts, selected, split_tokens, static_cast<int>(splits), scale);
+    } else if (vec_ok) {
         attn_partial128_kernel<QT, KT><<<grid, kAttnThreads, 0, stream>>>(
             static_cast<const QT*>(queries), static_cast<const KT*>(pk), static_cast<const KT*>(pv),
             static_cast<const KT*>(ck), static_cast<const KT*>(cv), indices, valid, head_to_kv,
@@ -435,6 +694,8 @@ extern "C" int popkv_attn_merge(const float* partials, int64_t rows, int64_t spl
     if (rows == 0) return POPKV_OK;
     if (!partials || !out) return fail(POPKV_ERR_INVALID, "popkv_attn_merge: null pointer");
     if (rows > 0x7FFFFFFFll) return fail(POPKV_ERR_UNSUPPORTED, "popkv_attn_merge: too many rows");
+    if (splits > kMergeMaxSplits)
+        return fail(POPKV_ERR_UNSUPPORTED, "popkv_attn_merge: more than %d splits", kMergeMaxSplits);
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     const unsigned threads = head_dim >= 128 ? 128 : 32 * static_cast<unsigned>((head_dim + 31) / 32);
     const int d = static_cast<int>(head_dim);

@@ -173,20 +173,175 @@ __global__ void __launch_bounds__(kTopkThreads) topk_kernel(
     }
 }
 
+// Register-resident variant for rows of up to kTopkThreads * kVec * CHUNKS
+// scores: one vectorised pass over the row puts every key in registers (chunk
+// c = tid + kTopkThreads * j holds elements [c * kVec, (c + 1) * kVec)); the
+// histogram passes and the compaction then run on registers only.  Round j of
+// the compaction covers a contiguous slice of the row in thread order, so a
+// block scan per round (carrying the previous rounds' totals) yields the
+// ascending-index output positions.
+template <bool F32, int CHUNKS>
+__global__ void __launch_bounds__(kTopkThreads) topk_reg_kernel(
+    const void* __restrict__ scores, int64_t tokens, int64_t row_stride, int64_t k,
+    int64_t current_index, int64_t* __restrict__ out, int64_t out_stride, bool vec_ok) {
+    constexpr int kVec = F32 ? 4 : 8;
+    __shared__ uint32_t hist[kHistBins];
+    __shared__ unsigned long long scan_sums[kTopkWarps + 1];
+    __shared__ uint32_t sel_bin;
+    __shared__ unsigned long long sel_above;
+
+    const int64_t row = blockIdx.x;
+    const int tid = threadIdx.x;
+    int64_t* dst = out + row * out_stride;
+    if (current_index >= 0 && tid == 0) dst[k] = current_index;
+    if (k <= 0) return;
+
+    // Four registers per chunk: fp32 keys one per register, fp16 keys two per register.
+    uint32_t packed[CHUNKS][4];
+#pragma unroll
+    for (int j = 0; j < CHUNKS; ++j) {
+        const int64_t base = (static_cast<int64_t>(tid) + static_cast<int64_t>(kTopkThreads) * j) * kVec;
+        if (vec_ok && base + kVec <= tokens) {
+            if constexpr (F32) {
+                const uint4 v = __ldg(reinterpret_cast<const uint4*>(
+                    static_cast<const float*>(scores) + row * row_stride + base));
+                packed[j][0] = key32(v.x); packed[j][1] = key32(v.y);
+                packed[j][2] = key32(v.z); packed[j][3] = key32(v.w);
+            } else {
+                const uint4 v = __ldg(reinterpret_cast<const uint4*>(
+                    static_cast<const uint16_t*>(scores) + row * row_stride + base));
+                const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+                for (int e = 0; e < 4; ++e)
+                    packed[j][e] = key16(static_cast<uint16_t>(w[e] & 0xFFFFu)) |
+                                   (key16(static_cast<uint16_t>(w[e] >> 16)) << 16);
+            }
+        } else {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) packed[j][e] = 0;
+#pragma unroll
+            for (int e = 0; e < kVec; ++e) {
+                const int64_t i = base + e;
+                if (i < tokens) {
+                    if constexpr (F32) packed[j][e] = key32(static_cast<const uint32_t*>(scores)[row * row_stride + i]);
+                    else packed[j][e >> 1] |= key16(static_cast<const uint16_t*>(scores)[row * row_stride + i]) << (16 * (e & 1));
+                }
+            }
+        }
+    }
+    auto key_of = [&](int j, int e) -> uint32_t {
+        if constexpr (F32) return packed[j][e];
+        else return (packed[j][e >> 1] >> (16 * (e & 1))) & 0xFFFFu;
+    };
+    auto valid = [&](int j, int e) -> bool {
+        return (static_cast<int64_t>(tid) + static_cast<int64_t>(kTopkThreads) * j) * kVec + e < tokens;
+    };
+
+    constexpr int kPasses = F32 ? 3 : 2;
+    const int shifts[3] = {F32 ? 21 : 5, F32 ? 10 : 0, 0};
+    const int widths[3] = {11, F32 ? 11 : 5, 10};
+    uint32_t prefix = 0, prefix_mask = 0;
+    unsigned long long above = 0;
+#pragma unroll 1
+    for (int p = 0; p < kPasses; ++p) {
+        const int shift = shifts[p], width = widths[p];
+        const uint32_t nbins = 1u << width;
+        const uint32_t digit_mask = nbins - 1u;
+        for (uint32_t b = tid; b < nbins; b += kTopkThreads) hist[b] = 0;
+        __syncthreads();
+#pragma unroll
+        for (int j = 0; j < CHUNKS; ++j)
+#pragma unroll
+            for (int e = 0; e < kVec; ++e)
+                if (valid(j, e) && (key_of(j, e) & prefix_mask) == prefix)
+                    atomicAdd(&hist[(key_of(j, e) >> shift) & digit_mask], 1u);
+        __syncthreads();
+        const unsigned long long remaining = static_cast<unsigned long long>(k) - above;
+        const uint32_t per = (nbins + kTopkThreads - 1) / kTopkThreads;
+        unsigned long long local = 0;
+        for (uint32_t jj = tid * per; jj < min(nbins, (tid + 1) * per); ++jj) local += hist[nbins - 1 - jj];
+        unsigned long long total;
+        unsigned long long run = block_exclusive_scan<unsigned long long>(local, scan_sums, total);
+        for (uint32_t jj = tid * per; jj < min(nbins, (tid + 1) * per); ++jj) {
+            const uint32_t cnt = hist[nbins - 1 - jj];
+            if (run < remaining && run + cnt >= remaining) {
+                sel_bin = nbins - 1 - jj;
+                sel_above = run;
+            }
+            run += cnt;
+        }
+        __syncthreads();
+        prefix |= sel_bin << shift;
+        prefix_mask |= digit_mask << shift;
+        above += sel_above;
+        __syncthreads();
+    }
+    const uint32_t threshold = prefix;
+    const unsigned long long need = static_cast<unsigned long long>(k) - above;
+
+    unsigned long long gt_carry = 0, eq_carry = 0;
+#pragma unroll
+    for (int j = 0; j < CHUNKS; ++j) {
+        unsigned int gt = 0, eq = 0;
+#pragma unroll
+        for (int e = 0; e < kVec; ++e) {
+            if (valid(j, e)) {
+                gt += key_of(j, e) > threshold;
+                eq += key_of(j, e) == threshold;
+            }
+        }
+        unsigned long long total;
+        const unsigned long long excl = block_exclusive_scan<unsigned long long>(
+            (static_cast<unsigned long long>(gt) << 32) | eq, scan_sums, total);
+        unsigned long long gt_before = gt_carry + (excl >> 32);
+        unsigned long long eq_before = eq_carry + (excl & 0xFFFFFFFFull);
+        const int64_t base = (static_cast<int64_t>(tid) + static_cast<int64_t>(kTopkThreads) * j) * kVec;
+#pragma unroll
+        for (int e = 0; e < kVec; ++e) {
+            if (!valid(j, e)) continue;
+            const uint32_t key = key_of(j, e);
+            if (key > threshold) {
+                dst[gt_before + min(eq_before, need)] = base + e;
+                ++gt_before;
+            } else if (key == threshold) {
+                if (eq_before < need) dst[gt_before + eq_before] = base + e;
+                ++eq_before;
+            }
+        }
+        gt_carry += total >> 32;
+        eq_carry += total & 0xFFFFFFFFull;
+    }
+}
+
 template <bool F32>
 int launch_topk(const void* scores, int64_t rows, int64_t tokens, int64_t row_stride, int64_t k,
                 int64_t current_index, int64_t* out, int64_t out_stride, cudaStream_t stream) {
     const size_t key_bytes = F32 ? 4 : 2;
+    constexpr int64_t kVec = F32 ? 4 : 8;
+    const bool vec_ok = aligned(scores, 16) && (row_stride * static_cast<int64_t>(key_bytes)) % 16 == 0;
+    const int64_t per_chunk = kTopkThreads * kVec;
+    const unsigned grid = static_cast<unsigned>(rows);
+#define POPKV_TOPK_REG(C)                                                                      \
+    if (tokens <= per_chunk * (C)) {                                                           \
+        topk_reg_kernel<F32, C><<<grid, kTopkThreads, 0, stream>>>(                            \
+            scores, tokens, row_stride, k, current_index, out, out_stride, vec_ok);            \
+        return check_launch("popkv_topk");                                                     \
+    }
+    POPKV_TOPK_REG(1)
+    POPKV_TOPK_REG(2)
+    POPKV_TOPK_REG(4)
+    if constexpr (F32) { POPKV_TOPK_REG(8) }
+#undef POPKV_TOPK_REG
     const size_t stage = static_cast<size_t>(tokens) * key_bytes;
     if (stage <= kStageBytes) {
         auto kernel = topk_kernel<F32, true>;
         cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(kStageBytes));
-        kernel<<<static_cast<unsigned>(rows), kTopkThreads, stage, stream>>>(
-            scores, tokens, row_stride, k, current_index, out, out_stride);
+        kernel<<<grid, kTopkThreads, stage, stream>>>(scores, tokens, row_stride, k, current_index,
+                                                      out, out_stride);
     } else {
-        topk_kernel<F32, false><<<static_cast<unsigned>(rows), kTopkThreads, 0, stream>>>(
-            scores, tokens, row_stride, k, current_index, out, out_stride);
+        topk_kernel<F32, false><<<grid, kTopkThreads, 0, stream>>>(scores, tokens, row_stride, k,
+                                                                   current_index, out, out_stride);
     }
     return check_launch("popkv_topk");
 }

@@ -1,0 +1,146 @@
+"""Graph-captured PopKV decode step for one attention layer.
+
+The reference runs each decode stage as a separate eager launch with Python
+integers for the token count (popkv.py:1076-1115), so its host overhead is
+part of every token.  ``SparseAttentionStep`` owns static input/output buffers
+and preallocated intermediates, calls the C-ABI kernels directly, and captures
+the four launches (popcount score with the query encoding in its prologue,
+top-k + current slot, split partials, merge) into one CUDA graph.  Replaying the graph costs one launch.
+
+The graph is specific to the cache length it was captured at.  Call
+``recapture()`` after appending tokens (or use ``run_eager``).
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+
+from . import _lib
+from .popkv import PopKVCache
+
+
+class SparseAttentionStep:
+    """One layer's decode-time retrieval + sparse attention for a batch of queries.
+
+    Args:
+        cache: the layer's PopKV metadata (prefix keys already packed).
+        prefix_keys, prefix_values: [B, KVH, T, D] (strided views allowed, head_dim
+            contiguous) or [KVH, T, D] for batch 1; T = the cache's token count.
+        head_to_kv: int64 [QH] GQA mapping (consecutive query heads per KV head).
+        budget: selected tokens per query head including the current slot.
+        q_dtype: dtype of the queries / outputs.
+    """
+
+    def __init__(self, cache: PopKVCache, prefix_keys: torch.Tensor, prefix_values: torch.Tensor,
+                 head_to_kv: torch.Tensor, *, budget: int, q_heads: int | None = None,
+                 q_dtype: torch.dtype = torch.bfloat16, split_tokens: int = 256,
+                 batch: int = 1, use_graph: bool = True) -> None:
+        if prefix_keys.ndim == 3:
+            prefix_keys, prefix_values = prefix_keys[None], prefix_values[None]
+        if prefix_keys.stride(-1) != 1 or prefix_values.stride(-1) != 1:
+            raise ValueError("prefix keys/values need a contiguous head dim")
+        self.cache = cache
+        self.device = prefix_keys.device
+        self.batch = int(batch)
+        self.kv_heads = int(prefix_keys.shape[1])
+        self.prefix_tokens = int(prefix_keys.shape[2])
+        self.head_dim = int(prefix_keys.shape[3])
+        if self.head_dim != 128:
+            raise ValueError("SparseAttentionStep needs head_dim 128 (the fp16 score path)")
+        if int(prefix_keys.shape[0]) != self.batch:
+            raise ValueError("prefix keys batch does not match")
+        if cache.token_count != self.prefix_tokens:
+            raise ValueError("cache token count must equal the prefix length")
+        self.head_to_kv = head_to_kv.to(device=self.device, dtype=torch.int64).contiguous()
+        self.q_heads = int(self.head_to_kv.numel()) if q_heads is None else int(q_heads)
+        self.prefix_keys, self.prefix_values = prefix_keys, prefix_values
+        self.budget = int(budget)
+        self.k = min(self.budget - 1, self.prefix_tokens)
+        self.selected = self.k + 1
+        self.split_tokens = int(split_tokens)
+        self.splits = math.ceil(self.selected / self.split_tokens)
+        self.g = int(cache.dim_group_size)
+        reps = 128 // self.g
+        dev, B, QH, KVH, D = self.device, self.batch, self.q_heads, self.kv_heads, self.head_dim
+        kv_dtype = prefix_keys.dtype
+        # Static inputs / outputs.
+        self.queries = torch.zeros((B, QH, D), device=dev, dtype=q_dtype)
+        self.current_keys = torch.zeros((B, KVH, D), device=dev, dtype=kv_dtype)
+        self.current_values = torch.zeros((B, KVH, D), device=dev, dtype=kv_dtype)
+        self.output = torch.zeros((B, QH, D), device=dev, dtype=q_dtype)
+        # Intermediates.
+        self.q_sign = torch.zeros((B, QH, 4), device=dev, dtype=torch.int32)
+        self.q_mag = torch.zeros_like(self.q_sign)
+        self.q_low = torch.zeros((B, QH, reps), device=dev, dtype=torch.float32)
+        self.q_delta = torch.zeros_like(self.q_low)
+        self.scores = torch.zeros((B, QH, self.prefix_tokens), device=dev, dtype=torch.float16)
+        self.indices = torch.zeros((B, QH, self.selected), device=dev, dtype=torch.int64)
+        self.partials = torch.zeros((B, QH, self.splits, D + 2), device=dev, dtype=torch.float32)
+        self.graph = None
+        self.use_graph = use_graph
+        if use_graph:
+            self.recapture()
+
+    # -- launches ---------------------------------------------------------------
+    def _launch(self, stream) -> None:
+        lib, check, ptr = _lib.lib(), _lib.check, _lib.ptr
+        s = ctypes_stream(stream)
+        B, QH, KVH = self.batch, self.q_heads, self.kv_heads
+        packed = self.cache.packed
+        capacity = int(packed[0].shape[1])
+        # Query encoding runs in the score kernel's prologue (one launch fewer).
+        check(lib.popkv_score(ptr(self.queries), _lib.dtype_code(self.queries), B, QH, 128,
+                              *(ptr(t) for t in packed), KVH, capacity, ptr(self.head_to_kv),
+                              self.prefix_tokens, self.g, ptr(self.scores), _lib.F16, s))
+        check(lib.popkv_topk(ptr(self.scores), _lib.F16, B * QH, self.prefix_tokens,
+                             self.prefix_tokens, self.k, self.prefix_tokens, ptr(self.indices),
+                             self.selected, s))
+        pk, pv = self.prefix_keys, self.prefix_values
+        check(lib.popkv_attn_partial(
+            ptr(self.queries), _lib.dtype_code(self.queries), B, QH, 128, ptr(pk), ptr(pv),
+            _lib.dtype_code(pk), KVH, self.prefix_tokens, pk.stride(0), pk.stride(1), pk.stride(2),
+            pv.stride(0), pv.stride(1), pv.stride(2), ptr(self.current_keys),
+            ptr(self.current_values), ptr(self.indices), self.selected, None, ptr(self.head_to_kv),
+            self.split_tokens, ptr(self.partials), s))
+        check(lib.popkv_attn_merge(ptr(self.partials), B * QH, self.splits, 128, ptr(self.output),
+                                   _lib.dtype_code(self.output), s))
+
+    def recapture(self) -> None:
+        """(Re)build the CUDA graph of the four launches for the current buffers."""
+        with torch.cuda.device(self.device):
+            side = torch.cuda.Stream(self.device)
+            side.wait_stream(torch.cuda.current_stream(self.device))
+            with torch.cuda.stream(side):
+                for _ in range(2):  # warm up outside capture (sets kernel attributes)
+                    self._launch(side)
+            torch.cuda.current_stream(self.device).wait_stream(side)
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=side):
+                self._launch(side)
+            self.graph = graph
+
+    def run_eager(self) -> torch.Tensor:
+        with torch.cuda.device(self.device):
+            self._launch(torch.cuda.current_stream(self.device))
+        return self.output
+
+    def replay(self) -> torch.Tensor:
+        """Run the step on the static buffers; returns ``self.output``."""
+        if self.graph is None:
+            return self.run_eager()
+        self.graph.replay()
+        return self.output
+
+    def __call__(self, queries: torch.Tensor, current_keys: torch.Tensor,
+                 current_values: torch.Tensor) -> torch.Tensor:
+        """Copy the step's inputs (host or device) in, run, return the device output."""
+        self.queries.copy_(queries.view_as(self.queries), non_blocking=True)
+        self.current_keys.copy_(current_keys.view_as(self.current_keys), non_blocking=True)
+        self.current_values.copy_(current_values.view_as(self.current_values), non_blocking=True)
+        return self.replay()
+
+
+def ctypes_stream(stream: torch.cuda.Stream):
+    import ctypes
+    return ctypes.c_void_p(stream.cuda_stream)

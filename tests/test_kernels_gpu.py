@@ -286,10 +286,14 @@ def _oracle_attention(queries, keys, values, cur_k, cur_v, indices, mapping, mas
                                None if mask is None else mask.cpu().numpy(), split_tokens=split)
 
 
-def _check_attention(out, want):
+_OUT_EPS = {torch.float32: 0.0, torch.float16: 2.0 ** -11, torch.bfloat16: 2.0 ** -8}
+
+
+def _check_attention(out, want, dtype=torch.float32):
     err = np.abs(out.astype(np.float64) - want)
     assert err.max() <= 2e-2 and err.mean() <= 2e-3, (err.max(), err.mean())
-    assert err.max() <= 1e-4, err.max()  # fp32 kernel: far inside the stated bar
+    # fp32 arithmetic: beyond the output's own rounding, the error stays near 1e-5.
+    assert np.all(err <= 2e-5 + np.abs(want) * _OUT_EPS[dtype]), err.max()
 
 
 @pytest.mark.parametrize("dtype", DTYPES)
@@ -307,7 +311,7 @@ def test_split_attention_matches_oracle(cuda_device, dtype, valid, split):
     np.testing.assert_allclose(got[..., 1:], want[..., 1:], atol=1e-3, rtol=1e-4)
     merged = S.indexed_attention_split_merge(partials, args[0])
     assert merged.dtype == dtype
-    _check_attention(merged.float().cpu().numpy(), oracle.attn_merge(want))
+    _check_attention(merged.float().cpu().numpy(), oracle.attn_merge(want), dtype)
 
 
 @pytest.mark.parametrize("dim", (64, 96))
@@ -315,7 +319,7 @@ def test_split_attention_generic_head_dim(cuda_device, dim):
     args = _attn_inputs(cuda_device, dim=dim, valid=True, seed=dim)
     out = S.indexed_attention_split(*args[:6], args[6], args[7], split_tokens=256)
     want = oracle.attn_merge(_oracle_attention(*args, 256))
-    _check_attention(out.float().cpu().numpy(), want)
+    _check_attention(out.float().cpu().numpy(), want, torch.bfloat16)
 
 
 def test_split_attention_matches_reference_golden(cuda_device, golden):
