@@ -237,10 +237,14 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_partial128_kernel(
 // 32 states are combined once at the end.  Eight threads read one 256-byte row
 // per phase, which touches all 32 banks once: no conflicts.
 // ---------------------------------------------------------------------------
-constexpr int kPipeRows = 32;       // slots per sub-chunk
-constexpr int kPipeStages = 3;      // ring depth (2 sub-chunks in flight while computing)
-constexpr int kPipeMaxSub = 8;      // prefetched slot indices per thread (splits <= 256 slots)
-constexpr int kRowBytes = 256;      // 128 x 16-bit
+constexpr int kPipeRowGroups = 32;  // 8 threads per row -> 32 row groups per CTA
+constexpr int kPipeRowsPerGroup = 2; // rows per row group per sub-chunk
+constexpr int kPipeRows = kPipeRowGroups * kPipeRowsPerGroup;  // 64 slots per sub-chunk
+constexpr int kPipeStages = 3;       // ring depth (2 sub-chunks in flight while computing)
+constexpr int kPipeMaxSub = 4;       // sub-chunks per split (splits <= 256 slots)
+constexpr int kRowBytes = 256;       // 128 x 16-bit
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn2 = 0.6931471805599453f;
 
 __device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
     const uint32_t dst = static_cast<uint32_t>(__cvta_generic_to_shared(smem));
@@ -266,22 +270,27 @@ __device__ __forceinline__ void unpack_unit(const uint4& u, float* f) {
     }
 }
 
-struct SoftmaxState {
-    float m, s, acc[16];
-};
-
+// Pipelined partial kernel (head_dim 128, 16-bit K/V).
+//
+// Thread t owns row group r = t / 8 and 16-byte units c and c + 8 (dims
+// 8c..8c+7 and 64+8c..64+8c+7) of each row it handles.  The split is walked
+// in sub-chunks of 64 slots, two rows per row group; thread t cp.async-copies
+// exactly the K and V units it will read into a kPipeStages-deep ring, so the
+// hand-off is a per-thread cp.async.wait_group with no block barrier.  Logits
+// are kept in the base-2 domain (scale * log2 e folded in) so each softmax
+// weight is one exp2; the running sum/accumulator are rescaled only when the
+// running maximum grows.  The partial's max is written back in natural units.
 template <typename QT, typename KT>
-__global__ void __launch_bounds__(kAttnThreads, 4) attn_partial_pipe_kernel(
+__global__ void __launch_bounds__(kAttnThreads, 2) attn_partial_pipe_kernel(
     const QT* __restrict__ queries, const KT* __restrict__ prefix_k, const KT* __restrict__ prefix_v,
     const KT* __restrict__ cur_k, const KT* __restrict__ cur_v, const int64_t* __restrict__ indices,
     const uint8_t* __restrict__ valid, const int64_t* __restrict__ head_to_kv,
     float* __restrict__ partials, int q_heads, int kv_heads, int64_t prefix_tokens,
     int64_t kbs, int64_t khs, int64_t kts, int64_t vbs, int64_t vhs, int64_t vts,
     int64_t selected, int64_t split_tokens, int splits, float scale) {
-    extern __shared__ __align__(16) unsigned char ring[];  // [stage][K|V][32 rows][256 B]
+    extern __shared__ __align__(16) unsigned char ring[];  // [stage][K|V][64 rows][256 B]
     __shared__ float s_m[kAttnThreads / 32], s_s[kAttnThreads / 32];
     __shared__ float s_acc[kAttnThreads / 32][8][16];
-    __shared__ __align__(16) float s_q[128];
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int r = tid >> 3, c = tid & 7;
@@ -294,102 +303,111 @@ __global__ void __launch_bounds__(kAttnThreads, 4) attn_partial_pipe_kernel(
     const int64_t slot_end = min(slot0 + split_tokens, selected);
     const int nsub = static_cast<int>((slot_end - slot0 + kPipeRows - 1) / kPipeRows);
 
-    // Cache-row offsets (elements) of this thread's slots; -1 = masked.
-    const unsigned char* kb = reinterpret_cast<const unsigned char*>(prefix_k + b * kbs + kvh * khs);
-    const unsigned char* vb = reinterpret_cast<const unsigned char*>(prefix_v + b * vbs + kvh * vhs);
-    const unsigned char* ckb = reinterpret_cast<const unsigned char*>(cur_k + (b * kv_heads + kvh) * 128);
-    const unsigned char* cvb = reinterpret_cast<const unsigned char*>(cur_v + (b * kv_heads + kvh) * 128);
-    int rid[kPipeMaxSub];
-#pragma unroll
-    for (int i = 0; i < kPipeMaxSub; ++i) {
-        const int64_t slot = slot0 + static_cast<int64_t>(i) * kPipeRows + r;
-        int id = kSlotMasked;
-        if (i < nsub && slot < slot_end && (!valid || valid[row * selected + slot])) {
-            const int64_t idx = indices[row * selected + slot];
-            id = idx == prefix_tokens ? kSlotCurrent
-                                      : static_cast<int>(idx < 0 ? 0 : (idx > prefix_tokens - 1 ? prefix_tokens - 1 : idx));
-        }
-        rid[i] = id;
-    }
+    const unsigned char* kb = reinterpret_cast<const unsigned char*>(prefix_k + b * kbs + kvh * khs) + c * 16;
+    const unsigned char* vb = reinterpret_cast<const unsigned char*>(prefix_v + b * vbs + kvh * vhs) + c * 16;
+    const unsigned char* ckb = reinterpret_cast<const unsigned char*>(cur_k + (b * kv_heads + kvh) * 128) + c * 16;
+    const unsigned char* cvb = reinterpret_cast<const unsigned char*>(cur_v + (b * kv_heads + kvh) * 128) + c * 16;
+    const int64_t kstride = kts * 2, vstride = vts * 2;
 
-    auto stage_k = [&](int st) { return ring + (st * 2 + 0) * kPipeRows * kRowBytes + r * kRowBytes; };
-    auto stage_v = [&](int st) { return ring + (st * 2 + 1) * kPipeRows * kRowBytes + r * kRowBytes; };
+    // Cache row of each slot this thread copies: slot = slot0 + i*64 + h*32 + r.
+    int rid[kPipeMaxSub][kPipeRowsPerGroup];
+#pragma unroll
+    for (int i = 0; i < kPipeMaxSub; ++i)
+#pragma unroll
+        for (int h = 0; h < kPipeRowsPerGroup; ++h) {
+            const int64_t slot = slot0 + static_cast<int64_t>(i) * kPipeRows + h * kPipeRowGroups + r;
+            int id = kSlotMasked;
+            if (slot < slot_end && (!valid || valid[row * selected + slot])) {
+                const int64_t idx = __ldg(indices + row * selected + slot);
+                id = idx == prefix_tokens ? kSlotCurrent
+                                          : static_cast<int>(idx < 0 ? 0 : (idx > prefix_tokens - 1 ? prefix_tokens - 1 : idx));
+            }
+            rid[i][h] = id;
+        }
+
+    auto stage_k = [&](int st, int h) {
+        return ring + ((st * 2 + 0) * kPipeRows + h * kPipeRowGroups + r) * kRowBytes + c * 16;
+    };
+    auto stage_v = [&](int st, int h) {
+        return ring + ((st * 2 + 1) * kPipeRows + h * kPipeRowGroups + r) * kRowBytes + c * 16;
+    };
     auto issue = [&](int i) {
         if (i < nsub) {
-            const int id = rid[i];
-            if (id != kSlotMasked) {
-                const unsigned char* ks = id == kSlotCurrent ? ckb : kb + static_cast<int64_t>(id) * kts * 2;
-                const unsigned char* vs = id == kSlotCurrent ? cvb : vb + static_cast<int64_t>(id) * vts * 2;
-                const int st = i % kPipeStages;
-                cp_async16(stage_k(st) + c * 16, ks + c * 16);
-                cp_async16(stage_k(st) + (c + 8) * 16, ks + (c + 8) * 16);
-                cp_async16(stage_v(st) + c * 16, vs + c * 16);
-                cp_async16(stage_v(st) + (c + 8) * 16, vs + (c + 8) * 16);
+            const int st = i % kPipeStages;
+#pragma unroll
+            for (int h = 0; h < kPipeRowsPerGroup; ++h) {
+                const int id = rid[i][h];
+                if (id != kSlotMasked) {
+                    const unsigned char* ks = id == kSlotCurrent ? ckb : kb + static_cast<int64_t>(id) * kstride;
+                    const unsigned char* vs = id == kSlotCurrent ? cvb : vb + static_cast<int64_t>(id) * vstride;
+                    cp_async16(stage_k(st, h), ks);
+                    cp_async16(stage_k(st, h) + 128, ks + 128);
+                    cp_async16(stage_v(st, h), vs);
+                    cp_async16(stage_v(st, h) + 128, vs + 128);
+                }
             }
         }
         cp_async_commit();
     };
 
-    if (tid < 128) s_q[tid] = load_float(queries + row * 128 + tid);
-
 #pragma unroll
     for (int i = 0; i < kPipeStages - 1; ++i) issue(i);
-    __syncthreads();  // s_q
 
-    SoftmaxState st;
-    st.m = -INFINITY;
-    st.s = 0.0f;
+    float q[16];
+    {
+        const QT* qp = queries + row * 128;
+        const float qscale = scale * kLog2e;
 #pragma unroll
-    for (int j = 0; j < 16; ++j) st.acc[j] = 0.0f;
+        for (int j = 0; j < 8; ++j) {
+            q[j] = load_float(qp + 8 * c + j) * qscale;
+            q[8 + j] = load_float(qp + 64 + 8 * c + j) * qscale;
+        }
+    }
+
+    float m = -INFINITY, ssum = 0.0f;  // m in log2 units
+    float acc[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) acc[j] = 0.0f;
 
 #pragma unroll
     for (int i = 0; i < kPipeMaxSub; ++i) {
         if (i >= nsub) break;
         issue(i + kPipeStages - 1);
         cp_async_wait<kPipeStages - 1>();
-        const int id = rid[i];
-        // Every thread of the row group sees the same id, so the shuffles below
-        // are uniform across the 8 lanes that take part in them.
-        const int sidx = i % kPipeStages;
-        float kf[16];
-        if (id != kSlotMasked) {
-            unpack_unit<KT>(*reinterpret_cast<const uint4*>(stage_k(sidx) + c * 16), kf);
-            unpack_unit<KT>(*reinterpret_cast<const uint4*>(stage_k(sidx) + (c + 8) * 16), kf + 8);
-        } else {
+        const int st = i % kPipeStages;
 #pragma unroll
-            for (int j = 0; j < 16; ++j) kf[j] = 0.0f;
-        }
-        float dot = 0.0f;
-        {
-            const float4* q0 = reinterpret_cast<const float4*>(s_q + 8 * c);
-            const float4* q1 = reinterpret_cast<const float4*>(s_q + 64 + 8 * c);
-            const float4 qa = q0[0], qb = q0[1], qc = q1[0], qd = q1[1];
-            const float qv[16] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w,
-                                  qc.x, qc.y, qc.z, qc.w, qd.x, qd.y, qd.z, qd.w};
-#pragma unroll
-            for (int j = 0; j < 16; ++j) dot = __fmaf_rn(kf[j], qv[j], dot);
-        }
-        dot += __shfl_xor_sync(0xFFFFFFFFu, dot, 4);
-        dot += __shfl_xor_sync(0xFFFFFFFFu, dot, 2);
-        dot += __shfl_xor_sync(0xFFFFFFFFu, dot, 1);
-        if (id != kSlotMasked) {
-            const float logit = dot * scale;
-            float vf[16];
-            unpack_unit<KT>(*reinterpret_cast<const uint4*>(stage_v(sidx) + c * 16), vf);
-            unpack_unit<KT>(*reinterpret_cast<const uint4*>(stage_v(sidx) + (c + 8) * 16), vf + 8);
-            if (st.m == -INFINITY) {
-                st.m = logit;
-                st.s = 1.0f;
-#pragma unroll
-                for (int j = 0; j < 16; ++j) st.acc[j] = vf[j];
+        for (int h = 0; h < kPipeRowsPerGroup; ++h) {
+            const int id = rid[i][h];  // uniform across the 8 lanes of the row group
+            float kf[16];
+            if (id != kSlotMasked) {
+                unpack_unit<KT>(*reinterpret_cast<const uint4*>(stage_k(st, h)), kf);
+                unpack_unit<KT>(*reinterpret_cast<const uint4*>(stage_k(st, h) + 128), kf + 8);
             } else {
-                const float m_new = fmaxf(st.m, logit);
-                const float alpha = expf(st.m - m_new);
-                const float p = expf(logit - m_new);
-                st.s = __fmaf_rn(st.s, alpha, p);
 #pragma unroll
-                for (int j = 0; j < 16; ++j) st.acc[j] = __fmaf_rn(p, vf[j], st.acc[j] * alpha);
-                st.m = m_new;
+                for (int j = 0; j < 16; ++j) kf[j] = 0.0f;
+            }
+            float dot = 0.0f;
+#pragma unroll
+            for (int j = 0; j < 16; ++j) dot = __fmaf_rn(kf[j], q[j], dot);
+            dot += __shfl_xor_sync(0xFFFFFFFFu, dot, 4);
+            dot += __shfl_xor_sync(0xFFFFFFFFu, dot, 2);
+            dot += __shfl_xor_sync(0xFFFFFFFFu, dot, 1);
+            if (id != kSlotMasked) {
+                float vf[16];
+                unpack_unit<KT>(*reinterpret_cast<const uint4*>(stage_v(st, h)), vf);
+                unpack_unit<KT>(*reinterpret_cast<const uint4*>(stage_v(st, h) + 128), vf + 8);
+                if (dot > m) {  // new maximum: rescale what has been accumulated
+                    const float alpha = exp2f(m - dot);  // 0 when m == -inf
+                    ssum = __fmaf_rn(ssum, alpha, 1.0f);
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) acc[j] = __fmaf_rn(acc[j], alpha, vf[j]);
+                    m = dot;
+                } else {
+                    const float p = exp2f(dot - m);
+                    ssum += p;
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) acc[j] = __fmaf_rn(p, vf[j], acc[j]);
+                }
             }
         }
     }
@@ -398,25 +416,25 @@ __global__ void __launch_bounds__(kAttnThreads, 4) attn_partial_pipe_kernel(
     // Combine the 4 row groups of this warp (lanes with equal c), then the 8 warps.
 #pragma unroll
     for (int o = 8; o <= 16; o <<= 1) {
-        const float m2 = __shfl_xor_sync(0xFFFFFFFFu, st.m, o);
-        const float s2 = __shfl_xor_sync(0xFFFFFFFFu, st.s, o);
-        const float M = fmaxf(st.m, m2);
-        const float f1 = st.m == -INFINITY ? 0.0f : expf(st.m - M);
-        const float f2 = m2 == -INFINITY ? 0.0f : expf(m2 - M);
+        const float m2 = __shfl_xor_sync(0xFFFFFFFFu, m, o);
+        const float s2 = __shfl_xor_sync(0xFFFFFFFFu, ssum, o);
+        const float M = fmaxf(m, m2);
+        const float f1 = m == -INFINITY ? 0.0f : exp2f(m - M);
+        const float f2 = m2 == -INFINITY ? 0.0f : exp2f(m2 - M);
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
-            const float a2 = __shfl_xor_sync(0xFFFFFFFFu, st.acc[j], o);
-            st.acc[j] = st.acc[j] * f1 + a2 * f2;
+            const float a2 = __shfl_xor_sync(0xFFFFFFFFu, acc[j], o);
+            acc[j] = acc[j] * f1 + a2 * f2;
         }
-        st.s = st.s * f1 + s2 * f2;
-        st.m = M;
+        ssum = ssum * f1 + s2 * f2;
+        m = M;
     }
     if (lane < 8) {
 #pragma unroll
-        for (int j = 0; j < 16; ++j) s_acc[warp][lane][j] = st.acc[j];
+        for (int j = 0; j < 16; ++j) s_acc[warp][lane][j] = acc[j];
         if (lane == 0) {
-            s_m[warp] = st.m;
-            s_s[warp] = st.s;
+            s_m[warp] = m;
+            s_s[warp] = ssum;
         }
     }
     __syncthreads();
@@ -431,19 +449,19 @@ __global__ void __launch_bounds__(kAttnThreads, 4) attn_partial_pipe_kernel(
         if (M != -INFINITY) {
 #pragma unroll
             for (int w = 0; w < kAttnThreads / 32; ++w)
-                if (s_m[w] != -INFINITY) a = __fmaf_rn(s_acc[w][cc][j], expf(s_m[w] - M), a);
+                if (s_m[w] != -INFINITY) a = __fmaf_rn(s_acc[w][cc][j], exp2f(s_m[w] - M), a);
         }
         out[2 + d] = a;
     }
     if (tid == 0) {
-        float ssum = 0.0f;
+        float total = 0.0f;
         if (M != -INFINITY) {
 #pragma unroll
             for (int w = 0; w < kAttnThreads / 32; ++w)
-                if (s_m[w] != -INFINITY) ssum = __fmaf_rn(s_s[w], expf(s_m[w] - M), ssum);
+                if (s_m[w] != -INFINITY) total = __fmaf_rn(s_s[w], exp2f(s_m[w] - M), total);
         }
-        out[0] = M;
-        out[1] = ssum;
+        out[0] = M == -INFINITY ? -INFINITY : M * kLn2;
+        out[1] = total;
     }
 }
 
@@ -586,6 +604,8 @@ int launch_partial(const void* queries, int64_t batch, int64_t q_heads, int64_t 
                         (vts * es) % 16 == 0;
     if (vec_ok && sizeof(KT) == 2 && split_tokens <= kPipeRows * kPipeMaxSub) {
         constexpr size_t ring_bytes = static_cast<size_t>(kPipeStages) * 2 * kPipeRows * kRowBytes;
+        const int st = allow_dynamic_smem(attn_partial_pipe_kernel<QT, KT>, static_cast<int>(ring_bytes));
+        if (st != POPKV_OK) return st;
         attn_partial_pipe_kernel<QT, KT><<<grid, kAttnThreads, ring_bytes, stream>>>(
             static_cast<const QT*>(queries), static_cast<const KT*>(pk), static_cast<const KT*>(pv),
             static_cast<const KT*>(ck), static_cast<const KT*>(cv), indices, valid, head_to_kv,

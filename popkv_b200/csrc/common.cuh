@@ -19,6 +19,21 @@ int check_launch(const char* what);
 bool valid_dtype(int dtype);
 size_t dtype_size(int dtype);
 
+// Raise a kernel's dynamic shared-memory limit once per device (needed above 48 KB).
+template <typename Kernel>
+int allow_dynamic_smem(Kernel kernel, int bytes) {
+    static unsigned long long done_mask = 0;  // bit d: device d configured
+    int device = 0;
+    if (cudaGetDevice(&device) != cudaSuccess) return fail(POPKV_ERR_CUDA, "cudaGetDevice failed");
+    const unsigned long long bit = 1ull << (device & 63);
+    if (__atomic_load_n(&done_mask, __ATOMIC_ACQUIRE) & bit) return POPKV_OK;
+    cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (err != cudaSuccess)
+        return fail(POPKV_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(err));
+    __atomic_fetch_or(&done_mask, bit, __ATOMIC_RELEASE);
+    return POPKV_OK;
+}
+
 inline bool aligned(const void* p, size_t bytes) {
     return (reinterpret_cast<uintptr_t>(p) % bytes) == 0;
 }

@@ -14,6 +14,8 @@
 // pass gives every thread a contiguous slice of the row: a block scan of its
 // (greater, equal) counts yields each winner's output position, taking equal
 // keys in index order until the quota is filled.
+#include <cooperative_groups.h>
+
 #include <cstdint>
 #include <type_traits>
 
@@ -313,6 +315,262 @@ __global__ void __launch_bounds__(kTopkThreads) topk_reg_kernel(
     }
 }
 
+// ---------------------------------------------------------------------------
+// Cluster variant: CPR CTAs (a thread-block cluster) share one row, so a few
+// dozen rows still occupy every SM.  CTA q of the cluster holds the keys of
+// row slice [q * slice, (q + 1) * slice) in registers; after each local
+// histogram pass the cluster barrier makes the CPR shared-memory histograms
+// visible and every CTA sums them through distributed shared memory, so all
+// CTAs pick the same digit.  For the compaction each CTA publishes its
+// (greater, equal) totals; a CTA's output offset is the sum over lower ranks.
+// ---------------------------------------------------------------------------
+namespace cg = cooperative_groups;
+constexpr int kClusterThreads = 512;
+constexpr int kClusterWarps = kClusterThreads / 32;
+
+template <typename V>
+__device__ __forceinline__ V cta_exclusive_scan(V x, V* warp_sums, V& total) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    V incl = x;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        V y = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+        if (lane >= o) incl += y;
+    }
+    if (lane == 31) warp_sums[warp] = incl;
+    __syncthreads();
+    if (warp == 0) {
+        V w = lane < kClusterWarps ? warp_sums[lane] : V(0);
+        V wi = w;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            V y = __shfl_up_sync(0xFFFFFFFFu, wi, o);
+            if (lane >= o) wi += y;
+        }
+        if (lane < kClusterWarps) warp_sums[lane] = wi - w;
+        if (lane == kClusterWarps - 1) warp_sums[kClusterWarps] = wi;
+    }
+    __syncthreads();
+    V result = warp_sums[warp] + incl - x;
+    total = warp_sums[kClusterWarps];
+    __syncthreads();
+    return result;
+}
+
+template <bool F32, int CPR, int CHUNKS>
+__global__ void __launch_bounds__(kClusterThreads) topk_cluster_kernel(
+    const void* __restrict__ scores, int64_t tokens, int64_t row_stride, int64_t k,
+    int64_t current_index, int64_t* __restrict__ out, int64_t out_stride, bool vec_ok) {
+    constexpr int kVec = F32 ? 4 : 8;
+    constexpr int64_t kSlice = static_cast<int64_t>(kClusterThreads) * kVec * CHUNKS;
+    __shared__ uint32_t hist[kHistBins];
+    __shared__ unsigned long long scan_sums[kClusterWarps + 1];
+    __shared__ uint32_t sel_bin;
+    __shared__ unsigned long long sel_above;
+    __shared__ unsigned long long cta_totals;  // (gt << 32) | eq of this CTA
+
+    cg::cluster_group cluster = cg::this_cluster();
+    const int rank = static_cast<int>(cluster.block_rank());
+    const int64_t row = blockIdx.x / CPR;
+    const int tid = threadIdx.x;
+    int64_t* dst = out + row * out_stride;
+    if (current_index >= 0 && tid == 0 && rank == 0) dst[k] = current_index;
+    if (k <= 0) return;  // uniform across the cluster: no CTA reaches a cluster barrier
+
+    const int64_t slice0 = static_cast<int64_t>(rank) * kSlice;
+    uint32_t packed[CHUNKS][4];
+    int lim[CHUNKS];  // valid elements of each chunk (0..kVec)
+#pragma unroll
+    for (int j = 0; j < CHUNKS; ++j) {
+        const int64_t base = slice0 + (static_cast<int64_t>(tid) + static_cast<int64_t>(kClusterThreads) * j) * kVec;
+        const int64_t left = tokens - base;
+        lim[j] = left <= 0 ? 0 : (left >= kVec ? kVec : static_cast<int>(left));
+        if (vec_ok && lim[j] == kVec) {
+            if constexpr (F32) {
+                const uint4 v = __ldg(reinterpret_cast<const uint4*>(
+                    static_cast<const float*>(scores) + row * row_stride + base));
+                packed[j][0] = key32(v.x); packed[j][1] = key32(v.y);
+                packed[j][2] = key32(v.z); packed[j][3] = key32(v.w);
+            } else {
+                const uint4 v = __ldg(reinterpret_cast<const uint4*>(
+                    static_cast<const uint16_t*>(scores) + row * row_stride + base));
+                const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+                for (int e = 0; e < 4; ++e)
+                    packed[j][e] = key16(static_cast<uint16_t>(w[e] & 0xFFFFu)) |
+                                   (key16(static_cast<uint16_t>(w[e] >> 16)) << 16);
+            }
+        } else {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) packed[j][e] = 0;
+#pragma unroll
+            for (int e = 0; e < kVec; ++e) {
+                if (e < lim[j]) {
+                    if constexpr (F32) packed[j][e] = key32(static_cast<const uint32_t*>(scores)[row * row_stride + base + e]);
+                    else packed[j][e >> 1] |= key16(static_cast<const uint16_t*>(scores)[row * row_stride + base + e]) << (16 * (e & 1));
+                }
+            }
+        }
+    }
+    auto key_of = [&](int j, int e) -> uint32_t {
+        if constexpr (F32) return packed[j][e];
+        else return (packed[j][e >> 1] >> (16 * (e & 1))) & 0xFFFFu;
+    };
+
+    constexpr int kPasses = F32 ? 3 : 2;
+    uint32_t prefix = 0, prefix_mask = 0;
+    unsigned long long above = 0;
+#pragma unroll
+    for (int p = 0; p < kPasses; ++p) {
+        const int shift = p == 0 ? (F32 ? 21 : 5) : (p == 1 ? (F32 ? 10 : 0) : 0);
+        const int width = p == 0 ? 11 : (p == 1 ? (F32 ? 11 : 5) : 10);
+        const uint32_t nbins = 1u << width;
+        const uint32_t digit_mask = nbins - 1u;
+        for (uint32_t b = tid; b < nbins; b += kClusterThreads) hist[b] = 0;
+        __syncthreads();
+#pragma unroll
+        for (int j = 0; j < CHUNKS; ++j)
+#pragma unroll
+            for (int e = 0; e < kVec; ++e) {
+                const uint32_t key = key_of(j, e);
+                if (e < lim[j] && (key & prefix_mask) == prefix)
+                    atomicAdd(&hist[(key >> shift) & digit_mask], 1u);
+            }
+        cluster.sync();  // every CTA's histogram is complete
+        const unsigned long long remaining = static_cast<unsigned long long>(k) - above;
+        const uint32_t per = (nbins + kClusterThreads - 1) / kClusterThreads;
+        uint32_t counts[4];
+        unsigned long long local = 0;
+#pragma unroll
+        for (uint32_t q = 0; q < 4; ++q) {
+            counts[q] = 0;
+            const uint32_t jj = tid * per + q;
+            if (q < per && jj < nbins) {
+                const uint32_t bin = nbins - 1 - jj;
+#pragma unroll
+                for (int c = 0; c < CPR; ++c) counts[q] += cluster.map_shared_rank(hist, c)[bin];
+                local += counts[q];
+            }
+        }
+        unsigned long long total;
+        unsigned long long run = cta_exclusive_scan<unsigned long long>(local, scan_sums, total);
+#pragma unroll
+        for (uint32_t q = 0; q < 4; ++q) {
+            const uint32_t jj = tid * per + q;
+            if (q < per && jj < nbins) {
+                if (run < remaining && run + counts[q] >= remaining) {
+                    sel_bin = nbins - 1 - jj;
+                    sel_above = run;
+                }
+                run += counts[q];
+            }
+        }
+        cluster.sync();  // remote reads done; sel_* visible
+        prefix |= sel_bin << shift;
+        prefix_mask |= digit_mask << shift;
+        above += sel_above;
+    }
+    const uint32_t threshold = prefix;
+    const unsigned long long need = static_cast<unsigned long long>(k) - above;
+
+    unsigned long long round_counts[CHUNKS];
+    unsigned long long mine = 0;
+#pragma unroll
+    for (int j = 0; j < CHUNKS; ++j) {
+        unsigned int gt = 0, eq = 0;
+#pragma unroll
+        for (int e = 0; e < kVec; ++e) {
+            const uint32_t key = key_of(j, e);
+            if (e < lim[j]) {
+                gt += key > threshold;
+                eq += key == threshold;
+            }
+        }
+        round_counts[j] = (static_cast<unsigned long long>(gt) << 32) | eq;
+        mine += round_counts[j];
+    }
+    unsigned long long cta_sum;
+    (void)cta_exclusive_scan<unsigned long long>(mine, scan_sums, cta_sum);
+    if (tid == 0) cta_totals = cta_sum;
+    cluster.sync();  // totals published
+    unsigned long long carry = 0;
+    for (int c = 0; c < rank; ++c) carry += *cluster.map_shared_rank(&cta_totals, c);
+    cluster.sync();  // nobody exits while a peer may still read its totals
+    unsigned long long gt_carry = carry >> 32, eq_carry = carry & 0xFFFFFFFFull;
+#pragma unroll
+    for (int j = 0; j < CHUNKS; ++j) {
+        unsigned long long total;
+        const unsigned long long excl = cta_exclusive_scan<unsigned long long>(round_counts[j], scan_sums, total);
+        unsigned long long gt_before = gt_carry + (excl >> 32);
+        unsigned long long eq_before = eq_carry + (excl & 0xFFFFFFFFull);
+        const int64_t base = slice0 + (static_cast<int64_t>(tid) + static_cast<int64_t>(kClusterThreads) * j) * kVec;
+#pragma unroll
+        for (int e = 0; e < kVec; ++e) {
+            if (e >= lim[j]) continue;
+            const uint32_t key = key_of(j, e);
+            if (key > threshold) {
+                dst[gt_before + min(eq_before, need)] = base + e;
+                ++gt_before;
+            } else if (key == threshold) {
+                if (eq_before < need) dst[gt_before + eq_before] = base + e;
+                ++eq_before;
+            }
+        }
+        gt_carry += total >> 32;
+        eq_carry += total & 0xFFFFFFFFull;
+    }
+}
+
+template <bool F32, int CPR, int CHUNKS>
+int launch_cluster(const void* scores, int64_t rows, int64_t tokens, int64_t row_stride, int64_t k,
+                   int64_t current_index, int64_t* out, int64_t out_stride, bool vec_ok,
+                   cudaStream_t stream) {
+    cudaLaunchConfig_t config = {};
+    config.gridDim = dim3(static_cast<unsigned>(rows * CPR), 1, 1);
+    config.blockDim = dim3(kClusterThreads, 1, 1);
+    config.dynamicSmemBytes = 0;
+    config.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = CPR;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    config.attrs = attr;
+    config.numAttrs = 1;
+    cudaError_t err = cudaLaunchKernelEx(&config, topk_cluster_kernel<F32, CPR, CHUNKS>, scores, tokens,
+                                         row_stride, k, current_index, out, out_stride, vec_ok);
+    if (err != cudaSuccess) return fail(POPKV_ERR_CUDA, "popkv_topk: %s", cudaGetErrorString(err));
+    return check_launch("popkv_topk");
+}
+
+// Picks the cluster size (CTAs per row) so that rows * CPR is about one wave
+// of the 148 SMs, then the smallest register footprint that holds the slice.
+template <bool F32>
+int try_launch_cluster(const void* scores, int64_t rows, int64_t tokens, int64_t row_stride,
+                       int64_t k, int64_t current_index, int64_t* out, int64_t out_stride,
+                       bool vec_ok, cudaStream_t stream) {
+    constexpr int64_t kVec = F32 ? 4 : 8;
+    int cpr = 1;
+    while (cpr < 8 && rows * cpr * 2 <= 160) cpr *= 2;
+    while (cpr < 8 && tokens > cpr * kClusterThreads * kVec * 4) cpr *= 2;
+    if (tokens > cpr * kClusterThreads * kVec * 4) return -1;
+    const int64_t per_cta = (tokens + cpr - 1) / cpr;
+    int chunks = 1;
+    while (per_cta > chunks * kClusterThreads * kVec) chunks *= 2;
+#define POPKV_CLUSTER(CPR_, CH_)                                                                   \
+    if (cpr == CPR_ && chunks == CH_)                                                              \
+        return launch_cluster<F32, CPR_, CH_>(scores, rows, tokens, row_stride, k, current_index, \
+                                              out, out_stride, vec_ok, stream);
+#define POPKV_CLUSTER_CPR(CPR_) POPKV_CLUSTER(CPR_, 1) POPKV_CLUSTER(CPR_, 2) POPKV_CLUSTER(CPR_, 4)
+    POPKV_CLUSTER_CPR(1)
+    POPKV_CLUSTER_CPR(2)
+    POPKV_CLUSTER_CPR(4)
+    POPKV_CLUSTER_CPR(8)
+#undef POPKV_CLUSTER_CPR
+#undef POPKV_CLUSTER
+    return -1;
+}
+
 template <bool F32>
 int launch_topk(const void* scores, int64_t rows, int64_t tokens, int64_t row_stride, int64_t k,
                 int64_t current_index, int64_t* out, int64_t out_stride, cudaStream_t stream) {
@@ -321,6 +579,11 @@ int launch_topk(const void* scores, int64_t rows, int64_t tokens, int64_t row_st
     const bool vec_ok = aligned(scores, 16) && (row_stride * static_cast<int64_t>(key_bytes)) % 16 == 0;
     const int64_t per_chunk = kTopkThreads * kVec;
     const unsigned grid = static_cast<unsigned>(rows);
+    if (rows <= 0x7FFFFFF && k > 0) {
+        const int st = try_launch_cluster<F32>(scores, rows, tokens, row_stride, k, current_index,
+                                               out, out_stride, vec_ok, stream);
+        if (st >= 0) return st;
+    }
 #define POPKV_TOPK_REG(C)                                                                      \
     if (tokens <= per_chunk * (C)) {                                                           \
         topk_reg_kernel<F32, C><<<grid, kTopkThreads, 0, stream>>>(                            \
@@ -335,8 +598,8 @@ int launch_topk(const void* scores, int64_t rows, int64_t tokens, int64_t row_st
     const size_t stage = static_cast<size_t>(tokens) * key_bytes;
     if (stage <= kStageBytes) {
         auto kernel = topk_kernel<F32, true>;
-        cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(kStageBytes));
+        const int st = allow_dynamic_smem(kernel, static_cast<int>(kStageBytes));
+        if (st != POPKV_OK) return st;
         kernel<<<grid, kTopkThreads, stage, stream>>>(scores, tokens, row_stride, k, current_index,
                                                       out, out_stride);
     } else {
