@@ -170,6 +170,26 @@ POPKV_API int popkv_attn_partial(const void* queries, int queries_dtype, int64_t
 POPKV_API int popkv_attn_merge(const float* partials, int64_t rows, int64_t splits, int64_t head_dim,
                      void* out, int out_dtype, void* stream);
 
+/*
+ * Split partials and their log-sum-exp merge in one call: the arguments of
+ * popkv_attn_partial plus `counters` (int32 [batch*q_heads], zero before the
+ * first call; every call leaves them zero again) and the merged output
+ * `out` [batch, q_heads, head_dim] of `out_dtype`.  For bf16 queries/K/V with
+ * head_dim 128, split_tokens <= 256 and at most 64 splits this is one launch
+ * (the last CTA of each row merges it); otherwise it runs popkv_attn_partial
+ * then popkv_attn_merge.  `partials` is scratch of popkv_attn_partial's size.
+ *
+ * Replaces sparse_kernels.indexed_attention_split (sparse_kernels.py:390-401).
+ */
+POPKV_API int popkv_attn_partial_merge(
+    const void* queries, int queries_dtype, int64_t batch, int64_t q_heads, int64_t head_dim,
+    const void* prefix_keys, const void* prefix_values, int kv_dtype, int64_t kv_heads,
+    int64_t prefix_tokens, int64_t k_batch_stride, int64_t k_head_stride, int64_t k_token_stride,
+    int64_t v_batch_stride, int64_t v_head_stride, int64_t v_token_stride,
+    const void* current_keys, const void* current_values, const int64_t* indices, int64_t selected,
+    const uint8_t* valid, const int64_t* head_to_kv, int64_t split_tokens, float* partials,
+    int32_t* counters, void* out, int out_dtype, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

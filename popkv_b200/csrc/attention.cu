@@ -238,12 +238,13 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_partial128_kernel(
 // per phase, which touches all 32 banks once: no conflicts.
 // ---------------------------------------------------------------------------
 constexpr int kPipeRowGroups = 32;  // 8 threads per row -> 32 row groups per CTA
-constexpr int kPipeRowsPerGroup = 2; // rows per row group per sub-chunk
-constexpr int kPipeRows = kPipeRowGroups * kPipeRowsPerGroup;  // 64 slots per sub-chunk
+constexpr int kPipeRowsPerGroup = 1; // rows per row group per sub-chunk
+constexpr int kPipeRows = kPipeRowGroups * kPipeRowsPerGroup;  // 32 slots per sub-chunk
 constexpr int kPipeStages = 3;       // ring depth (2 sub-chunks in flight while computing)
-constexpr int kPipeMaxSub = 4;       // sub-chunks per split (splits <= 256 slots)
+constexpr int kPipeMaxSub = 8;       // sub-chunks per split (splits <= 256 slots)
 constexpr int kRowBytes = 256;       // 128 x 16-bit
 constexpr float kLog2e = 1.4426950408889634f;
+constexpr int kMaxFusedSplits = 64;
 constexpr float kLn2 = 0.6931471805599453f;
 
 __device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
@@ -274,21 +275,32 @@ __device__ __forceinline__ void unpack_unit(const uint4& u, float* f) {
 //
 // Thread t owns row group r = t / 8 and 16-byte units c and c + 8 (dims
 // 8c..8c+7 and 64+8c..64+8c+7) of each row it handles.  The split is walked
-// in sub-chunks of 64 slots, two rows per row group; thread t cp.async-copies
+// in sub-chunks of 32 slots, one row per row group; thread t cp.async-copies
 // exactly the K and V units it will read into a kPipeStages-deep ring, so the
 // hand-off is a per-thread cp.async.wait_group with no block barrier.  Logits
 // are kept in the base-2 domain (scale * log2 e folded in) so each softmax
 // weight is one exp2; the running sum/accumulator are rescaled only when the
 // running maximum grows.  The partial's max is written back in natural units.
-template <typename QT, typename KT>
-__global__ void __launch_bounds__(kAttnThreads, 2) attn_partial_pipe_kernel(
+template <typename OT>
+__device__ __forceinline__ void store_out(OT* p, float v) {
+    if constexpr (std::is_same<OT, float>::value) *p = v;
+    else if constexpr (std::is_same<OT, __half>::value) *p = __float2half_rn(v);
+    else *p = __float2bfloat16_rn(v);
+}
+
+// When OT is not void the kernel also merges: the last CTA to finish a row
+// (counted with counters[row], which it resets to 0) combines the row's split
+// states, read back through L2, into out[row].
+template <typename QT, typename KT, typename OT>
+__global__ void __launch_bounds__(kAttnThreads, 4) attn_partial_pipe_kernel(
     const QT* __restrict__ queries, const KT* __restrict__ prefix_k, const KT* __restrict__ prefix_v,
     const KT* __restrict__ cur_k, const KT* __restrict__ cur_v, const int64_t* __restrict__ indices,
     const uint8_t* __restrict__ valid, const int64_t* __restrict__ head_to_kv,
     float* __restrict__ partials, int q_heads, int kv_heads, int64_t prefix_tokens,
     int64_t kbs, int64_t khs, int64_t kts, int64_t vbs, int64_t vhs, int64_t vts,
-    int64_t selected, int64_t split_tokens, int splits, float scale) {
-    extern __shared__ __align__(16) unsigned char ring[];  // [stage][K|V][64 rows][256 B]
+    int64_t selected, int64_t split_tokens, int splits, float scale, int* __restrict__ counters,
+    OT* __restrict__ merged) {
+    extern __shared__ __align__(16) unsigned char ring[];  // [stage][K|V][32 rows][256 B]
     __shared__ float s_m[kAttnThreads / 32], s_s[kAttnThreads / 32];
     __shared__ float s_acc[kAttnThreads / 32][8][16];
 
@@ -463,6 +475,36 @@ __global__ void __launch_bounds__(kAttnThreads, 2) attn_partial_pipe_kernel(
         out[0] = M == -INFINITY ? -INFINITY : M * kLn2;
         out[1] = total;
     }
+    if constexpr (!std::is_same<OT, void>::value) {
+        __shared__ int s_last;
+        __shared__ float s_w[kMaxFusedSplits];
+        __shared__ float s_den;
+        __threadfence();
+        __syncthreads();
+        if (tid == 0) s_last = atomicAdd(counters + row, 1) == splits - 1;
+        __syncthreads();
+        if (!s_last) return;
+        __threadfence();
+        const float* pr = partials + row * splits * (128 + 2);
+        if (tid == 0) {
+            float gm = -INFINITY;
+            for (int sp = 0; sp < splits; ++sp) gm = fmaxf(gm, __ldcg(pr + sp * 130));
+            float den = 0.0f;
+            for (int sp = 0; sp < splits; ++sp) {
+                const float w = expf(__ldcg(pr + sp * 130) - gm);
+                s_w[sp] = w;
+                den = __fmaf_rn(__ldcg(pr + sp * 130 + 1), w, den);
+            }
+            s_den = den;
+            counters[row] = 0;
+        }
+        __syncthreads();
+        if (tid < 128) {
+            float num = 0.0f;
+            for (int sp = 0; sp < splits; ++sp) num = __fmaf_rn(__ldcg(pr + sp * 130 + 2 + tid), s_w[sp], num);
+            store_out(merged + row * 128 + tid, num / s_den);
+        }
+    }
 }
 
 // Generic head dims: one warp per (row, split), serial over slots.
@@ -604,13 +646,14 @@ int launch_partial(const void* queries, int64_t batch, int64_t q_heads, int64_t 
                         (vts * es) % 16 == 0;
     if (vec_ok && sizeof(KT) == 2 && split_tokens <= kPipeRows * kPipeMaxSub) {
         constexpr size_t ring_bytes = static_cast<size_t>(kPipeStages) * 2 * kPipeRows * kRowBytes;
-        const int st = allow_dynamic_smem(attn_partial_pipe_kernel<QT, KT>, static_cast<int>(ring_bytes));
+        const int st = allow_dynamic_smem(attn_partial_pipe_kernel<QT, KT, void>, static_cast<int>(ring_bytes));
         if (st != POPKV_OK) return st;
-        attn_partial_pipe_kernel<QT, KT><<<grid, kAttnThreads, ring_bytes, stream>>>(
+        attn_partial_pipe_kernel<QT, KT, void><<<grid, kAttnThreads, ring_bytes, stream>>>(
             static_cast<const QT*>(queries), static_cast<const KT*>(pk), static_cast<const KT*>(pv),
             static_cast<const KT*>(ck), static_cast<const KT*>(cv), indices, valid, head_to_kv,
             partials, static_cast<int>(q_heads), static_cast<int>(kv_heads), prefix_tokens, kbs,
-            khs, kts, vbs, vhs, vts, selected, split_tokens, static_cast<int>(splits), scale);
+            khs, kts, vbs, vhs, vts, selected, split_tokens, static_cast<int>(splits), scale,
+            nullptr, nullptr);
     } else if (vec_ok) {
         attn_partial128_kernel<QT, KT><<<grid, kAttnThreads, 0, stream>>>(
             static_cast<const QT*>(queries), static_cast<const KT*>(pk), static_cast<const KT*>(pv),
@@ -626,6 +669,41 @@ int launch_partial(const void* queries, int64_t batch, int64_t q_heads, int64_t 
             split_tokens, static_cast<int>(splits), scale);
     }
     return check_launch("popkv_attn_partial");
+}
+
+// Partials + merge in one launch when the pipelined kernel applies; otherwise
+// the two-launch path.  Returns POPKV_ERR_UNSUPPORTED (without launching) when
+// the single-launch form does not apply, so the caller can fall back.
+template <typename QT, typename KT, typename OT>
+int launch_partial_merged(const void* queries, int64_t batch, int64_t q_heads, int64_t head_dim,
+                          const void* pk, const void* pv, int64_t kv_heads, int64_t prefix_tokens,
+                          int64_t kbs, int64_t khs, int64_t kts, int64_t vbs, int64_t vhs,
+                          int64_t vts, const void* ck, const void* cv, const int64_t* indices,
+                          int64_t selected, const uint8_t* valid, const int64_t* head_to_kv,
+                          int64_t split_tokens, float* partials, int* counters, void* out,
+                          cudaStream_t stream) {
+    const int64_t splits = (selected + split_tokens - 1) / split_tokens;
+    const size_t es = sizeof(KT);
+    const bool ok = sizeof(KT) == 2 && head_dim == 128 && split_tokens <= kPipeRows * kPipeMaxSub &&
+                    splits <= kMaxFusedSplits && aligned(pk, 16) && aligned(pv, 16) &&
+                    aligned(ck, 16) && aligned(cv, 16) && (kbs * es) % 16 == 0 &&
+                    (khs * es) % 16 == 0 && (kts * es) % 16 == 0 && (vbs * es) % 16 == 0 &&
+                    (vhs * es) % 16 == 0 && (vts * es) % 16 == 0;
+    if (!ok) return POPKV_ERR_UNSUPPORTED;
+    if constexpr (sizeof(KT) == 2) {
+        dim3 grid(static_cast<unsigned>(splits), static_cast<unsigned>(batch * q_heads));
+        constexpr size_t ring_bytes = static_cast<size_t>(kPipeStages) * 2 * kPipeRows * kRowBytes;
+        const int st = allow_dynamic_smem(attn_partial_pipe_kernel<QT, KT, OT>, static_cast<int>(ring_bytes));
+        if (st != POPKV_OK) return st;
+        attn_partial_pipe_kernel<QT, KT, OT><<<grid, kAttnThreads, ring_bytes, stream>>>(
+            static_cast<const QT*>(queries), static_cast<const KT*>(pk), static_cast<const KT*>(pv),
+            static_cast<const KT*>(ck), static_cast<const KT*>(cv), indices, valid, head_to_kv,
+            partials, static_cast<int>(q_heads), static_cast<int>(kv_heads), prefix_tokens, kbs,
+            khs, kts, vbs, vhs, vts, selected, split_tokens, static_cast<int>(splits),
+            score_scale_for(head_dim), counters, static_cast<OT*>(out));
+        return check_launch("popkv_attn_partial_merge");
+    }
+    return POPKV_ERR_UNSUPPORTED;
 }
 
 template <typename QT>
@@ -729,4 +807,47 @@ extern "C" int popkv_attn_merge(const float* partials, int64_t rows, int64_t spl
         attn_merge_kernel<__nv_bfloat16><<<static_cast<unsigned>(rows), threads, 0, s>>>(
             partials, splits, d, static_cast<__nv_bfloat16*>(out));
     return check_launch("popkv_attn_merge");
+}
+
+extern "C" int popkv_attn_partial_merge(
+    const void* queries, int queries_dtype, int64_t batch, int64_t q_heads, int64_t head_dim,
+    const void* prefix_keys, const void* prefix_values, int kv_dtype, int64_t kv_heads,
+    int64_t prefix_tokens, int64_t k_batch_stride, int64_t k_head_stride, int64_t k_token_stride,
+    int64_t v_batch_stride, int64_t v_head_stride, int64_t v_token_stride,
+    const void* current_keys, const void* current_values, const int64_t* indices, int64_t selected,
+    const uint8_t* valid, const int64_t* head_to_kv, int64_t split_tokens, float* partials,
+    int32_t* counters, void* out, int out_dtype, void* stream) {
+    using namespace popkv;
+    if (!valid_dtype(out_dtype))
+        return fail(POPKV_ERR_INVALID, "popkv_attn_partial_merge: output must be fp32/fp16/bf16");
+    if (!counters || !out) return fail(POPKV_ERR_INVALID, "popkv_attn_partial_merge: null pointer");
+    if (queries_dtype == POPKV_DTYPE_BF16 && kv_dtype == POPKV_DTYPE_BF16 && batch > 0 &&
+        q_heads > 0 && q_heads * batch <= 65535 && prefix_tokens > 0 && prefix_tokens < 0x7FFFFFFFll &&
+        selected > 0 && split_tokens > 0 && split_tokens % 16 == 0 && queries && prefix_keys &&
+        prefix_values && current_keys && current_values && indices && head_to_kv && partials) {
+        cudaStream_t s = static_cast<cudaStream_t>(stream);
+        int st = POPKV_ERR_UNSUPPORTED;
+        if (out_dtype == POPKV_DTYPE_BF16)
+            st = launch_partial_merged<__nv_bfloat16, __nv_bfloat16, __nv_bfloat16>(
+                queries, batch, q_heads, head_dim, prefix_keys, prefix_values, kv_heads, prefix_tokens,
+                k_batch_stride, k_head_stride, k_token_stride, v_batch_stride, v_head_stride,
+                v_token_stride, current_keys, current_values, indices, selected, valid, head_to_kv,
+                split_tokens, partials, counters, out, s);
+        else if (out_dtype == POPKV_DTYPE_F32)
+            st = launch_partial_merged<__nv_bfloat16, __nv_bfloat16, float>(
+                queries, batch, q_heads, head_dim, prefix_keys, prefix_values, kv_heads, prefix_tokens,
+                k_batch_stride, k_head_stride, k_token_stride, v_batch_stride, v_head_stride,
+                v_token_stride, current_keys, current_values, indices, selected, valid, head_to_kv,
+                split_tokens, partials, counters, out, s);
+        if (st != POPKV_ERR_UNSUPPORTED) return st;
+    }
+    // General case: two launches.
+    int st = popkv_attn_partial(queries, queries_dtype, batch, q_heads, head_dim, prefix_keys,
+                                prefix_values, kv_dtype, kv_heads, prefix_tokens, k_batch_stride,
+                                k_head_stride, k_token_stride, v_batch_stride, v_head_stride,
+                                v_token_stride, current_keys, current_values, indices, selected,
+                                valid, head_to_kv, split_tokens, partials, stream);
+    if (st != POPKV_OK) return st;
+    return popkv_attn_merge(partials, batch * q_heads, (selected + split_tokens - 1) / split_tokens,
+                            head_dim, out, out_dtype, stream);
 }

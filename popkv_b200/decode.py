@@ -4,8 +4,9 @@ The reference runs each decode stage as a separate eager launch with Python
 integers for the token count (popkv.py:1076-1115), so its host overhead is
 part of every token.  ``SparseAttentionStep`` owns static input/output buffers
 and preallocated intermediates, calls the C-ABI kernels directly, and captures
-the four launches (popcount score with the query encoding in its prologue,
-top-k + current slot, split partials, merge) into one CUDA graph.  Replaying the graph costs one launch.
+the three launches (popcount score with the query encoding in its prologue,
+top-k + current slot, split partials with the merge done by the last CTA of
+each row) into one CUDA graph.  Replaying the graph costs one launch.
 
 The graph is specific to the cache length it was captured at.  Call
 ``recapture()`` after appending tokens (or use ``run_eager``).
@@ -77,6 +78,7 @@ class SparseAttentionStep:
         self.scores = torch.zeros((B, QH, self.prefix_tokens), device=dev, dtype=torch.float16)
         self.indices = torch.zeros((B, QH, self.selected), device=dev, dtype=torch.int64)
         self.partials = torch.zeros((B, QH, self.splits, D + 2), device=dev, dtype=torch.float32)
+        self.counters = torch.zeros((B * QH,), device=dev, dtype=torch.int32)  # self-resetting
         self.graph = None
         self.use_graph = use_graph
         if use_graph:
@@ -97,17 +99,17 @@ class SparseAttentionStep:
                              self.prefix_tokens, self.k, self.prefix_tokens, ptr(self.indices),
                              self.selected, s))
         pk, pv = self.prefix_keys, self.prefix_values
-        check(lib.popkv_attn_partial(
+        # Partials and their merge in one launch (the last CTA of each row merges).
+        check(lib.popkv_attn_partial_merge(
             ptr(self.queries), _lib.dtype_code(self.queries), B, QH, 128, ptr(pk), ptr(pv),
             _lib.dtype_code(pk), KVH, self.prefix_tokens, pk.stride(0), pk.stride(1), pk.stride(2),
             pv.stride(0), pv.stride(1), pv.stride(2), ptr(self.current_keys),
             ptr(self.current_values), ptr(self.indices), self.selected, None, ptr(self.head_to_kv),
-            self.split_tokens, ptr(self.partials), s))
-        check(lib.popkv_attn_merge(ptr(self.partials), B * QH, self.splits, 128, ptr(self.output),
-                                   _lib.dtype_code(self.output), s))
+            self.split_tokens, ptr(self.partials), ptr(self.counters), ptr(self.output),
+            _lib.dtype_code(self.output), s))
 
     def recapture(self) -> None:
-        """(Re)build the CUDA graph of the four launches for the current buffers."""
+        """(Re)build the CUDA graph of the three launches for the current buffers."""
         with torch.cuda.device(self.device):
             side = torch.cuda.Stream(self.device)
             side.wait_stream(torch.cuda.current_stream(self.device))

@@ -359,3 +359,29 @@ def test_attention_rejects_bad_arguments(cuda_device):
     with pytest.raises(ValueError, match="valid mask"):
         S.indexed_attention_split_partial(*args[:6], args[6], torch.ones(3, 3, dtype=torch.bool,
                                                                             device=cuda_device))
+
+
+@pytest.mark.parametrize("valid", (False, True))
+def test_partial_merge_single_launch_matches_two_launches(cuda_device, valid):
+    """popkv_attn_partial_merge (last CTA merges) == popkv_attn_partial + popkv_attn_merge."""
+    from popkv_b200 import _lib
+    args = _attn_inputs(cuda_device, valid=valid, seed=77, selected=1000)
+    q, keys, values, ck, cv, idx, mapping, mask = args
+    partials = S.indexed_attention_split_partial(*args[:6], mapping, mask)
+    want = S.indexed_attention_split_merge(partials, q)
+    out = torch.empty_like(q)
+    scratch = torch.empty_like(partials)
+    counters = torch.zeros(q.shape[0], dtype=torch.int32, device=cuda_device)
+    idx = idx.contiguous()
+    m = None if mask is None else mask.to(torch.uint8).contiguous()
+    for _ in range(2):  # the counters reset themselves
+        _lib.check(_lib.lib().popkv_attn_partial_merge(
+            _lib.ptr(q), _lib.BF16, 1, q.shape[0], 128, _lib.ptr(keys), _lib.ptr(values), _lib.BF16,
+            keys.shape[0], keys.shape[1], 0, keys.stride(0), keys.stride(1), 0, values.stride(0),
+            values.stride(1), _lib.ptr(ck), _lib.ptr(cv), _lib.ptr(idx), idx.shape[1], _lib.ptr(m),
+            _lib.ptr(mapping), 256, _lib.ptr(scratch), _lib.ptr(counters), _lib.ptr(out), _lib.BF16,
+            _lib.stream_of(cuda_device)))
+        torch.cuda.synchronize()
+        assert int(counters.abs().sum()) == 0
+        torch.testing.assert_close(out.float(), want.float(), atol=1e-2, rtol=0)
+        assert (out.float() - want.float()).abs().max().item() <= 2 ** -7
