@@ -190,6 +190,35 @@ POPKV_API int popkv_attn_partial_merge(
     const uint8_t* valid, const int64_t* head_to_kv, int64_t split_tokens, float* partials,
     int32_t* counters, void* out, int out_dtype, void* stream);
 
+/*
+ * Fused decode-time retrieval for head_dim 128: popcount score of the first
+ * `tokens` cached keys, per-head top-(budget-1) with the current slot
+ * reserved, sparse attention over the selected rows plus the current token,
+ * and the merge -- one launch, no global intermediates.
+ *
+ * queries [batch, q_heads, 128] and K/V share one dtype (bf16 or fp16); the
+ * packed planes are laid out as for popkv_score_encoded with batch entry b at
+ * row offset b*plane_batch_stride; prefix/current K/V as for
+ * popkv_attn_partial; q_heads/kv_heads in {1, 2, 4}; tokens <= 131072.
+ * out [batch, q_heads, 128] (queries' dtype).  Optional outputs (NULL to skip):
+ * scores_out fp16 [batch, q_heads, tokens] (identical to popkv_score) and
+ * indices_out int64 [batch, q_heads, k + 1], k = min(budget - 1, tokens)
+ * (identical to popkv_topk with current_index = tokens).
+ *
+ * Replaces the PopKV branch of LlamaSparseDecoder.decode (popkv.py:1076-1115):
+ * query_encode + score_encoded + torch.topk + _append_current +
+ * indexed_attention_split_partial + indexed_attention_split_merge.
+ */
+POPKV_API int popkv_retrieve(
+    const void* queries, int queries_dtype, int64_t batch, int64_t q_heads, int64_t head_dim,
+    const int32_t* k_sign, const int32_t* k_mag, const uint16_t* k_low, const uint16_t* k_delta,
+    int64_t kv_heads, int64_t capacity, int64_t plane_batch_stride, int64_t tokens,
+    int64_t dim_group_size, const int64_t* head_to_kv, const void* prefix_keys,
+    const void* prefix_values, int kv_dtype, int64_t k_batch_stride, int64_t k_head_stride,
+    int64_t k_token_stride, int64_t v_batch_stride, int64_t v_head_stride, int64_t v_token_stride,
+    const void* current_keys, const void* current_values, int64_t budget, void* out,
+    uint16_t* scores_out, int64_t* indices_out, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

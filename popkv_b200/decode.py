@@ -36,7 +36,7 @@ class SparseAttentionStep:
     def __init__(self, cache: PopKVCache, prefix_keys: torch.Tensor, prefix_values: torch.Tensor,
                  head_to_kv: torch.Tensor, *, budget: int, q_heads: int | None = None,
                  q_dtype: torch.dtype = torch.bfloat16, split_tokens: int = 256,
-                 batch: int = 1, use_graph: bool = True) -> None:
+                 batch: int = 1, use_graph: bool = True, fused: bool = True) -> None:
         if prefix_keys.ndim == 3:
             prefix_keys, prefix_values = prefix_keys[None], prefix_values[None]
         if prefix_keys.stride(-1) != 1 or prefix_values.stride(-1) != 1:
@@ -81,6 +81,9 @@ class SparseAttentionStep:
         self.counters = torch.zeros((B * QH,), device=dev, dtype=torch.int32)  # self-resetting
         self.graph = None
         self.use_graph = use_graph
+        # fused=True: one popkv_retrieve launch (score, select, attention, merge in
+        # one thread-block cluster per KV head); fused=False: the three-launch chain.
+        self.fused = fused and batch == 1 and self.q_heads // self.kv_heads in (1, 2, 4)
         if use_graph:
             self.recapture()
 
@@ -91,6 +94,16 @@ class SparseAttentionStep:
         B, QH, KVH = self.batch, self.q_heads, self.kv_heads
         packed = self.cache.packed
         capacity = int(packed[0].shape[1])
+        pk, pv = self.prefix_keys, self.prefix_values
+        if self.fused:
+            check(lib.popkv_retrieve(
+                ptr(self.queries), _lib.dtype_code(self.queries), B, QH, 128,
+                *(ptr(t) for t in packed), KVH, capacity, KVH * capacity, self.prefix_tokens, self.g,
+                ptr(self.head_to_kv), ptr(pk), ptr(pv), _lib.dtype_code(pk), pk.stride(0),
+                pk.stride(1), pk.stride(2), pv.stride(0), pv.stride(1), pv.stride(2),
+                ptr(self.current_keys), ptr(self.current_values), self.budget, ptr(self.output),
+                None, ptr(self.indices), s))
+            return
         # Query encoding runs in the score kernel's prologue (one launch fewer).
         check(lib.popkv_score(ptr(self.queries), _lib.dtype_code(self.queries), B, QH, 128,
                               *(ptr(t) for t in packed), KVH, capacity, ptr(self.head_to_kv),
@@ -98,7 +111,6 @@ class SparseAttentionStep:
         check(lib.popkv_topk(ptr(self.scores), _lib.F16, B * QH, self.prefix_tokens,
                              self.prefix_tokens, self.k, self.prefix_tokens, ptr(self.indices),
                              self.selected, s))
-        pk, pv = self.prefix_keys, self.prefix_values
         # Partials and their merge in one launch (the last CTA of each row merges).
         check(lib.popkv_attn_partial_merge(
             ptr(self.queries), _lib.dtype_code(self.queries), B, QH, 128, ptr(pk), ptr(pv),

@@ -13,7 +13,7 @@ from dataclasses import dataclass
 
 import torch
 
-from . import popkv_cuda, sparse_kernels
+from . import _lib, popkv_cuda, sparse_kernels
 
 METHODS = ("popkv-normal", "popkv-q", "popkv-s")
 POPKV_PRESETS = {
@@ -169,3 +169,66 @@ def popkv_attention(
         None, split_tokens=split_tokens,
     )
     return sparse_kernels.indexed_attention_split_merge(partials, queries)
+
+
+def popkv_retrieve(
+    queries: torch.Tensor, packed, prefix_keys: torch.Tensor, prefix_values: torch.Tensor,
+    current_keys: torch.Tensor, current_values: torch.Tensor, head_to_kv: torch.Tensor, *,
+    tokens: int, budget: int, dim_group_size: int, out: torch.Tensor | None = None,
+    return_scores: bool = False, return_indices: bool = False,
+):
+    """The whole PopKV decode branch (popkv.py:1076-1115) in one fused launch.
+
+    queries [B, QH, 128]; packed planes [KVH, cap, *] (B == 1) or
+    [B, KVH, cap, *]; prefix K/V [B, KVH, T, 128] or [KVH, T, 128] (strided
+    views allowed); current K/V [B, KVH, 128] or [KVH, 128].  Scores the first
+    ``tokens`` cached keys, keeps the top ``min(budget - 1, tokens)`` per query
+    head plus the current slot, and returns the attention output [B, QH, 128]
+    -- the same selection as score -> topk -> split attention.  With
+    ``return_scores`` / ``return_indices`` also returns the fp16 scores and the
+    int64 selected indices (last column = current slot).
+    """
+    if queries.ndim != 3 or not queries.is_cuda:
+        raise ValueError("queries must be CUDA [batch, query heads, head dim]")
+    batch, q_heads, head_dim = (int(x) for x in queries.shape)
+    if prefix_keys.ndim == 3:
+        prefix_keys, prefix_values = prefix_keys[None], prefix_values[None]
+    if current_keys.ndim == 2:
+        current_keys, current_values = current_keys[None], current_values[None]
+    packed = tuple(packed)
+    if len(packed) != 4:
+        raise ValueError("packed must contain k_sign, k_mag, k_low, k_delta")
+    if packed[0].ndim == 3:
+        if batch != 1:
+            raise ValueError("batched retrieval needs planes stacked as [batch, KV heads, capacity, *]")
+        kv_heads, capacity = int(packed[0].shape[0]), int(packed[0].shape[1])
+        plane_batch_stride = kv_heads * capacity
+    else:
+        kv_heads, capacity = int(packed[0].shape[1]), int(packed[0].shape[2])
+        plane_batch_stride = kv_heads * capacity
+    for t in packed:
+        if not t.is_contiguous():
+            raise ValueError("packed planes must be contiguous")
+    queries = queries.contiguous()
+    current_keys = current_keys.to(prefix_keys.dtype).contiguous()
+    current_values = current_values.to(prefix_keys.dtype).contiguous()
+    mapping = head_to_kv.to(device=queries.device, dtype=torch.int64).contiguous()
+    if out is None:
+        out = torch.empty_like(queries)
+    k = min(int(budget) - 1, int(tokens))
+    scores = (torch.empty((batch, q_heads, int(tokens)), device=queries.device, dtype=torch.float16)
+              if return_scores else None)
+    indices = (torch.empty((batch, q_heads, k + 1), device=queries.device, dtype=torch.int64)
+               if return_indices else None)
+    with torch.cuda.device(queries.device):
+        _lib.check(_lib.lib().popkv_retrieve(
+            _lib.ptr(queries), _lib.dtype_code(queries), batch, q_heads, head_dim,
+            *(_lib.ptr(t) for t in packed), kv_heads, capacity, plane_batch_stride, int(tokens),
+            int(dim_group_size), _lib.ptr(mapping), _lib.ptr(prefix_keys), _lib.ptr(prefix_values),
+            _lib.dtype_code(prefix_keys), prefix_keys.stride(0), prefix_keys.stride(1),
+            prefix_keys.stride(2), prefix_values.stride(0), prefix_values.stride(1),
+            prefix_values.stride(2), _lib.ptr(current_keys), _lib.ptr(current_values), int(budget),
+            _lib.ptr(out), _lib.ptr(scores), _lib.ptr(indices), _lib.stream_of(queries.device)))
+    if return_scores or return_indices:
+        return out, scores, indices
+    return out

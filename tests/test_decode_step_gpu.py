@@ -46,3 +46,56 @@ def test_graph_step_matches_oracle(cuda_device, preset, context, budget):
                             head_to_kv(32, 8))
     err = np.abs(out[0].float().cpu().numpy() - want)
     assert err.max() <= 2e-2 and err.mean() <= 2e-3
+
+
+@pytest.mark.parametrize("preset,context,budget", [("popkv-q", 32768, 4096), ("popkv-s", 5000, 512),
+                                                   ("popkv-normal", 1000, 2000), ("popkv-q", 300, 64)])
+def test_fused_retrieve_matches_unfused_and_oracle(cuda_device, preset, context, budget):
+    """popkv_retrieve == score -> topk -> split attention (scores and indices bit-exact)."""
+    tg, g = P.POPKV_PRESETS[preset]
+    x = decode_inputs(context=context, seed=5, dtype="bf16")
+    dev = cuda_device
+    to = lambda a: torch.from_numpy(a).to(torch.bfloat16).to(dev)  # noqa: E731
+    keys, values = to(x.keys[0]), to(x.values[0])
+    cache = P.build_popkv_cache(keys, group_size=tg, dim_group_size=g, reserve_tokens=8)
+    mapping = torch.from_numpy(head_to_kv(32, 8)).to(dev)
+    q = to(x.queries)
+    ck, cv = to(x.current_keys[0]), to(x.current_values[0])
+    out, scores, indices = P.popkv_retrieve(q, cache.packed, keys, values, ck, cv, mapping,
+                                            tokens=context, budget=budget, dim_group_size=g,
+                                            return_scores=True, return_indices=True)
+    from popkv_b200 import popkv_cuda as C
+    want_scores = C.score(q, cache.packed, head_to_kv=mapping, tokens=context, dim_group_size=g)
+    assert torch.equal(scores, want_scores)
+    want_idx = P.select_tokens(want_scores, budget=budget, prefix_tokens=context)
+    assert torch.equal(indices, want_idx)
+    eager = P.popkv_attention(q[0], keys, values, ck, cv, cache, mapping, budget=budget)
+    err = (out[0].float() - eager.float()).abs()
+    assert err.max().item() <= 2 ** -6
+    kbits, qbits = x.bits("keys")[0], x.bits("queries")
+    opk = oracle.pack(kbits, "bf16", token_group_size=tg, dim_group_size=g)
+    enc = oracle.query_encode(qbits, "bf16", dim_group_size=g)
+    _, s16 = oracle.score(enc, opk, head_to_kv=head_to_kv(32, 8), tokens=context,
+                          dim_group_size=g, head_dim=128)
+    idx = oracle.select_with_current(s16, budget, context)[0]
+    np.testing.assert_array_equal(indices[0].cpu().numpy(), idx)
+    want = oracle.attention(qbits[0], "bf16", kbits, x.bits("values")[0], "bf16",
+                            x.bits("current_keys")[0], x.bits("current_values")[0], idx,
+                            head_to_kv(32, 8))
+    e = np.abs(out[0].float().cpu().numpy() - want)
+    assert e.max() <= 2e-2 and e.mean() <= 2e-3
+
+
+def test_fused_retrieve_zero_context(cuda_device):
+    """With no cached token the output is the current value (the only slot)."""
+    dev = cuda_device
+    keys = torch.zeros(8, 0, 128, dtype=torch.bfloat16, device=dev)
+    cache_keys = torch.randn(8, 64, 128, device=dev).to(torch.bfloat16)
+    cache = P.build_popkv_cache(cache_keys, group_size=64, dim_group_size=64, reserve_tokens=0)
+    q = torch.randn(1, 32, 128, device=dev).to(torch.bfloat16)
+    ck = torch.randn(8, 128, device=dev).to(torch.bfloat16)
+    cv = torch.randn(8, 128, device=dev).to(torch.bfloat16)
+    mapping = torch.from_numpy(head_to_kv(32, 8)).to(dev)
+    out = P.popkv_retrieve(q, cache.packed, cache_keys, cache_keys, ck, cv, mapping, tokens=0,
+                           budget=16, dim_group_size=64)
+    torch.testing.assert_close(out[0].float(), cv[mapping].float(), atol=0, rtol=0)
