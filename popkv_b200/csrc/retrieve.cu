@@ -37,6 +37,24 @@
 #include "common.cuh"
 #include "score_impl.cuh"
 
+// Phase timestamps for profiling builds (-DPOPKV_RETRIEVE_TIMING): thread 0 of
+// each CTA records %globaltimer at the phase boundaries into g_retrieve_phase_ns.
+#ifdef POPKV_RETRIEVE_TIMING
+__device__ unsigned long long g_retrieve_phase_ns[2048][8];
+#define POPKV_PHASE(i)                                                                  \
+    do {                                                                                \
+        if (threadIdx.x == 0 && blockIdx.x < 2048) {                                    \
+            unsigned long long t_;                                                      \
+            asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_));                     \
+            g_retrieve_phase_ns[blockIdx.x][i] = t_;                                    \
+        }                                                                               \
+    } while (0)
+#else
+#define POPKV_PHASE(i) \
+    do {               \
+    } while (0)
+#endif
+
 namespace popkv {
 namespace {
 
@@ -181,6 +199,9 @@ __global__ void __launch_bounds__(kRetThreads, 1) retrieve_kernel(const Retrieve
     __shared__ float part_acc[QPG][128];
     __shared__ int s_nu;
     __shared__ float s_w[16], s_den;
+    __shared__ uint32_t loc_b1[QPG], loc_thr[QPG];
+    __shared__ unsigned long long loc_need[QPG], loc_cgt[QPG], loc_ceq[QPG];
+    __shared__ float s_part_s[16];
 
     cg::cluster_group cluster = cg::this_cluster();
     const int C = static_cast<int>(cluster.num_blocks());
@@ -203,6 +224,7 @@ __global__ void __launch_bounds__(kRetThreads, 1) retrieve_kernel(const Retrieve
     unsigned char* ring = smem + lay.region;                               // aliases hist1
     float* red = reinterpret_cast<float*>(smem + lay.region);              // aliases both
 
+    POPKV_PHASE(0);
     // ---- A: zero the histograms, encode the queries ----------------------------
     for (int i = tid; i < QPG * kHist1Bins; i += kRetThreads) hist1[i] = 0;
     for (int i = tid; i < QPG * kHist2Bins; i += kRetThreads) (&hist2[0][0])[i] = 0;
@@ -215,6 +237,7 @@ __global__ void __launch_bounds__(kRetThreads, 1) retrieve_kernel(const Retrieve
     if (tid < QPG) finish_state<G>(states[tid]);
     cluster.sync();  // histograms zeroed cluster-wide before any remote add; states visible
 
+    POPKV_PHASE(1);
     // ---- B: score the slice ---------------------------------------------------
     {
         constexpr int R = 128 / G;
@@ -250,50 +273,78 @@ __global__ void __launch_bounds__(kRetThreads, 1) retrieve_kernel(const Retrieve
     }
     __syncthreads();
 
+    POPKV_PHASE(2);
     // ---- C: radix select across the cluster -------------------------------------
+    // Pass 1 (key bits 15..5), pull-based: the QPG*2048 histogram positions are
+    // split into C equal segments, segment q (one head, a run of bins in
+    // descending key order) being reduced by CTA q from all C CTAs' histograms
+    // through DSMEM.  The CTA whose segment holds the k-th largest key of its
+    // head finds the digit and stores it into the leader CTA.
     const int64_t k = a.k;
+    const int seg_len = QPG * kHist1Bins / C;         // positions per segment
+    const int segs_per_head = kHist1Bins / seg_len;   // = C / QPG
+    const int my_head = rank / segs_per_head;
+    const int my_seg = rank % segs_per_head;
     if (k > 0) {
-        uint32_t* leader_hist1 = cluster.map_shared_rank(hist1, 0);
-        if (rank != 0) {
-            for (int i = tid; i < QPG * kHist1Bins; i += kRetThreads) {
-                const uint32_t c = hist1[i];
-                if (c) atomicAdd(leader_hist1 + i, c);
+        cluster.sync();  // all local histograms complete
+        // This thread's positions of segment `rank`: p = my_seg*seg_len + j, bin = 2047 - p.
+        constexpr int kMaxPer = (4 * kHist1Bins / 8 + kRetThreads - 1) / kRetThreads;  // QPG<=4, C>=8
+        uint32_t cnt[kMaxPer];
+        unsigned long long local = 0;
+#pragma unroll
+        for (int q = 0; q < kMaxPer; ++q) {
+            cnt[q] = 0;
+            const int j = tid * kMaxPer + q;
+            if (j < seg_len) {
+                const int bin = kHist1Bins - 1 - (my_seg * seg_len + j);
+                const uint32_t* src = hist1 + my_head * kHist1Bins + bin;
+                uint32_t v[16];
+#pragma unroll
+                for (int r = 0; r < 16; ++r) v[r] = r < C ? *cluster.map_shared_rank(src, r) : 0u;
+#pragma unroll
+                for (int r = 0; r < 16; ++r) cnt[q] += v[r];
+                local += cnt[q];
             }
         }
-        cluster.sync();
-        if (rank == 0) {
-            // Per head: descending scan over the 2048 bins (4 per thread).
-            for (int h = 0; h < QPG; ++h) {
-                uint32_t cnt[4];
-                unsigned long long local = 0;
+        unsigned long long seg_total;
+        unsigned long long run = ret_exclusive_scan<unsigned long long>(local, scan_a, seg_total);
+        if (tid == 0) cta_gt[0] = seg_total;  // published segment total (reuses cta_gt[0])
+        cluster.sync();  // segment totals visible
+        if (tid < 32) {
+            // carry = totals of the segments before mine (same head), one lane per segment.
+            unsigned long long t = 0;
+            if (tid < my_seg) t = *cluster.map_shared_rank(&cta_gt[0], my_head * segs_per_head + tid);
 #pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    cnt[q] = hist1[h * kHist1Bins + (kHist1Bins - 1 - (tid * 4 + q))];
-                    local += cnt[q];
-                }
-                unsigned long long total;
-                unsigned long long run = ret_exclusive_scan<unsigned long long>(local, scan_a, total);
-                const unsigned long long remaining = static_cast<unsigned long long>(k);
+            for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xFFFFFFFFu, t, o);
+            if (tid == 0) cta_eq[0] = t;
+        }
+        __syncthreads();
+        const unsigned long long carry = cta_eq[0];
+        run += carry;
 #pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    if (run < remaining && run + cnt[q] >= remaining) {
-                        sel_b1[h] = kHist1Bins - 1 - (tid * 4 + q);
-                        sel_above1[h] = run;
-                    }
-                    run += cnt[q];
+        for (int q = 0; q < kMaxPer; ++q) {
+            const int j = tid * kMaxPer + q;
+            if (j < seg_len) {
+                if (run < static_cast<unsigned long long>(k) && run + cnt[q] >= static_cast<unsigned long long>(k)) {
+                    *cluster.map_shared_rank(&sel_b1[my_head], 0) = kHist1Bins - 1 - (my_seg * seg_len + j);
+                    *cluster.map_shared_rank(&sel_above1[my_head], 0) = run;
                 }
+                run += cnt[q];
             }
         }
-        cluster.sync();
-        uint32_t b1[QPG];
-#pragma unroll
-        for (int h = 0; h < QPG; ++h) b1[h] = *cluster.map_shared_rank(&sel_b1[h], 0);
+        cluster.sync();  // the leader holds every head's digit
+        if (tid < QPG) {
+            loc_b1[tid] = *cluster.map_shared_rank(&sel_b1[tid], 0);
+        }
+        __syncthreads();
+        // Pass 2 (key bits 4..0): the few keys inside the chosen digit, counted
+        // into the leader's 32-bin histograms.
         uint32_t* leader_hist2 = cluster.map_shared_rank(&hist2[0][0], 0);
         for (int i = tid; i < n_local; i += kRetThreads) {
 #pragma unroll
             for (int h = 0; h < QPG; ++h) {
                 const uint32_t key = score_key(scores16[h * a.slice + i]);
-                if ((key >> 5) == b1[h]) atomicAdd(leader_hist2 + h * kHist2Bins + (key & 31u), 1u);
+                if ((key >> 5) == loc_b1[h]) atomicAdd(leader_hist2 + h * kHist2Bins + (key & 31u), 1u);
             }
         }
         cluster.sync();
@@ -301,34 +352,38 @@ __global__ void __launch_bounds__(kRetThreads, 1) retrieve_kernel(const Retrieve
             const int h = warp;
             const unsigned long long remaining = static_cast<unsigned long long>(k) - sel_above1[h];
             // Descending: lane j holds digit 31 - j.
-            const uint32_t cnt = hist2[h][31 - lane];
-            uint32_t incl = cnt;
+            const uint32_t c2 = hist2[h][31 - lane];
+            uint32_t incl = c2;
 #pragma unroll
             for (int o = 1; o < 32; o <<= 1) {
                 const uint32_t y = __shfl_up_sync(0xFFFFFFFFu, incl, o);
                 if (lane >= o) incl += y;
             }
-            const uint32_t excl = incl - cnt;
+            const uint32_t excl = incl - c2;
             if (excl < remaining && incl >= remaining) {
                 sel_thr[h] = (sel_b1[h] << 5) | (31u - lane);
                 sel_need[h] = remaining - excl;  // ties at the threshold to take
             }
         }
         cluster.sync();
+        if (tid < QPG) {
+            loc_thr[tid] = *cluster.map_shared_rank(&sel_thr[tid], 0);
+            loc_need[tid] = *cluster.map_shared_rank(&sel_need[tid], 0);
+        }
+        __syncthreads();
     }
 
+    POPKV_PHASE(3);
     // Selection of this slice, in token order.  Thread t owns local tokens
     // [t*per, (t+1)*per); per-head (greater, equal) counts travel as four
     // 16-bit fields of one 64-bit scan (per <= 16, slice <= 8192).
     {
         uint32_t thr[QPG];
         unsigned long long need[QPG];
-        if (k > 0) {
 #pragma unroll
-            for (int h = 0; h < QPG; ++h) {
-                thr[h] = *cluster.map_shared_rank(&sel_thr[h], 0);
-                need[h] = *cluster.map_shared_rank(&sel_need[h], 0);
-            }
+        for (int h = 0; h < QPG; ++h) {
+            thr[h] = k > 0 ? loc_thr[h] : 0u;
+            need[h] = k > 0 ? loc_need[h] : 0ull;
         }
         const int per = (n_local + kRetThreads - 1) / kRetThreads;
         const int lo = min(n_local, tid * per), hi = min(n_local, lo + per);
@@ -352,17 +407,29 @@ __global__ void __launch_bounds__(kRetThreads, 1) retrieve_kernel(const Retrieve
             cta_eq[tid] = (eq_tot >> (16 * (tid & 3))) & 0xFFFFull;
         }
         cluster.sync();
+        // Carries from lower ranks: lane c of warp h reads rank c's counts of head h.
+        if (warp < QPG) {
+            unsigned long long tg = 0, te = 0;
+            if (k > 0 && lane < rank) {
+                tg = *cluster.map_shared_rank(&cta_gt[warp], lane);
+                te = *cluster.map_shared_rank(&cta_eq[warp], lane);
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                tg += __shfl_xor_sync(0xFFFFFFFFu, tg, o);
+                te += __shfl_xor_sync(0xFFFFFFFFu, te, o);
+            }
+            if (lane == 0) {
+                loc_cgt[warp] = tg;
+                loc_ceq[warp] = te;
+            }
+        }
+        __syncthreads();
         unsigned long long gt_before[QPG], eq_before[QPG];
 #pragma unroll
         for (int h = 0; h < QPG; ++h) {
-            unsigned long long cg_ = 0, ce = 0;
-            if (k > 0)
-                for (int c = 0; c < rank; ++c) {
-                    cg_ += *cluster.map_shared_rank(&cta_gt[h], c);
-                    ce += *cluster.map_shared_rank(&cta_eq[h], c);
-                }
-            gt_before[h] = cg_ + ((gt_ex >> (16 * (h & 3))) & 0xFFFFull);
-            eq_before[h] = ce + ((eq_ex >> (16 * (h & 3))) & 0xFFFFull);
+            gt_before[h] = loc_cgt[h] + ((gt_ex >> (16 * (h & 3))) & 0xFFFFull);
+            eq_before[h] = loc_ceq[h] + ((eq_ex >> (16 * (h & 3))) & 0xFFFFull);
         }
         for (int i = lo; i < hi; ++i) {
             uint32_t m = 0;
@@ -400,9 +467,10 @@ __global__ void __launch_bounds__(kRetThreads, 1) retrieve_kernel(const Retrieve
             if (rank == 0) ulist[nu++] = kCurrentEntry;
             s_nu = nu;
         }
-        cluster.sync();  // peers' count reads are done; s_nu / ulist visible
+        __syncthreads();
     }
 
+    POPKV_PHASE(4);
     // ---- D: attention over the union rows ---------------------------------------
     const int nu = s_nu;
     const int g = tid >> 4, c = tid & 15;  // row group, 16-byte unit (dims 8c..8c+7)
@@ -491,6 +559,7 @@ __global__ void __launch_bounds__(kRetThreads, 1) retrieve_kernel(const Retrieve
     cp_async_wait_ret<0>();
     __syncthreads();  // the ring is reused below
 
+    POPKV_PHASE(5);
     // Combine the two row groups of each warp, then the 16 warps, per head.
     float* red_m = red;                                       // [QPG][16]
     float* red_s = red + QPG * kRetWarps;                     // [QPG][16]
@@ -541,11 +610,13 @@ __global__ void __launch_bounds__(kRetThreads, 1) retrieve_kernel(const Retrieve
     }
     cluster.sync();  // partial states of every CTA visible
 
+    POPKV_PHASE(6);
     // ---- E: CTA h merges head h ---------------------------------------------------
     if (rank < QPG) {
         const int h = rank;
         if (tid < C) {
             s_w[tid] = *cluster.map_shared_rank(&part_m[h], tid);
+            s_part_s[tid] = *cluster.map_shared_rank(&part_s[h], tid);
         }
         __syncthreads();
         if (tid == 0) {
@@ -554,20 +625,25 @@ __global__ void __launch_bounds__(kRetThreads, 1) retrieve_kernel(const Retrieve
             float den = 0.0f;
             for (int q = 0; q < C; ++q) {
                 const float w = s_w[q] == -INFINITY ? 0.0f : exp2f(s_w[q] - M);
-                den = __fmaf_rn(*cluster.map_shared_rank(&part_s[h], q), w, den);
+                den = __fmaf_rn(s_part_s[q], w, den);
                 s_w[q] = w;
             }
             s_den = den;
         }
         __syncthreads();
         if (tid < 128) {
+            float v[16];
+#pragma unroll
+            for (int q = 0; q < 16; ++q) v[q] = q < C ? cluster.map_shared_rank(&part_acc[h][0], q)[tid] : 0.0f;
             float num = 0.0f;
-            for (int q = 0; q < C; ++q)
-                if (s_w[q] != 0.0f) num = __fmaf_rn(cluster.map_shared_rank(&part_acc[h][0], q)[tid], s_w[q], num);
+#pragma unroll
+            for (int q = 0; q < 16; ++q)
+                if (q < C) num = __fmaf_rn(v[q], s_w[q], num);
             store_elem(static_cast<QT*>(a.out) + (row0 + h) * 128 + tid, num / s_den);
         }
     }
     cluster.sync();  // keep this CTA's shared memory alive until every peer has read it
+    POPKV_PHASE(7);
 }
 
 template <int G, int QPG, typename QT, typename KT>
@@ -692,3 +768,10 @@ extern "C" int popkv_retrieve(
         return dispatch_g<__nv_bfloat16, __nv_bfloat16>(dim_group_size, qpg, args, clusters, s);
     return dispatch_g<__half, __half>(dim_group_size, qpg, args, clusters, s);
 }
+
+#ifdef POPKV_RETRIEVE_TIMING
+extern "C" __attribute__((visibility("default"))) int popkv_retrieve_phase_ns(unsigned long long* host, int ctas) {
+    return static_cast<int>(cudaMemcpyFromSymbol(host, g_retrieve_phase_ns,
+                                                  sizeof(unsigned long long) * 8 * static_cast<size_t>(ctas)));
+}
+#endif

@@ -32,7 +32,9 @@ def test_graph_step_matches_oracle(cuda_device, preset, context, budget):
     assert torch.equal(out, again)
     eager = P.popkv_attention(to(x.queries[0]), keys, values, to(x.current_keys[0]),
                               to(x.current_values[0]), cache, mapping, budget=budget)
-    torch.testing.assert_close(out[0], eager, atol=0, rtol=0)
+    # The graph runs the fused kernel, whose attention sums in another order than the
+    # three-launch chain: equal up to bf16 output rounding.
+    assert (out[0].float() - eager.float()).abs().max().item() <= 2 ** -6
 
     kbits, qbits = x.bits("keys")[0], x.bits("queries")
     opk = oracle.pack(kbits, "bf16", token_group_size=tg, dim_group_size=g)
