@@ -241,6 +241,8 @@ def algorithmic_bytes(args, layer) -> dict:
         "query_encode": qio + B * qh * (32 + 8 * reps),
         "score": meta + scores + B * qh * (32 + 8 * reps),
         "score_fused": meta + scores + qio,
+        "score_hist": meta + scores + qio + B * qh * 2048 * 4,
+        "topk_hist": scores + idx + 2 * B * qh * 2048 * 4,
         "topk": scores + idx,
         "attn_partial": gathered + idx + partials + qio,
         "attn_merge": partials + qio,
@@ -326,7 +328,7 @@ def run_ours(args, world, rank, local):
                 st["algorithmic_bytes"] = abytes[name]
                 st["achieved_gbs"] = round(gbs, 1)
                 st["frac_of_hbm"] = round(gbs / peaks["hbm_gbs"], 4)
-        timed = {k: v for k, v in stages.items() if k in ("score_fused", "topk", "attn_fused")}
+        timed = {k: v for k, v in stages.items() if k in ("score_hist", "topk_hist", "attn_partial", "attn_merge")}
         dominant = max(timed, key=lambda k: timed[k]["us"])
         dom = stages[dominant]
         step_bytes = abytes["step"]
@@ -360,7 +362,7 @@ def run_ours(args, world, rank, local):
             },
             "stages_us": {k: v for k, v in stages.items()},
             "e2e": e2e,
-            "gpu_launches": 3 * args.steps,
+            "gpu_launches": 4 * args.steps,
             "clocks": clocks,
         }
         if not args.no_cpu_baseline and world == 1:
@@ -374,24 +376,35 @@ def run_ours(args, world, rank, local):
 
 
 def time_events(fn, reps, device):
-    """Mean device time of one call over `reps` back-to-back calls (us).
+    """Device time of one call (us): `reps` calls captured in a CUDA graph and replayed.
 
-    The calls are enqueued between one pair of events, so host launch cost
-    hides behind the previous call's execution; each call includes its launch
-    gap on the device, as inside a captured step.
+    Launching through the graph keeps host overhead (Python, ctypes) out of the
+    measurement, as in the captured decode step; each call still pays its
+    in-graph launch gap.
     """
     import torch
-    stream = torch.cuda.current_stream(device)
-    for _ in range(3):
-        fn()
+    side = torch.cuda.Stream(device)
+    side.wait_stream(torch.cuda.current_stream(device))
+    with torch.cuda.stream(side):
+        for _ in range(3):
+            fn()
+    torch.cuda.current_stream(device).wait_stream(side)
+    torch.cuda.synchronize(device)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=side):
+        for _ in range(reps):
+            fn()
+    graph.replay()
     torch.cuda.synchronize(device)
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    stream = torch.cuda.current_stream(device)
     a.record(stream)
-    for _ in range(reps):
-        fn()
+    for _ in range(5):
+        graph.replay()
     b.record(stream)
     torch.cuda.synchronize(device)
-    return a.elapsed_time(b) / reps * 1e3
+    del graph
+    return a.elapsed_time(b) / (5 * reps) * 1e3
 
 
 def stage_breakdown(args, layer, steps, device):
@@ -400,8 +413,13 @@ def stage_breakdown(args, layer, steps, device):
     from popkv_b200 import _lib
     from popkv_b200 import popkv_cuda as C
     lib, check, ptr = _lib.lib(), _lib.check, _lib.ptr
-    s = _lib.stream_of(device)
     n = len(steps)
+
+    class _CurrentStream:  # resolves to the capturing stream at launch time
+        @property
+        def _as_parameter_(self):
+            return _lib.stream_of(device)
+    s = _CurrentStream()
     reps = args.stage_reps
     out = {}
     ctr = {"i": 0}
@@ -427,6 +445,13 @@ def stage_breakdown(args, layer, steps, device):
         ptr(st.queries), _lib.BF16, B, st.q_heads, 128, *(ptr(t) for t in st.cache.packed),
         st.kv_heads, int(st.cache.packed[0].shape[1]), ptr(st.head_to_kv), st.prefix_tokens, st.g,
         ptr(st.scores), _lib.F16, s)))
+    run("score_hist", lambda st: check(lib.popkv_score_hist(
+        ptr(st.queries), _lib.BF16, B, st.q_heads, *(ptr(t) for t in st.cache.packed), st.kv_heads,
+        int(st.cache.packed[0].shape[1]), ptr(st.head_to_kv), st.prefix_tokens, st.g, ptr(st.scores),
+        ptr(st.hist), s)))
+    run("topk_hist", lambda st: check(lib.popkv_topk_hist(
+        ptr(st.scores), ptr(st.hist), B * st.q_heads, st.prefix_tokens, st.prefix_tokens, st.k,
+        st.prefix_tokens, ptr(st.indices), st.selected, s)))
     run("topk", lambda st: check(lib.popkv_topk(
         ptr(st.scores), _lib.F16, B * st.q_heads, st.prefix_tokens, st.prefix_tokens, st.k,
         st.prefix_tokens, ptr(st.indices), st.selected, s)))
@@ -451,7 +476,18 @@ def stage_breakdown(args, layer, steps, device):
             None, ptr(st.head_to_kv), st.split_tokens, ptr(st.partials), ptr(st.counters),
             ptr(st.output), _lib.BF16, s))
     run("attn_fused", fused)
-    out["step_graph"] = {"us": round(time_events(lambda: cold().replay(), reps, device), 2)}
+    # The step's own graph: replayed back to back (one host call per step).
+    stream = torch.cuda.current_stream(device)
+    for _ in range(3):
+        cold().replay()
+    torch.cuda.synchronize(device)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for _ in range(reps):
+        cold().replay()
+    b.record(stream)
+    torch.cuda.synchronize(device)
+    out["step_graph"] = {"us": round(a.elapsed_time(b) / reps * 1e3, 2)}
 
     # Prepack of the whole context and a mid-group append (not part of the step),
     # launched through the C ABI so host-side validation stays outside the events.

@@ -118,6 +118,30 @@ POPKV_API int popkv_score(const void* queries, int queries_dtype, int64_t batch,
                 int64_t dim_group_size, void* scores, int scores_dtype, void* stream);
 
 /*
+ * popkv_score plus the first radix pass of the top-k, for head_dim 128 and at
+ * most 4 query heads per KV head: besides the fp16 scores it adds, for every
+ * query row, the count of scores per top-11-bit key digit into hist
+ * (uint32 [batch*q_heads, 2048]), which must hold zeros on entry.
+ * popkv_topk_hist consumes the histogram and leaves it zeroed again.
+ * No reference counterpart: the reference runs torch.topk on the scores.
+ */
+POPKV_API int popkv_score_hist(const void* queries, int queries_dtype, int64_t batch,
+                               int64_t q_heads, const int32_t* k_sign, const int32_t* k_mag,
+                               const uint16_t* k_low, const uint16_t* k_delta, int64_t kv_heads,
+                               int64_t capacity, const int64_t* head_to_kv, int64_t tokens,
+                               int64_t dim_group_size, uint16_t* scores, uint32_t* hist,
+                               void* stream);
+
+/*
+ * popkv_topk for fp16 scores whose first-pass histogram popkv_score_hist has
+ * already produced (rows of `tokens` <= 65536 scores).  Same output contract
+ * as popkv_topk; resets the rows of `hist` it reads to zero.
+ */
+POPKV_API int popkv_topk_hist(const uint16_t* scores, uint32_t* hist, int64_t rows, int64_t tokens,
+                              int64_t row_stride, int64_t k, int64_t current_index, int64_t* out,
+                              int64_t out_stride, void* stream);
+
+/*
  * Per-row top-k with the current-token slot reserved.
  *
  * For each of `rows` rows of `tokens` scores (fp16 or fp32, row r at

@@ -29,6 +29,8 @@ _SIGNATURES = {
     "popkv_score_encoded": ([_P, _P, _P, _P, _L, _L, _P, _P, _P, _P, _L, _L, _P, _L, _L, _P, _P], _I),
     "popkv_score": ([_P, _I, _L, _L, _L, _P, _P, _P, _P, _L, _L, _P, _L, _L, _P, _I, _P], _I),
     "popkv_topk": ([_P, _I, _L, _L, _L, _L, _L, _P, _L, _P], _I),
+    "popkv_score_hist": ([_P, _I, _L, _L, _P, _P, _P, _P, _L, _L, _P, _L, _L, _P, _P, _P], _I),
+    "popkv_topk_hist": ([_P, _P, _L, _L, _L, _L, _L, _P, _L, _P], _I),
     "popkv_attn_partial": ([_P, _I, _L, _L, _L, _P, _P, _I, _L, _L, _L, _L, _L, _L, _L, _L,
                             _P, _P, _P, _L, _P, _P, _L, _P, _P], _I),
     "popkv_attn_merge": ([_P, _L, _L, _L, _P, _I, _P], _I),

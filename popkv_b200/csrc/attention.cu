@@ -24,6 +24,28 @@
 
 #include "common.cuh"
 
+// Phase timestamps for profiling builds (-DPOPKV_ATTN_TIMING): thread 0 of each
+// CTA of the pipelined kernel records %globaltimer at its phase boundaries.
+#ifdef POPKV_ATTN_TIMING
+__device__ unsigned long long g_attn_phase_ns[4096][8];
+#define POPKV_ATTN_PHASE(i)                                                              \
+    do {                                                                                 \
+        const unsigned cta_ = blockIdx.y * gridDim.x + blockIdx.x;                       \
+        if (threadIdx.x == 0 && cta_ < 4096) {                                           \
+            unsigned long long t_;                                                       \
+            asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_));                      \
+            g_attn_phase_ns[cta_][i] = t_;                                               \
+        }                                                                                \
+    } while (0)
+extern "C" __attribute__((visibility("default"))) int popkv_attn_phase_ns(unsigned long long* host, int ctas) {
+    return static_cast<int>(cudaMemcpyFromSymbol(host, g_attn_phase_ns, sizeof(unsigned long long) * 8 * ctas));
+}
+#else
+#define POPKV_ATTN_PHASE(i) \
+    do {                    \
+    } while (0)
+#endif
+
 namespace popkv {
 namespace {
 
@@ -301,6 +323,7 @@ __global__ void __launch_bounds__(kAttnThreads, 4) attn_partial_pipe_kernel(
     int64_t selected, int64_t split_tokens, int splits, float scale, int* __restrict__ counters,
     OT* __restrict__ merged) {
     extern __shared__ __align__(16) unsigned char ring[];  // [stage][K|V][32 rows][256 B]
+    POPKV_ATTN_PHASE(0);
     __shared__ float s_m[kAttnThreads / 32], s_s[kAttnThreads / 32];
     __shared__ float s_acc[kAttnThreads / 32][8][16];
 
@@ -321,21 +344,25 @@ __global__ void __launch_bounds__(kAttnThreads, 4) attn_partial_pipe_kernel(
     const unsigned char* cvb = reinterpret_cast<const unsigned char*>(cur_v + (b * kv_heads + kvh) * 128) + c * 16;
     const int64_t kstride = kts * 2, vstride = vts * 2;
 
-    // Cache row of each slot this thread copies: slot = slot0 + i*64 + h*32 + r.
+    // Slot -> cache row map of the split, loaded with one coalesced pass and
+    // staged in shared memory; thread t then copies slot i*32 + r for each i.
+    __shared__ int s_rid[kPipeRows * kPipeMaxSub];
+    for (int j = tid; j < kPipeRows * kPipeMaxSub; j += kAttnThreads) {
+        const int64_t slot = slot0 + j;
+        int id = kSlotMasked;
+        if (slot < slot_end && (!valid || valid[row * selected + slot])) {
+            const int64_t idx = __ldg(indices + row * selected + slot);
+            id = idx == prefix_tokens ? kSlotCurrent
+                                      : static_cast<int>(idx < 0 ? 0 : (idx > prefix_tokens - 1 ? prefix_tokens - 1 : idx));
+        }
+        s_rid[j] = id;
+    }
+    __syncthreads();
     int rid[kPipeMaxSub][kPipeRowsPerGroup];
 #pragma unroll
     for (int i = 0; i < kPipeMaxSub; ++i)
 #pragma unroll
-        for (int h = 0; h < kPipeRowsPerGroup; ++h) {
-            const int64_t slot = slot0 + static_cast<int64_t>(i) * kPipeRows + h * kPipeRowGroups + r;
-            int id = kSlotMasked;
-            if (slot < slot_end && (!valid || valid[row * selected + slot])) {
-                const int64_t idx = __ldg(indices + row * selected + slot);
-                id = idx == prefix_tokens ? kSlotCurrent
-                                          : static_cast<int>(idx < 0 ? 0 : (idx > prefix_tokens - 1 ? prefix_tokens - 1 : idx));
-            }
-            rid[i][h] = id;
-        }
+        for (int h = 0; h < kPipeRowsPerGroup; ++h) rid[i][h] = s_rid[i * kPipeRows + h * kPipeRowGroups + r];
 
     auto stage_k = [&](int st, int h) {
         return ring + ((st * 2 + 0) * kPipeRows + h * kPipeRowGroups + r) * kRowBytes + c * 16;
@@ -362,8 +389,10 @@ __global__ void __launch_bounds__(kAttnThreads, 4) attn_partial_pipe_kernel(
         cp_async_commit();
     };
 
+    POPKV_ATTN_PHASE(1);
 #pragma unroll
     for (int i = 0; i < kPipeStages - 1; ++i) issue(i);
+    POPKV_ATTN_PHASE(2);
 
     float q[16];
     {
@@ -424,6 +453,7 @@ __global__ void __launch_bounds__(kAttnThreads, 4) attn_partial_pipe_kernel(
         }
     }
     cp_async_wait<0>();
+    POPKV_ATTN_PHASE(3);
 
     // Combine the 4 row groups of this warp (lanes with equal c), then the 8 warps.
 #pragma unroll
@@ -475,6 +505,7 @@ __global__ void __launch_bounds__(kAttnThreads, 4) attn_partial_pipe_kernel(
         out[0] = M == -INFINITY ? -INFINITY : M * kLn2;
         out[1] = total;
     }
+    POPKV_ATTN_PHASE(4);
     if constexpr (!std::is_same<OT, void>::value) {
         __shared__ int s_last;
         __shared__ float s_w[kMaxFusedSplits];
@@ -486,14 +517,20 @@ __global__ void __launch_bounds__(kAttnThreads, 4) attn_partial_pipe_kernel(
         if (!s_last) return;
         __threadfence();
         const float* pr = partials + row * splits * (128 + 2);
+        __shared__ float s_ps[kMaxFusedSplits];
+        if (tid < splits) {  // one thread per split: all loads in flight at once
+            s_w[tid] = __ldcg(pr + tid * 130);
+            s_ps[tid] = __ldcg(pr + tid * 130 + 1);
+        }
+        __syncthreads();
         if (tid == 0) {
             float gm = -INFINITY;
-            for (int sp = 0; sp < splits; ++sp) gm = fmaxf(gm, __ldcg(pr + sp * 130));
+            for (int sp = 0; sp < splits; ++sp) gm = fmaxf(gm, s_w[sp]);
             float den = 0.0f;
             for (int sp = 0; sp < splits; ++sp) {
-                const float w = expf(__ldcg(pr + sp * 130) - gm);
+                const float w = expf(s_w[sp] - gm);
                 s_w[sp] = w;
-                den = __fmaf_rn(__ldcg(pr + sp * 130 + 1), w, den);
+                den = __fmaf_rn(s_ps[sp], w, den);
             }
             s_den = den;
             counters[row] = 0;
@@ -501,6 +538,7 @@ __global__ void __launch_bounds__(kAttnThreads, 4) attn_partial_pipe_kernel(
         __syncthreads();
         if (tid < 128) {
             float num = 0.0f;
+#pragma unroll 8
             for (int sp = 0; sp < splits; ++sp) num = __fmaf_rn(__ldcg(pr + sp * 130 + 2 + tid), s_w[sp], num);
             store_out(merged + row * 128 + tid, num / s_den);
         }

@@ -30,6 +30,11 @@ int allow_dynamic_smem(Kernel kernel, int bytes) {
     cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
     if (err != cudaSuccess)
         return fail(POPKV_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(err));
+    // Prefer the largest shared-memory carveout so that several CTAs fit per SM.
+    err = cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                               cudaSharedmemCarveoutMaxShared);
+    if (err != cudaSuccess)
+        return fail(POPKV_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(err));
     __atomic_fetch_or(&done_mask, bit, __ATOMIC_RELEASE);
     return POPKV_OK;
 }
@@ -64,6 +69,14 @@ __device__ __forceinline__ float small_int_to_float(int c) {
 // fp32 -> fp16 round-to-nearest-even, returned as the 16-bit pattern.
 __device__ __forceinline__ uint16_t float_to_half_bits(float v) {
     return __half_as_ushort(__float2half_rn(v));
+}
+
+// Order-preserving 16-bit key of an fp16 score: a larger score has a larger key;
+// -0 and +0 share a key; NaN takes the largest key.
+__device__ __forceinline__ uint32_t order_key16(uint16_t h) {
+    if ((h & 0x7FFFu) == 0) h = 0;
+    if ((h & 0x7C00u) == 0x7C00u && (h & 0x3FFu)) return 0xFFFFu;
+    return (h & 0x8000u) ? (~static_cast<uint32_t>(h) & 0xFFFFu) : (static_cast<uint32_t>(h) | 0x8000u);
 }
 
 // Bucket means shared by every encoder (reference csrc/popkv_ext.cu:128-135):

@@ -40,7 +40,7 @@
 // Phase timestamps for profiling builds (-DPOPKV_RETRIEVE_TIMING): thread 0 of
 // each CTA records %globaltimer at the phase boundaries into g_retrieve_phase_ns.
 #ifdef POPKV_RETRIEVE_TIMING
-__device__ unsigned long long g_retrieve_phase_ns[2048][8];
+__device__ unsigned long long g_retrieve_phase_ns[2048][16];
 #define POPKV_PHASE(i)                                                                  \
     do {                                                                                \
         if (threadIdx.x == 0 && blockIdx.x < 2048) {                                    \
@@ -64,7 +64,6 @@ constexpr int kRetThreads = 512;
 constexpr int kRetWarps = kRetThreads / 32;
 constexpr int kHist1Bins = 2048;  // key bits 15..5
 constexpr int kHist2Bins = 32;    // key bits 4..0
-constexpr int kRingStages = 4;
 constexpr int kRingRows = 32;     // rows per stage: 32 row groups of 16 threads
 constexpr int kRowBytes128 = 256; // 128 x 16-bit
 constexpr int kMaxSlice = 8192;
@@ -166,7 +165,7 @@ struct RetrieveArgs {
 // Dynamic shared memory layout (bytes), computed identically on host and device.
 struct RetrieveSmem {
     size_t scores, mask, ulist, region, total;
-    static __host__ __device__ RetrieveSmem make(int qpg, int64_t slice) {
+    static __host__ __device__ RetrieveSmem make(int qpg, int64_t slice, int stages) {
         RetrieveSmem s;
         const size_t sc = static_cast<size_t>(qpg) * slice * 2;
         s.scores = 0;
@@ -174,7 +173,7 @@ struct RetrieveSmem {
         s.ulist = s.mask + (static_cast<size_t>(slice) + 15) / 16 * 16;
         s.region = s.ulist + (static_cast<size_t>(slice + 1) * 2 + 15) / 16 * 16;
         const size_t hist = static_cast<size_t>(qpg) * kHist1Bins * 4;
-        const size_t ring = static_cast<size_t>(kRingStages) * kRingRows * 2 * kRowBytes128;
+        const size_t ring = static_cast<size_t>(stages) * kRingRows * 2 * kRowBytes128;
         const size_t red = static_cast<size_t>(qpg) * kRetWarps * (2 + 16 * 8) * 4;
         size_t region = hist > ring ? hist : ring;
         region = region > red ? region : red;
@@ -183,8 +182,9 @@ struct RetrieveSmem {
     }
 };
 
-template <int G, int QPG, typename QT, typename KT>
+template <int G, int QPG, typename QT, typename KT, int STAGES>
 __global__ void __launch_bounds__(kRetThreads, 1) retrieve_kernel(const RetrieveArgs a) {
+    constexpr int kRingStages = STAGES;
     extern __shared__ __align__(16) unsigned char smem[];
     __shared__ QueryState<G> states[QPG];
     __shared__ float scratch[QPG][2 * 32 * 4];
@@ -216,7 +216,7 @@ __global__ void __launch_bounds__(kRetThreads, 1) retrieve_kernel(const Retrieve
     const int64_t t_begin = static_cast<int64_t>(rank) * a.slice;
     const int64_t t_end = min(t_begin + a.slice, a.tokens);
     const int n_local = t_end > t_begin ? static_cast<int>(t_end - t_begin) : 0;
-    const RetrieveSmem lay = RetrieveSmem::make(QPG, a.slice);
+    const RetrieveSmem lay = RetrieveSmem::make(QPG, a.slice, STAGES);
     uint16_t* scores16 = reinterpret_cast<uint16_t*>(smem + lay.scores);   // [QPG][slice]
     uint8_t* sel_mask = smem + lay.mask;                                    // [slice]
     uint16_t* ulist = reinterpret_cast<uint16_t*>(smem + lay.ulist);       // [slice + 1]
@@ -275,81 +275,56 @@ __global__ void __launch_bounds__(kRetThreads, 1) retrieve_kernel(const Retrieve
 
     POPKV_PHASE(2);
     // ---- C: radix select across the cluster -------------------------------------
-    // Pass 1 (key bits 15..5), pull-based: the QPG*2048 histogram positions are
-    // split into C equal segments, segment q (one head, a run of bins in
-    // descending key order) being reduced by CTA q from all C CTAs' histograms
-    // through DSMEM.  The CTA whose segment holds the k-th largest key of its
-    // head finds the digit and stores it into the leader CTA.
+    // CTA h owns head h's selection: pass 1 pulls head h's 2048-bin histograms
+    // (key bits 15..5) from every CTA through DSMEM, sums them and finds the digit
+    // holding the k-th largest key; pass 2 counts the few keys inside that digit
+    // by their low 5 bits into CTA h's 32-bin histogram, which gives the exact
+    // threshold and the number of ties at it to take.
     const int64_t k = a.k;
-    const int seg_len = QPG * kHist1Bins / C;         // positions per segment
-    const int segs_per_head = kHist1Bins / seg_len;   // = C / QPG
-    const int my_head = rank / segs_per_head;
-    const int my_seg = rank % segs_per_head;
     if (k > 0) {
         cluster.sync();  // all local histograms complete
-        // This thread's positions of segment `rank`: p = my_seg*seg_len + j, bin = 2047 - p.
-        constexpr int kMaxPer = (4 * kHist1Bins / 8 + kRetThreads - 1) / kRetThreads;  // QPG<=4, C>=8
-        uint32_t cnt[kMaxPer];
-        unsigned long long local = 0;
+        if (rank < QPG) {
+            const int h = rank;
+            constexpr int kPer = kHist1Bins / kRetThreads;  // 4 positions per thread
+            uint32_t cnt[kPer];
+            unsigned long long local = 0;
 #pragma unroll
-        for (int q = 0; q < kMaxPer; ++q) {
-            cnt[q] = 0;
-            const int j = tid * kMaxPer + q;
-            if (j < seg_len) {
-                const int bin = kHist1Bins - 1 - (my_seg * seg_len + j);
-                const uint32_t* src = hist1 + my_head * kHist1Bins + bin;
+            for (int q = 0; q < kPer; ++q) {
+                const int bin = kHist1Bins - 1 - (tid * kPer + q);  // descending key order
+                const uint32_t* src = hist1 + h * kHist1Bins + bin;
                 uint32_t v[16];
 #pragma unroll
                 for (int r = 0; r < 16; ++r) v[r] = r < C ? *cluster.map_shared_rank(src, r) : 0u;
+                cnt[q] = 0;
 #pragma unroll
                 for (int r = 0; r < 16; ++r) cnt[q] += v[r];
                 local += cnt[q];
             }
-        }
-        unsigned long long seg_total;
-        unsigned long long run = ret_exclusive_scan<unsigned long long>(local, scan_a, seg_total);
-        if (tid == 0) cta_gt[0] = seg_total;  // published segment total (reuses cta_gt[0])
-        cluster.sync();  // segment totals visible
-        if (tid < 32) {
-            // carry = totals of the segments before mine (same head), one lane per segment.
-            unsigned long long t = 0;
-            if (tid < my_seg) t = *cluster.map_shared_rank(&cta_gt[0], my_head * segs_per_head + tid);
+            unsigned long long total;
+            unsigned long long run = ret_exclusive_scan<unsigned long long>(local, scan_a, total);
 #pragma unroll
-            for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xFFFFFFFFu, t, o);
-            if (tid == 0) cta_eq[0] = t;
-        }
-        __syncthreads();
-        const unsigned long long carry = cta_eq[0];
-        run += carry;
-#pragma unroll
-        for (int q = 0; q < kMaxPer; ++q) {
-            const int j = tid * kMaxPer + q;
-            if (j < seg_len) {
+            for (int q = 0; q < kPer; ++q) {
                 if (run < static_cast<unsigned long long>(k) && run + cnt[q] >= static_cast<unsigned long long>(k)) {
-                    *cluster.map_shared_rank(&sel_b1[my_head], 0) = kHist1Bins - 1 - (my_seg * seg_len + j);
-                    *cluster.map_shared_rank(&sel_above1[my_head], 0) = run;
+                    sel_b1[h] = kHist1Bins - 1 - (tid * kPer + q);
+                    sel_above1[h] = run;
                 }
                 run += cnt[q];
             }
         }
-        cluster.sync();  // the leader holds every head's digit
-        if (tid < QPG) {
-            loc_b1[tid] = *cluster.map_shared_rank(&sel_b1[tid], 0);
-        }
+        cluster.sync();  // digits chosen; pulls of every peer's histogram done
+        if (tid < QPG) loc_b1[tid] = *cluster.map_shared_rank(&sel_b1[tid], tid);
         __syncthreads();
-        // Pass 2 (key bits 4..0): the few keys inside the chosen digit, counted
-        // into the leader's 32-bin histograms.
-        uint32_t* leader_hist2 = cluster.map_shared_rank(&hist2[0][0], 0);
         for (int i = tid; i < n_local; i += kRetThreads) {
 #pragma unroll
             for (int h = 0; h < QPG; ++h) {
                 const uint32_t key = score_key(scores16[h * a.slice + i]);
-                if ((key >> 5) == loc_b1[h]) atomicAdd(leader_hist2 + h * kHist2Bins + (key & 31u), 1u);
+                if ((key >> 5) == loc_b1[h])
+                    atomicAdd(cluster.map_shared_rank(&hist2[h][0], h) + (key & 31u), 1u);
             }
         }
         cluster.sync();
-        if (rank == 0 && warp < QPG) {
-            const int h = warp;
+        if (rank < QPG && warp == 0) {
+            const int h = rank;
             const unsigned long long remaining = static_cast<unsigned long long>(k) - sel_above1[h];
             // Descending: lane j holds digit 31 - j.
             const uint32_t c2 = hist2[h][31 - lane];
@@ -367,8 +342,8 @@ __global__ void __launch_bounds__(kRetThreads, 1) retrieve_kernel(const Retrieve
         }
         cluster.sync();
         if (tid < QPG) {
-            loc_thr[tid] = *cluster.map_shared_rank(&sel_thr[tid], 0);
-            loc_need[tid] = *cluster.map_shared_rank(&sel_need[tid], 0);
+            loc_thr[tid] = *cluster.map_shared_rank(&sel_thr[tid], tid);
+            loc_need[tid] = *cluster.map_shared_rank(&sel_need[tid], tid);
         }
         __syncthreads();
     }
@@ -473,6 +448,9 @@ __global__ void __launch_bounds__(kRetThreads, 1) retrieve_kernel(const Retrieve
     POPKV_PHASE(4);
     // ---- D: attention over the union rows ---------------------------------------
     const int nu = s_nu;
+#ifdef POPKV_RETRIEVE_TIMING
+    if (threadIdx.x == 0 && blockIdx.x < 2048) g_retrieve_phase_ns[blockIdx.x][8] = static_cast<unsigned long long>(nu);
+#endif
     const int g = tid >> 4, c = tid & 15;  // row group, 16-byte unit (dims 8c..8c+7)
     float qv[QPG][8];
 #pragma unroll
@@ -533,14 +511,17 @@ __global__ void __launch_bounds__(kRetThreads, 1) retrieve_kernel(const Retrieve
 #pragma unroll
             for (int j = 0; j < 8; ++j) kf[j] = vf[j] = 0.0f;
         }
+        // The 16 lanes of a row group share `mask`, so a head's dot product and
+        // its shuffles run only in the groups that selected the row.
+        const unsigned group = 0xFFFFu << (lane & 16);
 #pragma unroll
         for (int h = 0; h < QPG; ++h) {
-            float dot = 0.0f;
-#pragma unroll
-            for (int j = 0; j < 8; ++j) dot = __fmaf_rn(kf[j], qv[h][j], dot);
-#pragma unroll
-            for (int o = 8; o > 0; o >>= 1) dot += __shfl_xor_sync(0xFFFFFFFFu, dot, o);
             if (mask & (1u << h)) {
+                float dot = 0.0f;
+#pragma unroll
+                for (int j = 0; j < 8; ++j) dot = __fmaf_rn(kf[j], qv[h][j], dot);
+#pragma unroll
+                for (int o = 8; o > 0; o >>= 1) dot += __shfl_xor_sync(group, dot, o);
                 if (dot > m_[h]) {
                     const float alpha = exp2f(m_[h] - dot);
                     s_[h] = __fmaf_rn(s_[h], alpha, 1.0f);
@@ -646,9 +627,11 @@ __global__ void __launch_bounds__(kRetThreads, 1) retrieve_kernel(const Retrieve
     POPKV_PHASE(7);
 }
 
-template <int G, int QPG, typename QT, typename KT>
-int launch_retrieve_t(const RetrieveArgs& args, int64_t clusters, cudaStream_t stream) {
-    auto kernel = retrieve_kernel<G, QPG, QT, KT>;
+constexpr size_t kSmemLimit = 227 * 1024 - 16 * 1024;  // dynamic budget beside static smem
+
+template <int G, int QPG, typename QT, typename KT, int STAGES>
+int launch_retrieve_s(const RetrieveArgs& args, int64_t clusters, cudaStream_t stream, bool* tried) {
+    auto kernel = retrieve_kernel<G, QPG, QT, KT, STAGES>;
     cudaFuncSetAttribute(kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
     cudaLaunchConfig_t config = {};
     config.blockDim = dim3(kRetThreads, 1, 1);
@@ -659,15 +642,22 @@ int launch_retrieve_t(const RetrieveArgs& args, int64_t clusters, cudaStream_t s
     attr[0].val.clusterDim.z = 1;
     config.attrs = attr;
     config.numAttrs = 1;
-    for (int cs : {16, 8}) {
-        if (args.tokens > static_cast<int64_t>(cs) * kMaxSlice) continue;
-        RetrieveArgs a = args;
-        a.slice = ((args.tokens + cs - 1) / cs + 63) / 64 * 64;
-        if (a.slice < 64) a.slice = 64;
-        const RetrieveSmem lay = RetrieveSmem::make(QPG, a.slice);
-        cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                               static_cast<int>(lay.total));
-        if (err != cudaSuccess) return fail(POPKV_ERR_CUDA, "popkv_retrieve: %s", cudaGetErrorString(err));
+    // Pick the cluster size minimising (waves x tokens per CTA): every cluster of
+    // a wave must fit on the GPCs at once (one CTA per SM).
+    int best_cs = 0;
+    double best_cost = 0.0;
+    int64_t best_slice = 0;
+    for (int cs = 16; cs >= 8; --cs) {
+        int64_t slice = ((args.tokens + cs - 1) / cs + 63) / 64 * 64;
+        if (slice < 64) slice = 64;
+        if (slice > kMaxSlice) continue;
+        const RetrieveSmem lay = RetrieveSmem::make(QPG, slice, STAGES);
+        if (lay.total > kSmemLimit) continue;
+        if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 static_cast<int>(lay.total)) != cudaSuccess) {
+            cudaGetLastError();
+            continue;
+        }
         attr[0].val.clusterDim.x = cs;
         config.gridDim = dim3(static_cast<unsigned>(clusters * cs), 1, 1);
         config.dynamicSmemBytes = lay.total;
@@ -676,10 +666,37 @@ int launch_retrieve_t(const RetrieveArgs& args, int64_t clusters, cudaStream_t s
             cudaGetLastError();
             continue;
         }
-        err = cudaLaunchKernelEx(&config, kernel, a);
-        if (err != cudaSuccess) return fail(POPKV_ERR_CUDA, "popkv_retrieve: %s", cudaGetErrorString(err));
-        return check_launch("popkv_retrieve");
+        const double waves = static_cast<double>((clusters + active - 1) / active);
+        const double cost = waves * static_cast<double>(slice);
+        if (best_cs == 0 || cost < best_cost) {
+            best_cs = cs;
+            best_cost = cost;
+            best_slice = slice;
+        }
     }
+    if (best_cs == 0) return POPKV_ERR_UNSUPPORTED;
+    *tried = true;
+    RetrieveArgs a = args;
+    a.slice = best_slice;
+    const RetrieveSmem lay = RetrieveSmem::make(QPG, best_slice, STAGES);
+    cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           static_cast<int>(lay.total));
+    if (err != cudaSuccess) return fail(POPKV_ERR_CUDA, "popkv_retrieve: %s", cudaGetErrorString(err));
+    attr[0].val.clusterDim.x = best_cs;
+    config.gridDim = dim3(static_cast<unsigned>(clusters * best_cs), 1, 1);
+    config.dynamicSmemBytes = lay.total;
+    err = cudaLaunchKernelEx(&config, kernel, a);
+    if (err != cudaSuccess) return fail(POPKV_ERR_CUDA, "popkv_retrieve: %s", cudaGetErrorString(err));
+    return check_launch("popkv_retrieve");
+}
+
+template <int G, int QPG, typename QT, typename KT>
+int launch_retrieve_t(const RetrieveArgs& args, int64_t clusters, cudaStream_t stream) {
+    bool tried = false;
+    int st = launch_retrieve_s<G, QPG, QT, KT, 8>(args, clusters, stream, &tried);
+    if (tried || st != POPKV_ERR_UNSUPPORTED) return st;
+    st = launch_retrieve_s<G, QPG, QT, KT, 4>(args, clusters, stream, &tried);
+    if (tried || st != POPKV_ERR_UNSUPPORTED) return st;
     return fail(POPKV_ERR_UNSUPPORTED, "popkv_retrieve: no cluster size can be scheduled for %lld tokens",
                 static_cast<long long>(args.tokens));
 }
@@ -770,8 +787,35 @@ extern "C" int popkv_retrieve(
 }
 
 #ifdef POPKV_RETRIEVE_TIMING
+extern "C" __attribute__((visibility("default"))) int popkv_retrieve_phase_reset() {
+    static unsigned long long zeros[2048 * 16];
+    return static_cast<int>(cudaMemcpyToSymbol(g_retrieve_phase_ns, zeros, sizeof(zeros)));
+}
+
 extern "C" __attribute__((visibility("default"))) int popkv_retrieve_phase_ns(unsigned long long* host, int ctas) {
     return static_cast<int>(cudaMemcpyFromSymbol(host, g_retrieve_phase_ns,
-                                                  sizeof(unsigned long long) * 8 * static_cast<size_t>(ctas)));
+                                                  sizeof(unsigned long long) * 16 * static_cast<size_t>(ctas)));
+}
+
+extern "C" __attribute__((visibility("default"))) int popkv_retrieve_max_clusters(int cluster, int slice) {
+    using namespace popkv;
+    auto kernel = retrieve_kernel<16, 4, __nv_bfloat16, __nv_bfloat16, 8>;
+    const RetrieveSmem lay = RetrieveSmem::make(4, slice, 8);
+    cudaFuncSetAttribute(kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(lay.total));
+    cudaLaunchConfig_t config = {};
+    config.blockDim = dim3(kRetThreads, 1, 1);
+    config.gridDim = dim3(static_cast<unsigned>(8 * cluster), 1, 1);
+    config.dynamicSmemBytes = lay.total;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = cluster;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    config.attrs = attr;
+    config.numAttrs = 1;
+    int active = -1;
+    cudaError_t e = cudaOccupancyMaxActiveClusters(&active, kernel, &config);
+    return e == cudaSuccess ? active : -100 - static_cast<int>(e);
 }
 #endif

@@ -55,7 +55,14 @@ constexpr int kTokensPerThread = 2;
 constexpr int kScoreTile = kScoreThreads * kTokensPerThread;
 constexpr int kMaxGroupHeads = 16;
 
-template <int G, typename QT, bool RAW>
+// With HIST the kernel also counts every score's top 11 key bits
+// (order_key16 >> 5) per query row into hist [rows][2048] (global, must hold
+// zeros on entry): per-CTA shared-memory histograms flushed with one global
+// atomic per non-empty bin.  That is the first radix pass of the top-k.
+constexpr int kHistBins11 = 2048;
+constexpr int kMaxHistHeads = 4;
+
+template <int G, typename QT, bool RAW, bool HIST = false>
 __global__ void __launch_bounds__(kScoreThreads) score128_kernel(
     const QT* __restrict__ queries, const int32_t* __restrict__ q_sign,
     const int32_t* __restrict__ q_mag, const float* __restrict__ q_low,
@@ -63,8 +70,9 @@ __global__ void __launch_bounds__(kScoreThreads) score128_kernel(
     const int32_t* __restrict__ k_mag, const uint16_t* __restrict__ k_low,
     const uint16_t* __restrict__ k_delta, const int64_t* __restrict__ head_to_kv,
     uint16_t* __restrict__ scores, int q_heads, int group_heads, int64_t capacity,
-    int64_t tokens, float scale) {
+    int64_t tokens, float scale, uint32_t* __restrict__ hist = nullptr) {
     constexpr int R = 128 / G;
+    extern __shared__ uint32_t hist_s[];  // [group_heads][2048] when HIST
     __shared__ QueryState<G> states[kMaxGroupHeads];
     __shared__ float scratch[kScoreThreads / 32][2 * 32 * 4];
 
@@ -90,6 +98,9 @@ __global__ void __launch_bounds__(kScoreThreads) score128_kernel(
             else if (j < 8 + R) states[h].ql[j - 8] = q_low[row * R + j - 8];
             else states[h].dq[j - 8 - R] = q_delta[row * R + j - 8 - R];
         }
+    }
+    if constexpr (HIST) {
+        for (int i = threadIdx.x; i < group_heads * kHistBins11; i += kScoreThreads) hist_s[i] = 0;
     }
     __syncthreads();
     if (threadIdx.x < group_heads) finish_state<G>(states[threadIdx.x]);
@@ -118,8 +129,17 @@ __global__ void __launch_bounds__(kScoreThreads) score128_kernel(
             const float total = score_token<G>(st, tp[i]);
             if (live[i]) {
                 const int64_t t = tile0 + threadIdx.x + i * kScoreThreads;
-                out[t] = float_to_half_bits(__fmul_rn(total, scale));
+                const uint16_t bits = float_to_half_bits(__fmul_rn(total, scale));
+                out[t] = bits;
+                if constexpr (HIST) atomicAdd(&hist_s[h * kHistBins11 + (order_key16(bits) >> 5)], 1u);
             }
+        }
+    }
+    if constexpr (HIST) {
+        __syncthreads();
+        for (int i = threadIdx.x; i < group_heads * kHistBins11; i += kScoreThreads) {
+            const uint32_t c = hist_s[i];
+            if (c) atomicAdd(hist + (row0 + i / kHistBins11) * kHistBins11 + (i % kHistBins11), c);
         }
     }
 }
@@ -184,6 +204,22 @@ __global__ void __launch_bounds__(kGenericThreads) score_generic_kernel(
 // ---------------------------------------------------------------------------
 // Launchers.
 // ---------------------------------------------------------------------------
+
+template <int G, typename QT, bool RAW>
+int launch_score128_hist(const void* queries, int64_t batch, int64_t q_heads, const int32_t* k_sign,
+                         const int32_t* k_mag, const uint16_t* k_low, const uint16_t* k_delta,
+                         int64_t kv_heads, int64_t capacity, const int64_t* head_to_kv,
+                         int64_t tokens, uint16_t* scores, uint32_t* hist, cudaStream_t stream) {
+    const int group_heads = static_cast<int>(q_heads / kv_heads);
+    const int64_t tiles = (tokens + kScoreTile - 1) / kScoreTile;
+    dim3 grid(static_cast<unsigned>(tiles), static_cast<unsigned>(batch * kv_heads));
+    const size_t smem = sizeof(uint32_t) * kHistBins11 * group_heads;
+    score128_kernel<G, QT, RAW, true><<<grid, kScoreThreads, smem, stream>>>(
+        static_cast<const QT*>(queries), nullptr, nullptr, nullptr, nullptr, k_sign, k_mag, k_low,
+        k_delta, head_to_kv, scores, static_cast<int>(q_heads), group_heads, capacity, tokens,
+        score_scale_for(128), hist);
+    return check_launch("popkv_score_hist");
+}
 
 template <int G, typename QT, bool RAW>
 int launch_score128(const void* queries, const int32_t* q_sign, const int32_t* q_mag,
@@ -375,4 +411,36 @@ extern "C" int popkv_score(const void* queries, int queries_dtype, int64_t batch
 #undef POPKV_GEN_T
 #undef POPKV_GEN
     return check_launch("popkv_score");
+}
+
+extern "C" int popkv_score_hist(const void* queries, int queries_dtype, int64_t batch, int64_t q_heads,
+                                const int32_t* k_sign, const int32_t* k_mag, const uint16_t* k_low,
+                                const uint16_t* k_delta, int64_t kv_heads, int64_t capacity,
+                                const int64_t* head_to_kv, int64_t tokens, int64_t dim_group_size,
+                                uint16_t* scores, uint32_t* hist, void* stream) {
+    using namespace popkv;
+    if (!valid_dtype(queries_dtype)) return fail(POPKV_ERR_INVALID, "queries must be fp32/fp16/bf16");
+    int st = check_score_common(batch, q_heads, kv_heads, capacity, tokens, dim_group_size, head_to_kv);
+    if (st != POPKV_OK) return st;
+    if (q_heads / kv_heads > kMaxHistHeads)
+        return fail(POPKV_ERR_UNSUPPORTED, "popkv_score_hist: more than %d query heads per KV head",
+                    kMaxHistHeads);
+    if (batch == 0) return POPKV_OK;
+    if (!queries || !k_sign || !k_mag || !k_low || !k_delta || !scores || !hist)
+        return fail(POPKV_ERR_INVALID, "popkv_score_hist: null pointer");
+    if (!aligned(k_sign, 16) || !aligned(k_mag, 16) || !aligned(k_low, 16) || !aligned(k_delta, 16))
+        return fail(POPKV_ERR_INVALID, "packed planes must be 16-byte aligned");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+#define POPKV_SH(G_, T_)                                                                             \
+    return launch_score128_hist<G_, T_, true>(queries, batch, q_heads, k_sign, k_mag, k_low, k_delta, \
+                                               kv_heads, capacity, head_to_kv, tokens, scores, hist, s)
+#define POPKV_SH_T(T_)                         \
+    if (dim_group_size == 16) { POPKV_SH(16, T_); } \
+    if (dim_group_size == 32) { POPKV_SH(32, T_); } \
+    POPKV_SH(64, T_);
+    if (queries_dtype == POPKV_DTYPE_F32) { POPKV_SH_T(float) }
+    if (queries_dtype == POPKV_DTYPE_F16) { POPKV_SH_T(__half) }
+    POPKV_SH_T(__nv_bfloat16)
+#undef POPKV_SH_T
+#undef POPKV_SH
 }

@@ -447,8 +447,11 @@ __global__ void __launch_bounds__(kClusterThreads) topk_cluster_kernel(
             const uint32_t jj = tid * per + q;
             if (q < per && jj < nbins) {
                 const uint32_t bin = nbins - 1 - jj;
+                uint32_t v[CPR];
 #pragma unroll
-                for (int c = 0; c < CPR; ++c) counts[q] += cluster.map_shared_rank(hist, c)[bin];
+                for (int c = 0; c < CPR; ++c) v[c] = cluster.map_shared_rank(hist, c)[bin];  // all in flight
+#pragma unroll
+                for (int c = 0; c < CPR; ++c) counts[q] += v[c];
                 local += counts[q];
             }
         }
@@ -493,9 +496,14 @@ __global__ void __launch_bounds__(kClusterThreads) topk_cluster_kernel(
     (void)cta_exclusive_scan<unsigned long long>(mine, scan_sums, cta_sum);
     if (tid == 0) cta_totals = cta_sum;
     cluster.sync();  // totals published
-    unsigned long long carry = 0;
-    for (int c = 0; c < rank; ++c) carry += *cluster.map_shared_rank(&cta_totals, c);
+    if (tid < 32) {  // lane c < rank reads rank c's totals; one warp reduction
+        unsigned long long t = (tid < rank) ? *cluster.map_shared_rank(&cta_totals, tid) : 0ull;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xFFFFFFFFu, t, o);
+        if (tid == 0) scan_sums[kClusterWarps] = t;
+    }
     cluster.sync();  // nobody exits while a peer may still read its totals
+    const unsigned long long carry = scan_sums[kClusterWarps];
     unsigned long long gt_carry = carry >> 32, eq_carry = carry & 0xFFFFFFFFull;
 #pragma unroll
     for (int j = 0; j < CHUNKS; ++j) {
@@ -571,6 +579,157 @@ int try_launch_cluster(const void* scores, int64_t rows, int64_t tokens, int64_t
     return -1;
 }
 
+// ---------------------------------------------------------------------------
+// Top-k from a precomputed first-pass histogram (fp16 scores).
+//
+// The score kernel (popkv_score_hist) already counted every score's top 11
+// key bits per row, so one CTA per row only has to: read and re-zero its row of
+// the histogram and pick the digit of the k-th largest key; count the keys
+// inside that digit by their low 5 bits; and compact.  Thread t owns the
+// contiguous elements [t*PER, (t+1)*PER), held in registers (two keys per
+// register), so a single block scan gives the ascending-index output positions.
+// ---------------------------------------------------------------------------
+constexpr int kHistThreads = 1024;
+constexpr int kHistWarps = kHistThreads / 32;
+
+template <typename V>
+__device__ __forceinline__ V hist_exclusive_scan(V x, V* warp_sums, V& total) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    V incl = x;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        V y = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+        if (lane >= o) incl += y;
+    }
+    if (lane == 31) warp_sums[warp] = incl;
+    __syncthreads();
+    if (warp == 0) {
+        V w = lane < kHistWarps ? warp_sums[lane] : V(0);
+        V wi = w;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            V y = __shfl_up_sync(0xFFFFFFFFu, wi, o);
+            if (lane >= o) wi += y;
+        }
+        if (lane < kHistWarps) warp_sums[lane] = wi - w;
+        if (lane == kHistWarps - 1) warp_sums[kHistWarps] = wi;
+    }
+    __syncthreads();
+    V result = warp_sums[warp] + incl - x;
+    total = warp_sums[kHistWarps];
+    __syncthreads();
+    return result;
+}
+
+template <int PER>
+__global__ void __launch_bounds__(kHistThreads) topk_hist_kernel(
+    const uint16_t* __restrict__ scores, uint32_t* __restrict__ hist, int64_t tokens,
+    int64_t row_stride, int64_t k, int64_t current_index, int64_t* __restrict__ out,
+    int64_t out_stride) {
+    __shared__ unsigned long long scan_sums[kHistWarps + 1];
+    __shared__ uint32_t hist2[32];
+    __shared__ uint32_t sel_b1, sel_thr;
+    __shared__ unsigned long long sel_above, sel_need;
+    const int64_t row = blockIdx.x;
+    const int tid = threadIdx.x;
+    int64_t* dst = out + row * out_stride;
+    if (current_index >= 0 && tid == 0) dst[k] = current_index;
+    uint32_t* hrow = hist + row * 2048;
+
+    // Histogram of this row: positions 2*tid, 2*tid+1 in descending key order.
+    const uint2 hv = *reinterpret_cast<const uint2*>(hrow + 2048 - 2 - 2 * tid);
+    // hv.y is bin 2047 - 2*tid, hv.x is bin 2046 - 2*tid.
+    // Keys: elements [tid*PER, tid*PER + PER), two per register.
+    const int64_t base = static_cast<int64_t>(tid) * PER;
+    const uint16_t* src = scores + row * row_stride + base;
+    uint32_t packed[PER / 2];
+    const int64_t left = tokens - base;
+    const int lim = left <= 0 ? 0 : (left >= PER ? PER : static_cast<int>(left));
+    if (lim == PER) {
+#pragma unroll
+        for (int j = 0; j < PER / 8; ++j) {
+            const uint4 v = __ldg(reinterpret_cast<const uint4*>(src) + j);
+            const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+                packed[4 * j + e] = order_key16(static_cast<uint16_t>(w[e] & 0xFFFFu)) |
+                                    (order_key16(static_cast<uint16_t>(w[e] >> 16)) << 16);
+        }
+    } else {
+#pragma unroll
+        for (int j = 0; j < PER / 2; ++j) packed[j] = 0;
+#pragma unroll
+        for (int e = 0; e < PER; ++e)
+            if (e < lim) packed[e >> 1] |= order_key16(src[e]) << (16 * (e & 1));
+    }
+    auto key_of = [&](int e) -> uint32_t { return (packed[e >> 1] >> (16 * (e & 1))) & 0xFFFFu; };
+    __syncthreads();  // every thread has read its histogram entries
+    *reinterpret_cast<uint2*>(hrow + 2048 - 2 - 2 * tid) = make_uint2(0u, 0u);  // leave zeros for the next call
+    if (tid < 32) hist2[tid] = 0;
+
+    if (k > 0) {
+        const unsigned long long kk = static_cast<unsigned long long>(k);
+        unsigned long long total;
+        const unsigned long long run0 =
+            hist_exclusive_scan<unsigned long long>(static_cast<unsigned long long>(hv.x) + hv.y, scan_sums, total);
+        const unsigned long long run1 = run0 + hv.y;
+        if (run0 < kk && run1 >= kk) {
+            sel_b1 = 2047u - 2u * tid;
+            sel_above = run0;
+        } else if (run1 < kk && run1 + hv.x >= kk) {
+            sel_b1 = 2046u - 2u * tid;
+            sel_above = run1;
+        }
+        __syncthreads();
+        const uint32_t b1 = sel_b1;
+#pragma unroll
+        for (int e = 0; e < PER; ++e)
+            if (e < lim && (key_of(e) >> 5) == b1) atomicAdd(&hist2[key_of(e) & 31u], 1u);
+        __syncthreads();
+        if (tid < 32) {
+            const unsigned long long remaining = kk - sel_above;
+            const uint32_t c2 = hist2[31 - tid];
+            uint32_t incl = c2;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const uint32_t y = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+                if (tid >= o) incl += y;
+            }
+            const uint32_t excl = incl - c2;
+            if (excl < remaining && incl >= remaining) {
+                sel_thr = (b1 << 5) | (31u - tid);
+                sel_need = remaining - excl;
+            }
+        }
+        __syncthreads();
+        const uint32_t thr = sel_thr;
+        const unsigned long long need = sel_need;
+        unsigned int gt = 0, eq = 0;
+#pragma unroll
+        for (int e = 0; e < PER; ++e) {
+            if (e < lim) {
+                gt += key_of(e) > thr;
+                eq += key_of(e) == thr;
+            }
+        }
+        const unsigned long long ex = hist_exclusive_scan<unsigned long long>(
+            (static_cast<unsigned long long>(gt) << 32) | eq, scan_sums, total);
+        unsigned long long gt_before = ex >> 32, eq_before = ex & 0xFFFFFFFFull;
+#pragma unroll
+        for (int e = 0; e < PER; ++e) {
+            if (e >= lim) continue;
+            const uint32_t key = key_of(e);
+            if (key > thr) {
+                dst[gt_before + min(eq_before, need)] = base + e;
+                ++gt_before;
+            } else if (key == thr) {
+                if (eq_before < need) dst[gt_before + eq_before] = base + e;
+                ++eq_before;
+            }
+        }
+    }
+}
+
 template <bool F32>
 int launch_topk(const void* scores, int64_t rows, int64_t tokens, int64_t row_stride, int64_t k,
                 int64_t current_index, int64_t* out, int64_t out_stride, cudaStream_t stream) {
@@ -632,4 +791,33 @@ extern "C" int popkv_topk(const void* scores, int scores_dtype, int64_t rows, in
     if (scores_dtype == POPKV_DTYPE_F32)
         return launch_topk<true>(scores, rows, tokens, row_stride, k, current_index, out, out_stride, s);
     return launch_topk<false>(scores, rows, tokens, row_stride, k, current_index, out, out_stride, s);
+}
+
+extern "C" int popkv_topk_hist(const uint16_t* scores, uint32_t* hist, int64_t rows, int64_t tokens,
+                               int64_t row_stride, int64_t k, int64_t current_index, int64_t* out,
+                               int64_t out_stride, void* stream) {
+    using namespace popkv;
+    if (rows < 0 || tokens < 0) return fail(POPKV_ERR_INVALID, "popkv_topk_hist: negative shape");
+    if (k < 0 || k > tokens)
+        return fail(POPKV_ERR_INVALID, "popkv_topk_hist: k must be between 0 and the token count");
+    if (row_stride < tokens) return fail(POPKV_ERR_INVALID, "popkv_topk_hist: row_stride < tokens");
+    const int64_t width = k + (current_index >= 0 ? 1 : 0);
+    if (out_stride < width) return fail(POPKV_ERR_INVALID, "popkv_topk_hist: out_stride too small");
+    if (rows == 0) return POPKV_OK;
+    if (!out || !hist || !scores) return fail(POPKV_ERR_INVALID, "popkv_topk_hist: null pointer");
+    if (!aligned(scores, 16) || (row_stride * 2) % 16 != 0 || !aligned(hist, 16))
+        return fail(POPKV_ERR_INVALID, "popkv_topk_hist: scores rows and hist must be 16-byte aligned");
+    if (tokens > 64 * kHistThreads)
+        return fail(POPKV_ERR_UNSUPPORTED, "popkv_topk_hist: at most %d tokens", 64 * kHistThreads);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const unsigned grid = static_cast<unsigned>(rows);
+    if (tokens <= 8 * kHistThreads)
+        topk_hist_kernel<8><<<grid, kHistThreads, 0, s>>>(scores, hist, tokens, row_stride, k, current_index, out, out_stride);
+    else if (tokens <= 16 * kHistThreads)
+        topk_hist_kernel<16><<<grid, kHistThreads, 0, s>>>(scores, hist, tokens, row_stride, k, current_index, out, out_stride);
+    else if (tokens <= 32 * kHistThreads)
+        topk_hist_kernel<32><<<grid, kHistThreads, 0, s>>>(scores, hist, tokens, row_stride, k, current_index, out, out_stride);
+    else
+        topk_hist_kernel<64><<<grid, kHistThreads, 0, s>>>(scores, hist, tokens, row_stride, k, current_index, out, out_stride);
+    return check_launch("popkv_topk_hist");
 }

@@ -4,9 +4,10 @@ The reference runs each decode stage as a separate eager launch with Python
 integers for the token count (popkv.py:1076-1115), so its host overhead is
 part of every token.  ``SparseAttentionStep`` owns static input/output buffers
 and preallocated intermediates, calls the C-ABI kernels directly, and captures
-the three launches (popcount score with the query encoding in its prologue,
-top-k + current slot, split partials with the merge done by the last CTA of
-each row) into one CUDA graph.  Replaying the graph costs one launch.
+the four launches (popcount score with the query encoding in its prologue and
+the top-k's first radix histogram as a side output, top-k + current slot,
+split partials, merge) into one CUDA graph.  ``fused=True`` uses the single
+popkv_retrieve launch instead (one thread-block cluster per KV head).  Replaying the graph costs one launch.
 
 The graph is specific to the cache length it was captured at.  Call
 ``recapture()`` after appending tokens (or use ``run_eager``).
@@ -36,7 +37,7 @@ class SparseAttentionStep:
     def __init__(self, cache: PopKVCache, prefix_keys: torch.Tensor, prefix_values: torch.Tensor,
                  head_to_kv: torch.Tensor, *, budget: int, q_heads: int | None = None,
                  q_dtype: torch.dtype = torch.bfloat16, split_tokens: int = 256,
-                 batch: int = 1, use_graph: bool = True, fused: bool = True) -> None:
+                 batch: int = 1, use_graph: bool = True, fused: bool = False) -> None:
         if prefix_keys.ndim == 3:
             prefix_keys, prefix_values = prefix_keys[None], prefix_values[None]
         if prefix_keys.stride(-1) != 1 or prefix_values.stride(-1) != 1:
@@ -79,6 +80,8 @@ class SparseAttentionStep:
         self.indices = torch.zeros((B, QH, self.selected), device=dev, dtype=torch.int64)
         self.partials = torch.zeros((B, QH, self.splits, D + 2), device=dev, dtype=torch.float32)
         self.counters = torch.zeros((B * QH,), device=dev, dtype=torch.int32)  # self-resetting
+        # First-pass top-k histogram written by the score kernel, re-zeroed by the top-k.
+        self.hist = torch.zeros((B * QH, 2048), device=dev, dtype=torch.int32)
         self.graph = None
         self.use_graph = use_graph
         # fused=True: one popkv_retrieve launch (score, select, attention, merge in
@@ -104,24 +107,34 @@ class SparseAttentionStep:
                 ptr(self.current_keys), ptr(self.current_values), self.budget, ptr(self.output),
                 None, ptr(self.indices), s))
             return
-        # Query encoding runs in the score kernel's prologue (one launch fewer).
-        check(lib.popkv_score(ptr(self.queries), _lib.dtype_code(self.queries), B, QH, 128,
-                              *(ptr(t) for t in packed), KVH, capacity, ptr(self.head_to_kv),
-                              self.prefix_tokens, self.g, ptr(self.scores), _lib.F16, s))
-        check(lib.popkv_topk(ptr(self.scores), _lib.F16, B * QH, self.prefix_tokens,
-                             self.prefix_tokens, self.k, self.prefix_tokens, ptr(self.indices),
-                             self.selected, s))
-        # Partials and their merge in one launch (the last CTA of each row merges).
-        check(lib.popkv_attn_partial_merge(
+        # Query encoding runs in the score kernel's prologue, which also builds the
+        # top-k's first radix histogram; the top-k then needs one CTA per row.
+        hist_ok = QH // KVH <= 4 and self.prefix_tokens <= 65536
+        if hist_ok:
+            check(lib.popkv_score_hist(ptr(self.queries), _lib.dtype_code(self.queries), B, QH,
+                                       *(ptr(t) for t in packed), KVH, capacity, ptr(self.head_to_kv),
+                                       self.prefix_tokens, self.g, ptr(self.scores), ptr(self.hist), s))
+            check(lib.popkv_topk_hist(ptr(self.scores), ptr(self.hist), B * QH, self.prefix_tokens,
+                                      self.prefix_tokens, self.k, self.prefix_tokens,
+                                      ptr(self.indices), self.selected, s))
+        else:
+            check(lib.popkv_score(ptr(self.queries), _lib.dtype_code(self.queries), B, QH, 128,
+                                  *(ptr(t) for t in packed), KVH, capacity, ptr(self.head_to_kv),
+                                  self.prefix_tokens, self.g, ptr(self.scores), _lib.F16, s))
+            check(lib.popkv_topk(ptr(self.scores), _lib.F16, B * QH, self.prefix_tokens,
+                                 self.prefix_tokens, self.k, self.prefix_tokens, ptr(self.indices),
+                                 self.selected, s))
+        check(lib.popkv_attn_partial(
             ptr(self.queries), _lib.dtype_code(self.queries), B, QH, 128, ptr(pk), ptr(pv),
             _lib.dtype_code(pk), KVH, self.prefix_tokens, pk.stride(0), pk.stride(1), pk.stride(2),
             pv.stride(0), pv.stride(1), pv.stride(2), ptr(self.current_keys),
             ptr(self.current_values), ptr(self.indices), self.selected, None, ptr(self.head_to_kv),
-            self.split_tokens, ptr(self.partials), ptr(self.counters), ptr(self.output),
-            _lib.dtype_code(self.output), s))
+            self.split_tokens, ptr(self.partials), s))
+        check(lib.popkv_attn_merge(ptr(self.partials), B * QH, self.splits, 128, ptr(self.output),
+                                   _lib.dtype_code(self.output), s))
 
     def recapture(self) -> None:
-        """(Re)build the CUDA graph of the three launches for the current buffers."""
+        """(Re)build the CUDA graph of the step's launches for the current buffers."""
         with torch.cuda.device(self.device):
             side = torch.cuda.Stream(self.device)
             side.wait_stream(torch.cuda.current_stream(self.device))

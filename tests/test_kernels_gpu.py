@@ -385,3 +385,33 @@ def test_partial_merge_single_launch_matches_two_launches(cuda_device, valid):
         assert int(counters.abs().sum()) == 0
         torch.testing.assert_close(out.float(), want.float(), atol=1e-2, rtol=0)
         assert (out.float() - want.float()).abs().max().item() <= 2 ** -7
+
+
+@pytest.mark.parametrize("g", GROUPS)
+@pytest.mark.parametrize("tokens,budget", [(32768, 4096), (3000, 256), (100, 1000), (65536, 4096)])
+def test_score_hist_and_topk_hist_match_separate_kernels(cuda_device, g, tokens, budget):
+    """popkv_score_hist + popkv_topk_hist == popkv_score + popkv_topk, and the histogram is re-zeroed."""
+    from popkv_b200 import _lib
+    keys, q, mapping, packed = _score_case(cuda_device, g, 1, tokens, q_heads=32, kv_heads=8,
+                                           seed=tokens + g)
+    want_scores = C.score(q, packed, head_to_kv=mapping, tokens=tokens, dim_group_size=g)
+    k = min(budget - 1, tokens)
+    want_idx = C.topk(want_scores, k, current_index=tokens)
+    scores = torch.empty_like(want_scores)
+    hist = torch.zeros(32, 2048, dtype=torch.int32, device=cuda_device)
+    idx = torch.empty(1, 32, k + 1, dtype=torch.int64, device=cuda_device)
+    cap = packed[0].shape[1]
+    for _ in range(2):
+        _lib.check(_lib.lib().popkv_score_hist(
+            _lib.ptr(q), _lib.BF16, 1, 32, *(_lib.ptr(t) for t in packed), 8, cap, _lib.ptr(mapping),
+            tokens, g, _lib.ptr(scores), _lib.ptr(hist), _lib.stream_of(cuda_device)))
+        torch.cuda.synchronize()
+        key = scores.view(torch.int16).to(torch.int32) & 0xFFFF
+        assert int(hist.sum()) == 32 * tokens
+        _lib.check(_lib.lib().popkv_topk_hist(
+            _lib.ptr(scores), _lib.ptr(hist), 32, tokens, tokens, k, tokens, _lib.ptr(idx), k + 1,
+            _lib.stream_of(cuda_device)))
+        torch.cuda.synchronize()
+        assert torch.equal(scores, want_scores)
+        assert torch.equal(idx, want_idx)
+        assert int(hist.abs().sum()) == 0
