@@ -50,7 +50,7 @@ L2_BYTES = 126 * 1024 * 1024
 def parse_args(argv=None):
     p = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     p.add_argument("--gpus", type=int, default=1)
-    p.add_argument("--steps", type=int, default=2000)
+    p.add_argument("--steps", type=int, default=10000)
     p.add_argument("--warmup", type=int, default=50)
     p.add_argument("--impl", choices=("ours", "reference"), default="ours")
     p.add_argument("--context", type=int, default=32768)
@@ -58,6 +58,8 @@ def parse_args(argv=None):
     p.add_argument("--batch", type=int, default=1)
     p.add_argument("--preset", choices=("popkv-q", "popkv-s", "popkv-normal"), default="popkv-q")
     p.add_argument("--no-graph", action="store_true", help="launch eagerly instead of a CUDA graph")
+    p.add_argument("--select", choices=("auto", "hist", "radix"), default="radix",
+                   help="top-k path of the step (hist: score kernel builds the first radix histogram)")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU baseline sample budget")
     p.add_argument("--stage-reps", type=int, default=50)
@@ -208,7 +210,8 @@ def build_steps(args, layer, copies: int):
         if B > 1:
             raise SystemExit("batch > 1 benchmarking is not wired yet")
         step = SparseAttentionStep(caches[0], keys, values, layer["mapping"], budget=args.budget,
-                                   q_dtype=torch.bfloat16, batch=B, use_graph=not args.no_graph)
+                                   q_dtype=torch.bfloat16, batch=B, use_graph=not args.no_graph,
+                                   select=args.select)
         step.queries.copy_(layer["queries"])
         step.current_keys.copy_(layer["cur_k"])
         step.current_values.copy_(layer["cur_v"])
@@ -241,8 +244,8 @@ def algorithmic_bytes(args, layer) -> dict:
         "query_encode": qio + B * qh * (32 + 8 * reps),
         "score": meta + scores + B * qh * (32 + 8 * reps),
         "score_fused": meta + scores + qio,
-        "score_hist": meta + scores + qio + B * qh * 2048 * 4,
-        "topk_hist": scores + idx + 2 * B * qh * 2048 * 4,
+        "score_topk_hist": meta + 2 * scores + qio + idx + 2 * B * qh * 2048 * 4,
+        "score_topk_radix": meta + 2 * scores + qio + idx,
         "topk": scores + idx,
         "attn_partial": gathered + idx + partials + qio,
         "attn_merge": partials + qio,
@@ -328,7 +331,11 @@ def run_ours(args, world, rank, local):
                 st["algorithmic_bytes"] = abytes[name]
                 st["achieved_gbs"] = round(gbs, 1)
                 st["frac_of_hbm"] = round(gbs / peaks["hbm_gbs"], 4)
-        timed = {k: v for k, v in stages.items() if k in ("score_hist", "topk_hist", "attn_partial", "attn_merge")}
+        # The step's own kernels; a histogram top-k is only timed with its score kernel.
+        names = {"score": "score_fused", "topk": "topk", "score_hist": "score_topk_hist",
+                 "topk_hist": "score_topk_hist", "attn_partial": "attn_partial",
+                 "attn_merge": "attn_merge", "retrieve": "retrieve"}
+        timed = {names[k]: stages[names[k]] for k in steps[0].kernels if names[k] in stages}
         dominant = max(timed, key=lambda k: timed[k]["us"])
         dom = stages[dominant]
         step_bytes = abytes["step"]
@@ -445,13 +452,27 @@ def stage_breakdown(args, layer, steps, device):
         ptr(st.queries), _lib.BF16, B, st.q_heads, 128, *(ptr(t) for t in st.cache.packed),
         st.kv_heads, int(st.cache.packed[0].shape[1]), ptr(st.head_to_kv), st.prefix_tokens, st.g,
         ptr(st.scores), _lib.F16, s)))
-    run("score_hist", lambda st: check(lib.popkv_score_hist(
-        ptr(st.queries), _lib.BF16, B, st.q_heads, *(ptr(t) for t in st.cache.packed), st.kv_heads,
-        int(st.cache.packed[0].shape[1]), ptr(st.head_to_kv), st.prefix_tokens, st.g, ptr(st.scores),
-        ptr(st.hist), s)))
-    run("topk_hist", lambda st: check(lib.popkv_topk_hist(
-        ptr(st.scores), ptr(st.hist), B * st.q_heads, st.prefix_tokens, st.prefix_tokens, st.k,
-        st.prefix_tokens, ptr(st.indices), st.selected, s)))
+    # popkv_topk_hist consumes (and re-zeroes) the histogram popkv_score_hist
+    # builds, so the two are only timed as a pair.
+    def score_topk_hist(st):
+        check(lib.popkv_score_hist(
+            ptr(st.queries), _lib.BF16, B, st.q_heads, *(ptr(t) for t in st.cache.packed), st.kv_heads,
+            int(st.cache.packed[0].shape[1]), ptr(st.head_to_kv), st.prefix_tokens, st.g, ptr(st.scores),
+            ptr(st.hist), s))
+        check(lib.popkv_topk_hist(
+            ptr(st.scores), ptr(st.hist), B * st.q_heads, st.prefix_tokens, st.prefix_tokens, st.k,
+            st.prefix_tokens, ptr(st.indices), st.selected, s))
+    run("score_topk_hist", score_topk_hist)
+
+    def score_topk_radix(st):
+        check(lib.popkv_score(
+            ptr(st.queries), _lib.BF16, B, st.q_heads, 128, *(ptr(t) for t in st.cache.packed),
+            st.kv_heads, int(st.cache.packed[0].shape[1]), ptr(st.head_to_kv), st.prefix_tokens, st.g,
+            ptr(st.scores), _lib.F16, s))
+        check(lib.popkv_topk(
+            ptr(st.scores), _lib.F16, B * st.q_heads, st.prefix_tokens, st.prefix_tokens, st.k,
+            st.prefix_tokens, ptr(st.indices), st.selected, s))
+    run("score_topk_radix", score_topk_radix)
     run("topk", lambda st: check(lib.popkv_topk(
         ptr(st.scores), _lib.F16, B * st.q_heads, st.prefix_tokens, st.prefix_tokens, st.k,
         st.prefix_tokens, ptr(st.indices), st.selected, s)))

@@ -166,10 +166,12 @@ __global__ void __launch_bounds__(kTopkThreads) topk_kernel(
     for (int64_t i = lo; i < hi; ++i) {
         const uint32_t key = key_at(i);
         if (key > threshold) {
-            dst[gt_before + min(eq_before, need)] = i;
+            const unsigned long long pos = gt_before + min(eq_before, need);
+            if (pos < static_cast<unsigned long long>(k)) dst[pos] = i;
             ++gt_before;
         } else if (key == threshold) {
-            if (eq_before < need) dst[gt_before + eq_before] = i;
+            const unsigned long long pos = gt_before + eq_before;
+            if (eq_before < need && pos < static_cast<unsigned long long>(k)) dst[pos] = i;
             ++eq_before;
         }
     }
@@ -303,10 +305,12 @@ __global__ void __launch_bounds__(kTopkThreads) topk_reg_kernel(
             if (!valid(j, e)) continue;
             const uint32_t key = key_of(j, e);
             if (key > threshold) {
-                dst[gt_before + min(eq_before, need)] = base + e;
+                const unsigned long long pos = gt_before + min(eq_before, need);
+                if (pos < static_cast<unsigned long long>(k)) dst[pos] = base + e;
                 ++gt_before;
             } else if (key == threshold) {
-                if (eq_before < need) dst[gt_before + eq_before] = base + e;
+                const unsigned long long pos = gt_before + eq_before;
+                if (eq_before < need && pos < static_cast<unsigned long long>(k)) dst[pos] = base + e;
                 ++eq_before;
             }
         }
@@ -517,10 +521,12 @@ __global__ void __launch_bounds__(kClusterThreads) topk_cluster_kernel(
             if (e >= lim[j]) continue;
             const uint32_t key = key_of(j, e);
             if (key > threshold) {
-                dst[gt_before + min(eq_before, need)] = base + e;
+                const unsigned long long pos = gt_before + min(eq_before, need);
+                if (pos < static_cast<unsigned long long>(k)) dst[pos] = base + e;
                 ++gt_before;
             } else if (key == threshold) {
-                if (eq_before < need) dst[gt_before + eq_before] = base + e;
+                const unsigned long long pos = gt_before + eq_before;
+                if (eq_before < need && pos < static_cast<unsigned long long>(k)) dst[pos] = base + e;
                 ++eq_before;
             }
         }
@@ -625,7 +631,7 @@ template <int PER>
 __global__ void __launch_bounds__(kHistThreads) topk_hist_kernel(
     const uint16_t* __restrict__ scores, uint32_t* __restrict__ hist, int64_t tokens,
     int64_t row_stride, int64_t k, int64_t current_index, int64_t* __restrict__ out,
-    int64_t out_stride) {
+    int64_t out_stride, bool vec_ok) {
     __shared__ unsigned long long scan_sums[kHistWarps + 1];
     __shared__ uint32_t hist2[32];
     __shared__ uint32_t sel_b1, sel_thr;
@@ -633,7 +639,15 @@ __global__ void __launch_bounds__(kHistThreads) topk_hist_kernel(
     const int64_t row = blockIdx.x;
     const int tid = threadIdx.x;
     int64_t* dst = out + row * out_stride;
-    if (current_index >= 0 && tid == 0) dst[k] = current_index;
+    if (tid == 0) {
+        if (current_index >= 0) dst[k] = current_index;
+        // Defaults if the histogram does not hold this row's counts (all writes
+        // stay inside the row's k slots regardless).
+        sel_b1 = 0;
+        sel_above = 0;
+        sel_thr = 0;
+        sel_need = 0;
+    }
     uint32_t* hrow = hist + row * 2048;
 
     // Histogram of this row: positions 2*tid, 2*tid+1 in descending key order.
@@ -645,7 +659,7 @@ __global__ void __launch_bounds__(kHistThreads) topk_hist_kernel(
     uint32_t packed[PER / 2];
     const int64_t left = tokens - base;
     const int lim = left <= 0 ? 0 : (left >= PER ? PER : static_cast<int>(left));
-    if (lim == PER) {
+    if (vec_ok && lim == PER) {
 #pragma unroll
         for (int j = 0; j < PER / 8; ++j) {
             const uint4 v = __ldg(reinterpret_cast<const uint4*>(src) + j);
@@ -720,10 +734,12 @@ __global__ void __launch_bounds__(kHistThreads) topk_hist_kernel(
             if (e >= lim) continue;
             const uint32_t key = key_of(e);
             if (key > thr) {
-                dst[gt_before + min(eq_before, need)] = base + e;
+                const unsigned long long pos = gt_before + min(eq_before, need);
+                if (pos < kk) dst[pos] = base + e;
                 ++gt_before;
             } else if (key == thr) {
-                if (eq_before < need) dst[gt_before + eq_before] = base + e;
+                const unsigned long long pos = gt_before + eq_before;
+                if (eq_before < need && pos < kk) dst[pos] = base + e;
                 ++eq_before;
             }
         }
@@ -805,19 +821,19 @@ extern "C" int popkv_topk_hist(const uint16_t* scores, uint32_t* hist, int64_t r
     if (out_stride < width) return fail(POPKV_ERR_INVALID, "popkv_topk_hist: out_stride too small");
     if (rows == 0) return POPKV_OK;
     if (!out || !hist || !scores) return fail(POPKV_ERR_INVALID, "popkv_topk_hist: null pointer");
-    if (!aligned(scores, 16) || (row_stride * 2) % 16 != 0 || !aligned(hist, 16))
-        return fail(POPKV_ERR_INVALID, "popkv_topk_hist: scores rows and hist must be 16-byte aligned");
+    if (!aligned(hist, 16)) return fail(POPKV_ERR_INVALID, "popkv_topk_hist: hist must be 16-byte aligned");
+    const bool vec_ok = aligned(scores, 16) && (row_stride * 2) % 16 == 0;
     if (tokens > 64 * kHistThreads)
         return fail(POPKV_ERR_UNSUPPORTED, "popkv_topk_hist: at most %d tokens", 64 * kHistThreads);
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     const unsigned grid = static_cast<unsigned>(rows);
     if (tokens <= 8 * kHistThreads)
-        topk_hist_kernel<8><<<grid, kHistThreads, 0, s>>>(scores, hist, tokens, row_stride, k, current_index, out, out_stride);
+        topk_hist_kernel<8><<<grid, kHistThreads, 0, s>>>(scores, hist, tokens, row_stride, k, current_index, out, out_stride, vec_ok);
     else if (tokens <= 16 * kHistThreads)
-        topk_hist_kernel<16><<<grid, kHistThreads, 0, s>>>(scores, hist, tokens, row_stride, k, current_index, out, out_stride);
+        topk_hist_kernel<16><<<grid, kHistThreads, 0, s>>>(scores, hist, tokens, row_stride, k, current_index, out, out_stride, vec_ok);
     else if (tokens <= 32 * kHistThreads)
-        topk_hist_kernel<32><<<grid, kHistThreads, 0, s>>>(scores, hist, tokens, row_stride, k, current_index, out, out_stride);
+        topk_hist_kernel<32><<<grid, kHistThreads, 0, s>>>(scores, hist, tokens, row_stride, k, current_index, out, out_stride, vec_ok);
     else
-        topk_hist_kernel<64><<<grid, kHistThreads, 0, s>>>(scores, hist, tokens, row_stride, k, current_index, out, out_stride);
+        topk_hist_kernel<64><<<grid, kHistThreads, 0, s>>>(scores, hist, tokens, row_stride, k, current_index, out, out_stride, vec_ok);
     return check_launch("popkv_topk_hist");
 }

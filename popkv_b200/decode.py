@@ -4,10 +4,10 @@ The reference runs each decode stage as a separate eager launch with Python
 integers for the token count (popkv.py:1076-1115), so its host overhead is
 part of every token.  ``SparseAttentionStep`` owns static input/output buffers
 and preallocated intermediates, calls the C-ABI kernels directly, and captures
-the four launches (popcount score with the query encoding in its prologue and
-the top-k's first radix histogram as a side output, top-k + current slot,
-split partials, merge) into one CUDA graph.  ``fused=True`` uses the single
-popkv_retrieve launch instead (one thread-block cluster per KV head).  Replaying the graph costs one launch.
+the four launches (popcount score with the query encoding in its prologue,
+top-k + current slot, split partials, merge) into one CUDA graph.
+``fused=True`` uses the single popkv_retrieve launch instead (one thread-block
+cluster per KV head).  Replaying the graph costs one launch.
 
 The graph is specific to the cache length it was captured at.  Call
 ``recapture()`` after appending tokens (or use ``run_eager``).
@@ -32,12 +32,19 @@ class SparseAttentionStep:
         head_to_kv: int64 [QH] GQA mapping (consecutive query heads per KV head).
         budget: selected tokens per query head including the current slot.
         q_dtype: dtype of the queries / outputs.
+        select: "radix" (score, then the radix top-k: one thread-block
+            cluster per row) or "hist" (the score kernel also builds the top-k's
+            first radix histogram and one CTA per row finishes the selection;
+            needs <= 4 query heads per KV head and <= 65536 tokens).  "auto" is
+            "radix", the faster of the two on B200 at 32K tokens (57.5 vs 62.5
+            us per graph-captured step).
     """
 
     def __init__(self, cache: PopKVCache, prefix_keys: torch.Tensor, prefix_values: torch.Tensor,
                  head_to_kv: torch.Tensor, *, budget: int, q_heads: int | None = None,
                  q_dtype: torch.dtype = torch.bfloat16, split_tokens: int = 256,
-                 batch: int = 1, use_graph: bool = True, fused: bool = False) -> None:
+                 batch: int = 1, use_graph: bool = True, fused: bool = False,
+                 select: str = "auto") -> None:
         if prefix_keys.ndim == 3:
             prefix_keys, prefix_values = prefix_keys[None], prefix_values[None]
         if prefix_keys.stride(-1) != 1 or prefix_values.stride(-1) != 1:
@@ -87,6 +94,18 @@ class SparseAttentionStep:
         # fused=True: one popkv_retrieve launch (score, select, attention, merge in
         # one thread-block cluster per KV head); fused=False: the three-launch chain.
         self.fused = fused and batch == 1 and self.q_heads // self.kv_heads in (1, 2, 4)
+        hist_ok = self.q_heads // self.kv_heads <= 4 and self.prefix_tokens <= 65536
+        if select not in ("auto", "hist", "radix"):
+            raise ValueError(f"unknown select {select!r}")
+        if select == "hist" and not hist_ok:
+            raise ValueError("select='hist' needs <= 4 query heads per KV head and <= 65536 tokens")
+        self.select = "radix" if select == "auto" else select
+        if self.fused:
+            self.kernels = ("retrieve",)
+        elif self.select == "hist":
+            self.kernels = ("score_hist", "topk_hist", "attn_partial", "attn_merge")
+        else:
+            self.kernels = ("score", "topk", "attn_partial", "attn_merge")
         if use_graph:
             self.recapture()
 
@@ -107,10 +126,8 @@ class SparseAttentionStep:
                 ptr(self.current_keys), ptr(self.current_values), self.budget, ptr(self.output),
                 None, ptr(self.indices), s))
             return
-        # Query encoding runs in the score kernel's prologue, which also builds the
-        # top-k's first radix histogram; the top-k then needs one CTA per row.
-        hist_ok = QH // KVH <= 4 and self.prefix_tokens <= 65536
-        if hist_ok:
+        # Query encoding runs in the score kernel's prologue.
+        if self.select == "hist":
             check(lib.popkv_score_hist(ptr(self.queries), _lib.dtype_code(self.queries), B, QH,
                                        *(ptr(t) for t in packed), KVH, capacity, ptr(self.head_to_kv),
                                        self.prefix_tokens, self.g, ptr(self.scores), ptr(self.hist), s))

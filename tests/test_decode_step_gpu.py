@@ -13,9 +13,10 @@ from popkv_b200.workloads import decode_inputs, head_to_kv
 pytestmark = pytest.mark.gpu
 
 
+@pytest.mark.parametrize("select", ["hist", "radix"])
 @pytest.mark.parametrize("preset,context,budget", [("popkv-q", 2048, 256), ("popkv-s", 3000, 700),
                                                    ("popkv-normal", 777, 1000)])
-def test_graph_step_matches_oracle(cuda_device, preset, context, budget):
+def test_graph_step_matches_oracle(cuda_device, preset, context, budget, select):
     tg, g = P.POPKV_PRESETS[preset]
     x = decode_inputs(context=context, seed=11, dtype="bf16")
     dev = cuda_device
@@ -23,7 +24,8 @@ def test_graph_step_matches_oracle(cuda_device, preset, context, budget):
     keys, values = to(x.keys[0]), to(x.values[0])
     cache = P.build_popkv_cache(keys, group_size=tg, dim_group_size=g, reserve_tokens=8)
     mapping = torch.from_numpy(head_to_kv(32, 8)).to(dev)
-    step = SparseAttentionStep(cache, keys, values, mapping, budget=budget)
+    step = SparseAttentionStep(cache, keys, values, mapping, budget=budget, select=select)
+    assert step.select == select
     q_host = to(x.queries).cpu().pin_memory()
     k_host = to(x.current_keys[0]).cpu().pin_memory()
     v_host = to(x.current_values[0]).cpu().pin_memory()
@@ -32,8 +34,8 @@ def test_graph_step_matches_oracle(cuda_device, preset, context, budget):
     assert torch.equal(out, again)
     eager = P.popkv_attention(to(x.queries[0]), keys, values, to(x.current_keys[0]),
                               to(x.current_values[0]), cache, mapping, budget=budget)
-    # The graph runs the fused kernel, whose attention sums in another order than the
-    # three-launch chain: equal up to bf16 output rounding.
+    # The graph's attention kernels sum in another order than the eager chain:
+    # equal up to bf16 output rounding.
     assert (out[0].float() - eager.float()).abs().max().item() <= 2 ** -6
 
     kbits, qbits = x.bits("keys")[0], x.bits("queries")

@@ -388,7 +388,8 @@ def test_partial_merge_single_launch_matches_two_launches(cuda_device, valid):
 
 
 @pytest.mark.parametrize("g", GROUPS)
-@pytest.mark.parametrize("tokens,budget", [(32768, 4096), (3000, 256), (100, 1000), (65536, 4096)])
+@pytest.mark.parametrize("tokens,budget", [(32768, 4096), (3000, 256), (100, 1000), (65536, 4096),
+                                           (777, 500)])
 def test_score_hist_and_topk_hist_match_separate_kernels(cuda_device, g, tokens, budget):
     """popkv_score_hist + popkv_topk_hist == popkv_score + popkv_topk, and the histogram is re-zeroed."""
     from popkv_b200 import _lib
@@ -406,7 +407,6 @@ def test_score_hist_and_topk_hist_match_separate_kernels(cuda_device, g, tokens,
             _lib.ptr(q), _lib.BF16, 1, 32, *(_lib.ptr(t) for t in packed), 8, cap, _lib.ptr(mapping),
             tokens, g, _lib.ptr(scores), _lib.ptr(hist), _lib.stream_of(cuda_device)))
         torch.cuda.synchronize()
-        key = scores.view(torch.int16).to(torch.int32) & 0xFFFF
         assert int(hist.sum()) == 32 * tokens
         _lib.check(_lib.lib().popkv_topk_hist(
             _lib.ptr(scores), _lib.ptr(hist), 32, tokens, tokens, k, tokens, _lib.ptr(idx), k + 1,
