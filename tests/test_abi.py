@@ -116,3 +116,29 @@ def test_python_surface_validation_without_gpu():
     assert out[:, -1].tolist() == [11, 11]
     with pytest.raises(NotImplementedError):
         popkv_cuda.update_quest_metadata(keys, keys, keys, page=0)
+
+
+def test_install_as_reference_modules():
+    """The reference's lazy `from popkv_cuda import ...` / `from sparse_kernels import ...` resolve here."""
+    import sys
+    import popkv_b200
+    saved = {n: sys.modules.get(n) for n in ("popkv_cuda", "sparse_kernels")}
+    try:
+        for n in saved:
+            sys.modules.pop(n, None)
+        popkv_b200.install_as_reference_modules()
+        from popkv_cuda import pack_keys, pack_keys_into, query_encode, score_encoded  # noqa: F401
+        from sparse_kernels import (indexed_attention_split_merge,  # noqa: F401
+                                    indexed_attention_split_partial)
+        assert pack_keys is popkv_b200.popkv_cuda.pack_keys
+        assert indexed_attention_split_partial is popkv_b200.sparse_kernels.indexed_attention_split_partial
+        popkv_b200.install_as_reference_modules()  # idempotent
+        sys.modules["popkv_cuda"] = type(sys)("popkv_cuda")
+        with pytest.raises(RuntimeError, match="already imported"):
+            popkv_b200.install_as_reference_modules()
+    finally:
+        for n, m in saved.items():
+            if m is None:
+                sys.modules.pop(n, None)
+            else:
+                sys.modules[n] = m
