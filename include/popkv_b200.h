@@ -215,6 +215,40 @@ POPKV_API int popkv_attn_partial_merge(
     int32_t* counters, void* out, int out_dtype, void* stream);
 
 /*
+ * popkv_attn_partial_merge with its scratch in a fixed device array of the
+ * library instead of caller buffers: the call allocates no memory (no
+ * cudaMalloc / cudaFree, no allocator of the caller).  No counterpart in the
+ * reference, whose split attention allocates its partials with torch on every
+ * call (sparse_kernels.py:321-364).
+ *
+ * For callers that cannot allocate device memory at the point of the call: a
+ * C, Go or Java host that binds only this C ABI and owns no device allocator,
+ * and serving loops whose device memory is already reserved up front for the
+ * KV cache (there may be no free memory left), where a cudaMalloc / cudaFree
+ * pair per token would also synchronise the device.
+ *
+ * Limits (POPKV_ERR_CAPACITY beyond them, checked before any CUDA call):
+ * batch*q_heads <= 65536 and batch*q_heads*splits*(head_dim + 2) <= 2^20 fp32
+ * (4 MiB), splits = ceil(selected / split_tokens); head_dim <= 256.
+ *
+ * The first call on a device (with that device current) sets up: it looks up
+ * the array's address with cudaGetSymbolAddress and clears the completion
+ * counters with cudaMemset + cudaDeviceSynchronize.  Make that first call
+ * before any stream capture.  Every call leaves the counters zero.  All calls
+ * on one device share the one array: calls that overlap in time (other
+ * streams, other host threads) race on it and must be serialised by the
+ * caller.  Other arguments and results as for popkv_attn_partial_merge.
+ */
+POPKV_API int popkv_attn_partial_merge_static(
+    const void* queries, int queries_dtype, int64_t batch, int64_t q_heads, int64_t head_dim,
+    const void* prefix_keys, const void* prefix_values, int kv_dtype, int64_t kv_heads,
+    int64_t prefix_tokens, int64_t k_batch_stride, int64_t k_head_stride, int64_t k_token_stride,
+    int64_t v_batch_stride, int64_t v_head_stride, int64_t v_token_stride,
+    const void* current_keys, const void* current_values, const int64_t* indices, int64_t selected,
+    const uint8_t* valid, const int64_t* head_to_kv, int64_t split_tokens, void* out, int out_dtype,
+    void* stream);
+
+/*
  * Fused decode-time retrieval for head_dim 128: popcount score of the first
  * `tokens` cached keys, per-head top-(budget-1) with the current slot
  * reserved, sparse attention over the selected rows plus the current token,

@@ -36,6 +36,8 @@ _SIGNATURES = {
     "popkv_attn_merge": ([_P, _L, _L, _L, _P, _I, _P], _I),
     "popkv_attn_partial_merge": ([_P, _I, _L, _L, _L, _P, _P, _I, _L, _L, _L, _L, _L, _L, _L, _L,
                                   _P, _P, _P, _L, _P, _P, _L, _P, _P, _P, _I, _P], _I),
+    "popkv_attn_partial_merge_static": ([_P, _I, _L, _L, _L, _P, _P, _I, _L, _L, _L, _L, _L, _L, _L, _L,
+                                         _P, _P, _P, _L, _P, _P, _L, _P, _I, _P], _I),
     "popkv_retrieve": ([_P, _I, _L, _L, _L, _P, _P, _P, _P, _L, _L, _L, _L, _L, _P, _P, _P, _I,
                         _L, _L, _L, _L, _L, _L, _P, _P, _L, _P, _P, _P, _P], _I),
 }

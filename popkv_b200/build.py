@@ -19,7 +19,8 @@ CSRC = PACKAGE / "csrc"
 INCLUDE = ROOT / "include"
 LIB_DIR = PACKAGE / "lib"
 LIB_PATH = LIB_DIR / "libpopkv_b200.so"
-SOURCES = ("abi.cu", "pack.cu", "score.cu", "topk.cu", "attention.cu", "retrieve.cu")
+SOURCES = ("abi.cu", "pack.cu", "score.cu", "topk.cu", "attention.cu", "attention_static.cu",
+           "retrieve.cu")
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
