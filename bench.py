@@ -60,6 +60,8 @@ def parse_args(argv=None):
     p.add_argument("--no-graph", action="store_true", help="launch eagerly instead of a CUDA graph")
     p.add_argument("--select", choices=("auto", "hist", "radix"), default="radix",
                    help="top-k path of the step (hist: score kernel builds the first radix histogram)")
+    p.add_argument("--chunks", type=int, default=1,
+                   help="KV-head chunks pipelined on forked streams inside the step graph")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU baseline sample budget")
     p.add_argument("--stage-reps", type=int, default=50)
@@ -211,7 +213,7 @@ def build_steps(args, layer, copies: int):
             raise SystemExit("batch > 1 benchmarking is not wired yet")
         step = SparseAttentionStep(caches[0], keys, values, layer["mapping"], budget=args.budget,
                                    q_dtype=torch.bfloat16, batch=B, use_graph=not args.no_graph,
-                                   select=args.select)
+                                   select=args.select, chunks=args.chunks)
         step.queries.copy_(layer["queries"])
         step.current_keys.copy_(layer["cur_k"])
         step.current_values.copy_(layer["cur_v"])
@@ -226,8 +228,30 @@ def layer_bytes(args, layer) -> int:
     return args.batch * kv * T * (2 * D * 2 + 32 + 4 * reps)
 
 
-def algorithmic_bytes(args, layer) -> dict:
-    """Bytes each stage must move once (no re-reads), per step of this rank."""
+def union_rows(step) -> int:
+    """Distinct cached rows the step's query heads selected, summed over (batch, KV head).
+
+    The query heads of one KV head read the union of their selections from
+    HBM once (L2 serves the repeats), so the attention's algorithmic bytes
+    count each distinct row once.  The current token's slot is not a cached row.
+    """
+    import torch
+    idx = step.indices
+    B, QH, _ = idx.shape
+    group = QH // step.kv_heads
+    rows = 0
+    for b in range(B):
+        for h in range(step.kv_heads):
+            sel = idx[b, h * group:(h + 1) * group].reshape(-1)
+            rows += int(torch.unique(sel[sel < step.prefix_tokens]).numel())
+    return rows
+
+
+def algorithmic_bytes(args, layer, rows: int) -> dict:
+    """Bytes each stage must move once (no re-reads), per step of this rank.
+
+    `rows` = distinct selected cached rows (union over each KV head's query heads).
+    """
     T, D, B = args.context, 128, args.batch
     kv, qh = layer["kv_local"], layer["q_local"]
     reps = 128 // layer["g"]
@@ -237,7 +261,7 @@ def algorithmic_bytes(args, layer) -> dict:
     meta = B * kv * T * (32 + 4 * reps)
     scores = B * qh * T * 2
     idx = B * qh * sel * 8
-    gathered = B * qh * sel * 2 * D * 2  # each query head reads its own K and V rows
+    gathered = (rows + B * kv) * 2 * D * 2  # distinct K and V rows + the current token's
     partials = B * qh * splits * (D + 2) * 4
     qio = B * qh * D * 2
     return {
@@ -250,8 +274,11 @@ def algorithmic_bytes(args, layer) -> dict:
         "attn_partial": gathered + idx + partials + qio,
         "attn_merge": partials + qio,
         "attn_fused": gathered + idx + 2 * partials + 2 * qio,
-        # §8(d) per-step algorithmic bytes: metadata + gathered rows + indices + q/out.
+        # Per-step algorithmic bytes: metadata + distinct gathered rows + int32
+        # indices + q/out (scores and partials are intermediates).
         "step": meta + gathered + B * qh * sel * 4 + 2 * qio,
+        # The same with every query head's selection counted separately.
+        "step_upper_bound": meta + B * qh * sel * 2 * D * 2 + B * qh * sel * 4 + 2 * qio,
     }
 
 
@@ -323,7 +350,8 @@ def run_ours(args, world, rank, local):
             stages[k]["us"] = float(vec[j].item())
         e2e["value"] = float(vec[-1].item())
     if rank == 0:
-        abytes = algorithmic_bytes(args, layer)
+        rows = union_rows(steps[0])
+        abytes = algorithmic_bytes(args, layer, rows)
         peaks = measured_peaks()
         for name, st in stages.items():
             if name in abytes and st["us"] > 0:
@@ -364,6 +392,8 @@ def run_ours(args, world, rank, local):
             },
             "step_roofline": {
                 "algorithmic_bytes": step_bytes,
+                "distinct_rows": rows,
+                "upper_bound_bytes": abytes["step_upper_bound"],
                 "achieved_gbs": round(step_bytes / (ms_per_step * 1e-3) / 1e9, 1),
                 "frac": round(step_bytes / (ms_per_step * 1e-3) / 1e9 / peaks["hbm_gbs"], 4),
             },

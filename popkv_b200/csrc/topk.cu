@@ -21,6 +21,27 @@
 
 #include "common.cuh"
 
+// Phase timestamps for profiling builds (-DPOPKV_TOPK_TIMING): thread 0 of each
+// CTA of the cluster kernel records %globaltimer at its phase boundaries.
+#ifdef POPKV_TOPK_TIMING
+__device__ unsigned long long g_topk_phase_ns[1024][8];
+#define POPKV_TOPK_PHASE(i)                                                              \
+    do {                                                                                 \
+        if (threadIdx.x == 0 && blockIdx.x < 1024) {                                     \
+            unsigned long long t_;                                                       \
+            asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_));                      \
+            g_topk_phase_ns[blockIdx.x][i] = t_;                                         \
+        }                                                                                \
+    } while (0)
+extern "C" __attribute__((visibility("default"))) int popkv_topk_phase_ns(unsigned long long* host, int ctas) {
+    return static_cast<int>(cudaMemcpyFromSymbol(host, g_topk_phase_ns, sizeof(unsigned long long) * 8 * ctas));
+}
+#else
+#define POPKV_TOPK_PHASE(i) \
+    do {                    \
+    } while (0)
+#endif
+
 namespace popkv {
 namespace {
 
@@ -373,6 +394,7 @@ __global__ void __launch_bounds__(kClusterThreads) topk_cluster_kernel(
     __shared__ unsigned long long sel_above;
     __shared__ unsigned long long cta_totals;  // (gt << 32) | eq of this CTA
 
+    POPKV_TOPK_PHASE(0);
     cg::cluster_group cluster = cg::this_cluster();
     const int rank = static_cast<int>(cluster.block_rank());
     const int64_t row = blockIdx.x / CPR;
@@ -424,6 +446,7 @@ __global__ void __launch_bounds__(kClusterThreads) topk_cluster_kernel(
     constexpr int kPasses = F32 ? 3 : 2;
     uint32_t prefix = 0, prefix_mask = 0;
     unsigned long long above = 0;
+    POPKV_TOPK_PHASE(1);
 #pragma unroll
     for (int p = 0; p < kPasses; ++p) {
         const int shift = p == 0 ? (F32 ? 21 : 5) : (p == 1 ? (F32 ? 10 : 0) : 0);
@@ -440,7 +463,9 @@ __global__ void __launch_bounds__(kClusterThreads) topk_cluster_kernel(
                 if (e < lim[j] && (key & prefix_mask) == prefix)
                     atomicAdd(&hist[(key >> shift) & digit_mask], 1u);
             }
+        if (p == 0) POPKV_TOPK_PHASE(2);
         cluster.sync();  // every CTA's histogram is complete
+        if (p == 0) POPKV_TOPK_PHASE(3);
         const unsigned long long remaining = static_cast<unsigned long long>(k) - above;
         const uint32_t per = (nbins + kClusterThreads - 1) / kClusterThreads;
         uint32_t counts[4];
@@ -473,12 +498,14 @@ __global__ void __launch_bounds__(kClusterThreads) topk_cluster_kernel(
             }
         }
         cluster.sync();  // remote reads done; sel_* visible
+        if (p == 0) POPKV_TOPK_PHASE(4);
         prefix |= sel_bin << shift;
         prefix_mask |= digit_mask << shift;
         above += sel_above;
     }
     const uint32_t threshold = prefix;
     const unsigned long long need = static_cast<unsigned long long>(k) - above;
+    POPKV_TOPK_PHASE(5);
 
     unsigned long long round_counts[CHUNKS];
     unsigned long long mine = 0;
@@ -507,6 +534,7 @@ __global__ void __launch_bounds__(kClusterThreads) topk_cluster_kernel(
         if (tid == 0) scan_sums[kClusterWarps] = t;
     }
     cluster.sync();  // nobody exits while a peer may still read its totals
+    POPKV_TOPK_PHASE(6);
     const unsigned long long carry = scan_sums[kClusterWarps];
     unsigned long long gt_carry = carry >> 32, eq_carry = carry & 0xFFFFFFFFull;
 #pragma unroll
@@ -533,6 +561,7 @@ __global__ void __launch_bounds__(kClusterThreads) topk_cluster_kernel(
         gt_carry += total >> 32;
         eq_carry += total & 0xFFFFFFFFull;
     }
+    POPKV_TOPK_PHASE(7);
 }
 
 template <bool F32, int CPR, int CHUNKS>
@@ -746,6 +775,262 @@ __global__ void __launch_bounds__(kHistThreads) topk_hist_kernel(
     }
 }
 
+// ---------------------------------------------------------------------------
+// fp16 top-k, one thread-block cluster of CPR CTAs per row, three cluster
+// barriers in all.
+//
+// Thread t of rank r owns the contiguous keys [r*S + t*PER, r*S + (t+1)*PER),
+// S = 512*PER, held in registers two to a word.  (1) Every CTA counts its keys'
+// top 11 bits in shared memory; barrier A; every CTA then reads all CPR
+// histograms (one 16-byte DSMEM load per rank and thread: thread t sums the
+// four bins at descending positions 4t..4t+3) and scans them itself, so all
+// CTAs pick the same digit b1 without a further exchange.  (2) The keys of
+// digit b1 are counted by their low 5 bits into a 32-bin histogram; barrier B;
+// warp 0 of every CTA reads the CPR small histograms and picks the threshold
+// key and how many keys equal to it are taken.  (3) A block scan of each
+// thread's (greater, equal) counts gives positions inside the CTA; each CTA
+// stores its totals into the higher ranks' shared memory; barrier C; each CTA
+// adds the totals of the lower ranks and writes its winners in ascending
+// index order.  No DSMEM access follows barrier C, so CTAs exit freely.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t cta_exclusive_scan32(uint32_t x, uint32_t* warp_sums, uint32_t& total) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    uint32_t incl = x;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t y = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+        if (lane >= o) incl += y;
+    }
+    if (lane == 31) warp_sums[warp] = incl;
+    __syncthreads();
+    if (warp == 0) {
+        const uint32_t w = lane < kClusterWarps ? warp_sums[lane] : 0u;
+        uint32_t wi = w;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const uint32_t y = __shfl_up_sync(0xFFFFFFFFu, wi, o);
+            if (lane >= o) wi += y;
+        }
+        if (lane < kClusterWarps) warp_sums[lane] = wi - w;
+        if (lane == kClusterWarps - 1) warp_sums[kClusterWarps] = wi;
+    }
+    __syncthreads();
+    const uint32_t result = warp_sums[warp] + incl - x;
+    total = warp_sums[kClusterWarps];
+    return result;
+}
+
+template <int CPR, int PER>
+__global__ void __launch_bounds__(kClusterThreads) topk16_cluster_kernel(
+    const uint16_t* __restrict__ scores, int64_t tokens, int64_t row_stride, int64_t k,
+    int64_t current_index, int64_t* __restrict__ out, int64_t out_stride, bool vec_ok) {
+    static_assert(PER % 8 == 0 && PER <= 32, "PER keys per thread, whole uint4 loads");
+    constexpr int64_t kSlice = static_cast<int64_t>(kClusterThreads) * PER;
+    __shared__ __align__(16) uint32_t hist[kHistBins];
+    __shared__ uint32_t hist2[32];
+    __shared__ uint32_t warp_sums[kClusterWarps + 1];
+    __shared__ uint32_t lower_totals[CPR];  // packed (gt << 16) | eq of each lower rank
+    __shared__ uint32_t sel_b1, sel_above, sel_thr, sel_need;
+
+    POPKV_TOPK_PHASE(0);
+    cg::cluster_group cluster = cg::this_cluster();
+    const int rank = static_cast<int>(cluster.block_rank());
+    const int64_t row = blockIdx.x / CPR;
+    const int tid = threadIdx.x;
+    int64_t* dst = out + row * out_stride;
+    if (current_index >= 0 && tid == 0 && rank == 0) dst[k] = current_index;
+    if (k <= 0) return;  // uniform across the cluster: no CTA reaches a cluster barrier
+    const uint32_t kk = static_cast<uint32_t>(k);
+
+    for (int b = tid; b < kHistBins; b += kClusterThreads) hist[b] = 0;
+    if (tid < 32) hist2[tid] = 0;
+    if (tid < CPR) lower_totals[tid] = 0;
+    if (tid == 0) {  // defaults; the scans below always overwrite them when k <= tokens
+        sel_b1 = 0;
+        sel_above = 0;
+        sel_thr = 0;
+        sel_need = 0;
+    }
+
+    const int64_t base = static_cast<int64_t>(rank) * kSlice + static_cast<int64_t>(tid) * PER;
+    const uint16_t* src = scores + row * row_stride + base;
+    const int64_t left = tokens - base;
+    const int lim = left <= 0 ? 0 : (left >= PER ? PER : static_cast<int>(left));
+    uint32_t packed[PER / 2];
+    if (vec_ok && lim == PER) {
+#pragma unroll
+        for (int j = 0; j < PER / 8; ++j) {
+            const uint4 v = __ldg(reinterpret_cast<const uint4*>(src) + j);
+            const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+                packed[4 * j + e] = key16(static_cast<uint16_t>(w[e] & 0xFFFFu)) |
+                                    (key16(static_cast<uint16_t>(w[e] >> 16)) << 16);
+        }
+    } else {
+#pragma unroll
+        for (int j = 0; j < PER / 2; ++j) packed[j] = 0;
+#pragma unroll
+        for (int e = 0; e < PER; ++e)
+            if (e < lim) packed[e >> 1] |= key16(src[e]) << (16 * (e & 1));
+    }
+    auto key_of = [&](int e) -> uint32_t { return (packed[e >> 1] >> (16 * (e & 1))) & 0xFFFFu; };
+    POPKV_TOPK_PHASE(1);
+    __syncthreads();  // histograms zeroed
+
+    // (1) top 11 bits.
+#pragma unroll
+    for (int e = 0; e < PER; ++e)
+        if (e < lim) atomicAdd(&hist[key_of(e) >> 5], 1u);
+    POPKV_TOPK_PHASE(2);
+    cluster.sync();  // A: every CTA's histogram is complete
+    POPKV_TOPK_PHASE(3);
+    uint32_t cnt[4] = {0u, 0u, 0u, 0u};
+    {
+        uint4 v[CPR];
+#pragma unroll
+        for (int c = 0; c < CPR; ++c)  // all loads in flight at once
+            v[c] = *reinterpret_cast<const uint4*>(cluster.map_shared_rank(hist, c) + (kHistBins - 4) - 4 * tid);
+#pragma unroll
+        for (int c = 0; c < CPR; ++c) {
+            cnt[0] += v[c].w;  // bin 2047 - 4t (descending position 4t)
+            cnt[1] += v[c].z;
+            cnt[2] += v[c].y;
+            cnt[3] += v[c].x;
+        }
+    }
+    {
+        uint32_t total;
+        uint32_t run = cta_exclusive_scan32(cnt[0] + cnt[1] + cnt[2] + cnt[3], warp_sums, total);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            if (run < kk && run + cnt[q] >= kk) {
+                sel_b1 = static_cast<uint32_t>(kHistBins - 1 - 4 * tid - q);
+                sel_above = run;
+            }
+            run += cnt[q];
+        }
+    }
+    __syncthreads();
+    const uint32_t b1 = sel_b1;
+    POPKV_TOPK_PHASE(4);
+
+    // (2) low 5 bits of the keys in digit b1.
+#pragma unroll
+    for (int e = 0; e < PER; ++e)
+        if (e < lim && (key_of(e) >> 5) == b1) atomicAdd(&hist2[key_of(e) & 31u], 1u);
+    cluster.sync();  // B: every CTA's small histogram is complete
+    if (tid < 32) {
+        uint32_t v[CPR];
+#pragma unroll
+        for (int c = 0; c < CPR; ++c) v[c] = cluster.map_shared_rank(hist2, c)[31 - tid];
+        uint32_t c2 = 0;
+#pragma unroll
+        for (int c = 0; c < CPR; ++c) c2 += v[c];
+        uint32_t incl = c2;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const uint32_t y = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+            if (tid >= o) incl += y;
+        }
+        const uint32_t remaining = kk - sel_above;
+        const uint32_t excl = incl - c2;
+        if (excl < remaining && incl >= remaining) {
+            sel_thr = (b1 << 5) | (31u - static_cast<uint32_t>(tid));
+            sel_need = remaining - excl;
+        }
+    }
+    __syncthreads();
+    const uint32_t thr = sel_thr, need = sel_need;
+    POPKV_TOPK_PHASE(5);
+
+    // (3) positions.
+    uint32_t gt = 0, eq = 0;
+#pragma unroll
+    for (int e = 0; e < PER; ++e) {
+        if (e < lim) {
+            gt += key_of(e) > thr;
+            eq += key_of(e) == thr;
+        }
+    }
+    uint32_t cta_total;
+    const uint32_t excl = cta_exclusive_scan32((gt << 16) | eq, warp_sums, cta_total);
+    if (tid > rank && tid < CPR) *cluster.map_shared_rank(&lower_totals[rank], tid) = cta_total;
+    cluster.sync();  // C: lower ranks' totals have arrived; no DSMEM access after this
+    POPKV_TOPK_PHASE(6);
+    uint32_t gt_before = excl >> 16, eq_before = excl & 0xFFFFu;
+#pragma unroll
+    for (int c = 0; c < CPR; ++c) {  // zero for c >= rank; fields summed apart (no carry between them)
+        gt_before += lower_totals[c] >> 16;
+        eq_before += lower_totals[c] & 0xFFFFu;
+    }
+#pragma unroll
+    for (int e = 0; e < PER; ++e) {
+        if (e >= lim) continue;
+        const uint32_t key = key_of(e);
+        if (key > thr) {
+            const uint32_t pos = gt_before + min(eq_before, need);
+            if (pos < kk) dst[pos] = base + e;
+            ++gt_before;
+        } else if (key == thr) {
+            const uint32_t pos = gt_before + eq_before;
+            if (eq_before < need && pos < kk) dst[pos] = base + e;
+            ++eq_before;
+        }
+    }
+    POPKV_TOPK_PHASE(7);
+}
+
+template <int CPR, int PER>
+int launch_cluster16(const void* scores, int64_t rows, int64_t tokens, int64_t row_stride, int64_t k,
+                     int64_t current_index, int64_t* out, int64_t out_stride, bool vec_ok,
+                     cudaStream_t stream) {
+    cudaLaunchConfig_t config = {};
+    config.gridDim = dim3(static_cast<unsigned>(rows * CPR), 1, 1);
+    config.blockDim = dim3(kClusterThreads, 1, 1);
+    config.dynamicSmemBytes = 0;
+    config.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = CPR;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    config.attrs = attr;
+    config.numAttrs = 1;
+    cudaError_t err = cudaLaunchKernelEx(&config, topk16_cluster_kernel<CPR, PER>,
+                                         static_cast<const uint16_t*>(scores), tokens, row_stride, k,
+                                         current_index, out, out_stride, vec_ok);
+    if (err != cudaSuccess) return fail(POPKV_ERR_CUDA, "popkv_topk: %s", cudaGetErrorString(err));
+    return check_launch("popkv_topk");
+}
+
+// fp16 rows of up to 8 * 512 * 32 keys with 0 < k <= tokens < 2^16 per CTA
+// slice: about one wave of CTAs (rows * CPR near 148), the fewest keys per
+// thread that cover the row.  Returns -1 when the shape does not apply.
+int try_launch_cluster16(const void* scores, int64_t rows, int64_t tokens, int64_t row_stride,
+                         int64_t k, int64_t current_index, int64_t* out, int64_t out_stride,
+                         bool vec_ok, cudaStream_t stream) {
+    if (k <= 0 || k > tokens || rows > 0x7FFFFFF) return -1;
+    int cpr = 1;
+    while (cpr < 8 && rows * cpr * 2 <= 160) cpr *= 2;
+    while (cpr < 8 && tokens > static_cast<int64_t>(cpr) * kClusterThreads * 32) cpr *= 2;
+    int per = 8;
+    while (per < 32 && tokens > static_cast<int64_t>(cpr) * kClusterThreads * per) per *= 2;
+    if (tokens > static_cast<int64_t>(cpr) * kClusterThreads * per) return -1;
+#define POPKV_C16(CPR_, PER_)                                                                      \
+    if (cpr == CPR_ && per == PER_)                                                                \
+        return launch_cluster16<CPR_, PER_>(scores, rows, tokens, row_stride, k, current_index, out, \
+                                            out_stride, vec_ok, stream);
+#define POPKV_C16_CPR(CPR_) POPKV_C16(CPR_, 8) POPKV_C16(CPR_, 16) POPKV_C16(CPR_, 32)
+    POPKV_C16_CPR(1)
+    POPKV_C16_CPR(2)
+    POPKV_C16_CPR(4)
+    POPKV_C16_CPR(8)
+#undef POPKV_C16_CPR
+#undef POPKV_C16
+    return -1;
+}
+
 template <bool F32>
 int launch_topk(const void* scores, int64_t rows, int64_t tokens, int64_t row_stride, int64_t k,
                 int64_t current_index, int64_t* out, int64_t out_stride, cudaStream_t stream) {
@@ -754,6 +1039,11 @@ int launch_topk(const void* scores, int64_t rows, int64_t tokens, int64_t row_st
     const bool vec_ok = aligned(scores, 16) && (row_stride * static_cast<int64_t>(key_bytes)) % 16 == 0;
     const int64_t per_chunk = kTopkThreads * kVec;
     const unsigned grid = static_cast<unsigned>(rows);
+    if constexpr (!F32) {
+        const int st = try_launch_cluster16(scores, rows, tokens, row_stride, k, current_index, out,
+                                            out_stride, vec_ok, stream);
+        if (st >= 0) return st;
+    }
     if (rows <= 0x7FFFFFF && k > 0) {
         const int st = try_launch_cluster<F32>(scores, rows, tokens, row_stride, k, current_index,
                                                out, out_stride, vec_ok, stream);

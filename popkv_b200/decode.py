@@ -38,13 +38,16 @@ class SparseAttentionStep:
             needs <= 4 query heads per KV head and <= 65536 tokens).  "auto" is
             "radix", the faster of the two on B200 at 32K tokens (57.5 vs 62.5
             us per graph-captured step).
+        chunks: split the step into this many KV-head chunks on forked streams
+            so that one chunk's top-k and attention overlap the next chunk's
+            score (batch 1 with the consecutive GQA mapping only).
     """
 
     def __init__(self, cache: PopKVCache, prefix_keys: torch.Tensor, prefix_values: torch.Tensor,
                  head_to_kv: torch.Tensor, *, budget: int, q_heads: int | None = None,
                  q_dtype: torch.dtype = torch.bfloat16, split_tokens: int = 256,
                  batch: int = 1, use_graph: bool = True, fused: bool = False,
-                 select: str = "auto") -> None:
+                 select: str = "auto", chunks: int = 1) -> None:
         if prefix_keys.ndim == 3:
             prefix_keys, prefix_values = prefix_keys[None], prefix_values[None]
         if prefix_keys.stride(-1) != 1 or prefix_values.stride(-1) != 1:
@@ -106,6 +109,16 @@ class SparseAttentionStep:
             self.kernels = ("score_hist", "topk_hist", "attn_partial", "attn_merge")
         else:
             self.kernels = ("score", "topk", "attn_partial", "attn_merge")
+        self.chunks = int(chunks)
+        group = self.q_heads // self.kv_heads
+        standard = torch.equal(self.head_to_kv.cpu(), torch.arange(self.q_heads) // group)
+        if self.chunks < 1 or self.kv_heads % self.chunks:
+            raise ValueError(f"chunks must divide the {self.kv_heads} KV heads")
+        if self.chunks > 1 and (self.fused or self.batch != 1 or not standard):
+            raise ValueError("chunks > 1 needs batch 1, the unfused path and the consecutive GQA mapping")
+        per_chunk_q = self.q_heads // self.chunks
+        self._chunk_map = torch.arange(per_chunk_q, device=dev, dtype=torch.int64) // group
+        self._streams = [torch.cuda.Stream(dev) for _ in range(self.chunks)] if self.chunks > 1 else []
         if use_graph:
             self.recapture()
 
@@ -126,29 +139,69 @@ class SparseAttentionStep:
                 ptr(self.current_keys), ptr(self.current_values), self.budget, ptr(self.output),
                 None, ptr(self.indices), s))
             return
+        if self.chunks == 1:
+            self._launch_chunk(s, 0, KVH)
+            return
+        # KV-head chunks on forked streams: the scores run back to back on the
+        # chunk streams (chunk c waits for chunk c-1's score), and each chunk's
+        # top-k, attention and merge overlap the next chunk's score.
+        fork = torch.cuda.Event()
+        fork.record(stream)
+        prev, done = fork, []
+        per = KVH // self.chunks
+        for c, cs in enumerate(self._streams):
+            cs.wait_event(prev)
+            scored = torch.cuda.Event()
+            self._launch_chunk(ctypes_stream(cs), c * per, (c + 1) * per, scored_event=(scored, cs))
+            prev = scored
+            end = torch.cuda.Event()
+            end.record(cs)
+            done.append(end)
+        for end in done:
+            stream.wait_event(end)
+
+    def _launch_chunk(self, s, h0: int, h1: int, scored_event=None) -> None:
+        """Score, select and attend for KV heads [h0, h1) (all of them when unchunked)."""
+        lib, check, ptr = _lib.lib(), _lib.check, _lib.ptr
+        B, KVH = self.batch, h1 - h0
+        group = self.q_heads // self.kv_heads
+        q0, q1 = h0 * group, h1 * group
+        QH = q1 - q0
+        packed = [t[h0:h1] for t in self.cache.packed]
+        capacity = int(packed[0].shape[1])
+        pk, pv = self.prefix_keys[:, h0:h1], self.prefix_values[:, h0:h1]
+        ck, cv = self.current_keys[:, h0:h1], self.current_values[:, h0:h1]
+        queries = self.queries[:, q0:q1]
+        scores, indices = self.scores[:, q0:q1], self.indices[:, q0:q1]
+        partials, output = self.partials[:, q0:q1], self.output[:, q0:q1]
+        mapping = self.head_to_kv if (h0, h1) == (0, self.kv_heads) else self._chunk_map
         # Query encoding runs in the score kernel's prologue.
         if self.select == "hist":
-            check(lib.popkv_score_hist(ptr(self.queries), _lib.dtype_code(self.queries), B, QH,
-                                       *(ptr(t) for t in packed), KVH, capacity, ptr(self.head_to_kv),
-                                       self.prefix_tokens, self.g, ptr(self.scores), ptr(self.hist), s))
-            check(lib.popkv_topk_hist(ptr(self.scores), ptr(self.hist), B * QH, self.prefix_tokens,
+            hist = self.hist[q0:q1]
+            check(lib.popkv_score_hist(ptr(queries), _lib.dtype_code(queries), B, QH,
+                                       *(ptr(t) for t in packed), KVH, capacity, ptr(mapping),
+                                       self.prefix_tokens, self.g, ptr(scores), ptr(hist), s))
+            if scored_event is not None:
+                scored_event[0].record(scored_event[1])
+            check(lib.popkv_topk_hist(ptr(scores), ptr(hist), B * QH, self.prefix_tokens,
                                       self.prefix_tokens, self.k, self.prefix_tokens,
-                                      ptr(self.indices), self.selected, s))
+                                      ptr(indices), self.selected, s))
         else:
-            check(lib.popkv_score(ptr(self.queries), _lib.dtype_code(self.queries), B, QH, 128,
-                                  *(ptr(t) for t in packed), KVH, capacity, ptr(self.head_to_kv),
-                                  self.prefix_tokens, self.g, ptr(self.scores), _lib.F16, s))
-            check(lib.popkv_topk(ptr(self.scores), _lib.F16, B * QH, self.prefix_tokens,
-                                 self.prefix_tokens, self.k, self.prefix_tokens, ptr(self.indices),
+            check(lib.popkv_score(ptr(queries), _lib.dtype_code(queries), B, QH, 128,
+                                  *(ptr(t) for t in packed), KVH, capacity, ptr(mapping),
+                                  self.prefix_tokens, self.g, ptr(scores), _lib.F16, s))
+            if scored_event is not None:
+                scored_event[0].record(scored_event[1])
+            check(lib.popkv_topk(ptr(scores), _lib.F16, B * QH, self.prefix_tokens,
+                                 self.prefix_tokens, self.k, self.prefix_tokens, ptr(indices),
                                  self.selected, s))
         check(lib.popkv_attn_partial(
-            ptr(self.queries), _lib.dtype_code(self.queries), B, QH, 128, ptr(pk), ptr(pv),
+            ptr(queries), _lib.dtype_code(queries), B, QH, 128, ptr(pk), ptr(pv),
             _lib.dtype_code(pk), KVH, self.prefix_tokens, pk.stride(0), pk.stride(1), pk.stride(2),
-            pv.stride(0), pv.stride(1), pv.stride(2), ptr(self.current_keys),
-            ptr(self.current_values), ptr(self.indices), self.selected, None, ptr(self.head_to_kv),
-            self.split_tokens, ptr(self.partials), s))
-        check(lib.popkv_attn_merge(ptr(self.partials), B * QH, self.splits, 128, ptr(self.output),
-                                   _lib.dtype_code(self.output), s))
+            pv.stride(0), pv.stride(1), pv.stride(2), ptr(ck), ptr(cv), ptr(indices), self.selected,
+            None, ptr(mapping), self.split_tokens, ptr(partials), s))
+        check(lib.popkv_attn_merge(ptr(partials), B * QH, self.splits, 128, ptr(output),
+                                   _lib.dtype_code(output), s))
 
     def recapture(self) -> None:
         """(Re)build the CUDA graph of the step's launches for the current buffers."""

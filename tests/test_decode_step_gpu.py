@@ -103,3 +103,38 @@ def test_fused_retrieve_zero_context(cuda_device):
     out = P.popkv_retrieve(q, cache.packed, cache_keys, cache_keys, ck, cv, mapping, tokens=0,
                            budget=16, dim_group_size=64)
     torch.testing.assert_close(out[0].float(), cv[mapping].float(), atol=0, rtol=0)
+
+
+@pytest.mark.parametrize("chunks", [2, 4, 8])
+@pytest.mark.parametrize("select", ["radix", "hist"])
+def test_chunked_step_equals_unchunked(cuda_device, chunks, select):
+    """KV-head chunks on forked streams compute exactly what the single chain computes."""
+    x = decode_inputs(context=5000, seed=3, dtype="bf16")
+    dev = cuda_device
+    to = lambda a: torch.from_numpy(a).to(torch.bfloat16).to(dev)  # noqa: E731
+    keys, values = to(x.keys[0]), to(x.values[0])
+    tg, g = P.POPKV_PRESETS["popkv-q"]
+    cache = P.build_popkv_cache(keys, group_size=tg, dim_group_size=g, reserve_tokens=8)
+    mapping = torch.from_numpy(head_to_kv(32, 8)).to(dev)
+    q, ck, cv = to(x.queries), to(x.current_keys[0]), to(x.current_values[0])
+    one = SparseAttentionStep(cache, keys, values, mapping, budget=700, select=select)
+    want = one(q, ck, cv).clone()
+    many = SparseAttentionStep(cache, keys, values, mapping, budget=700, select=select, chunks=chunks)
+    for _ in range(2):
+        got = many(q, ck, cv).clone()
+        torch.cuda.synchronize()
+        assert torch.equal(many.indices, one.indices)
+        assert torch.equal(got, want)
+    eager = many.run_eager().clone()
+    assert torch.equal(eager, want)
+
+
+def test_chunked_step_rejects_unsupported(cuda_device):
+    dev = cuda_device
+    keys = torch.randn(8, 512, 128, device=dev).to(torch.bfloat16)
+    cache = P.build_popkv_cache(keys, group_size=64, dim_group_size=64, reserve_tokens=0)
+    mapping = torch.from_numpy(head_to_kv(32, 8)).to(dev)
+    with pytest.raises(ValueError, match="divide"):
+        SparseAttentionStep(cache, keys, keys, mapping, budget=64, chunks=3, use_graph=False)
+    with pytest.raises(ValueError, match="consecutive"):
+        SparseAttentionStep(cache, keys, keys, mapping.flip(0), budget=64, chunks=2, use_graph=False)

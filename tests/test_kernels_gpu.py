@@ -222,6 +222,20 @@ def test_topk_matches_oracle(cuda_device, tokens, dtype):
         assert torch.all(got[:, k] == tokens)
 
 
+@pytest.mark.parametrize("rows,tokens", [(1, 131072), (3, 65536), (32, 32768), (64, 8191), (200, 777)])
+def test_topk_all_equal_and_row_counts(cuda_device, rows, tokens):
+    """Every key equal (all winners are ties, taken in index order) and many cluster shapes."""
+    gen = torch.Generator().manual_seed(rows)
+    flat = torch.full((rows, tokens), 0.5, dtype=torch.float16, device=cuda_device)
+    mixed = _tie_heavy_scores(gen, rows, tokens, levels=2).half().to(cuda_device)
+    for scores in (flat, mixed):
+        for k in sorted({1, tokens // 3, tokens - 1, tokens}):
+            got = C.topk(scores, k, current_index=tokens)
+            want = oracle.topk(bits(scores), k)
+            np.testing.assert_array_equal(got[:, :k].cpu().numpy(), want)
+            assert torch.all(got[:, k] == tokens)
+
+
 def test_topk_special_values(cuda_device):
     vals = [0.0, -0.0, 1.0, -1.0, float("inf"), float("-inf"), float("nan"), 65504.0, -65504.0,
             6e-8, -6e-8, 0.0, -0.0, 1.0]
