@@ -324,6 +324,8 @@ __global__ void __launch_bounds__(kAttnThreads, 4) attn_partial_pipe_kernel(
     OT* __restrict__ merged) {
     extern __shared__ __align__(16) unsigned char ring[];  // [stage][K|V][32 rows][256 B]
     POPKV_ATTN_PHASE(0);
+    pdl_wait();
+    pdl_launch_dependents();
     __shared__ float s_m[kAttnThreads / 32], s_s[kAttnThreads / 32];
     __shared__ float s_acc[kAttnThreads / 32][8][16];
 
@@ -626,6 +628,8 @@ __global__ void attn_merge_kernel(const float* __restrict__ partials, int64_t sp
     __shared__ float s_w[kMergeMaxSplits];
     __shared__ float s_red[32];
     __shared__ float s_den;
+    pdl_wait();
+    pdl_launch_dependents();
     const int64_t row = blockIdx.x;
     const int64_t state = head_dim + 2;
     const float* p = partials + row * splits * state;
@@ -686,12 +690,15 @@ int launch_partial(const void* queries, int64_t batch, int64_t q_heads, int64_t 
         constexpr size_t ring_bytes = static_cast<size_t>(kPipeStages) * 2 * kPipeRows * kRowBytes;
         const int st = allow_dynamic_smem(attn_partial_pipe_kernel<QT, KT, void>, static_cast<int>(ring_bytes));
         if (st != POPKV_OK) return st;
-        attn_partial_pipe_kernel<QT, KT, void><<<grid, kAttnThreads, ring_bytes, stream>>>(
+        const cudaError_t err = launch_pdl(
+            attn_partial_pipe_kernel<QT, KT, void>, grid, dim3(kAttnThreads), ring_bytes, stream, 1,
             static_cast<const QT*>(queries), static_cast<const KT*>(pk), static_cast<const KT*>(pv),
             static_cast<const KT*>(ck), static_cast<const KT*>(cv), indices, valid, head_to_kv,
             partials, static_cast<int>(q_heads), static_cast<int>(kv_heads), prefix_tokens, kbs,
             khs, kts, vbs, vhs, vts, selected, split_tokens, static_cast<int>(splits), scale,
-            nullptr, nullptr);
+            static_cast<int*>(nullptr), static_cast<void*>(nullptr));
+        if (err != cudaSuccess)
+            return fail(POPKV_ERR_CUDA, "popkv_attn_partial: %s", cudaGetErrorString(err));
     } else if (vec_ok) {
         attn_partial128_kernel<QT, KT><<<grid, kAttnThreads, 0, stream>>>(
             static_cast<const QT*>(queries), static_cast<const KT*>(pk), static_cast<const KT*>(pv),
@@ -835,15 +842,18 @@ extern "C" int popkv_attn_merge(const float* partials, int64_t rows, int64_t spl
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     const unsigned threads = head_dim >= 128 ? 128 : 32 * static_cast<unsigned>((head_dim + 31) / 32);
     const int d = static_cast<int>(head_dim);
+    const dim3 grid(static_cast<unsigned>(rows)), block(threads);
+    cudaError_t err;
     if (out_dtype == POPKV_DTYPE_F32)
-        attn_merge_kernel<float><<<static_cast<unsigned>(rows), threads, 0, s>>>(partials, splits, d,
-                                                                                 static_cast<float*>(out));
+        err = launch_pdl(attn_merge_kernel<float>, grid, block, 0, s, 1, partials, splits, d,
+                         static_cast<float*>(out));
     else if (out_dtype == POPKV_DTYPE_F16)
-        attn_merge_kernel<__half><<<static_cast<unsigned>(rows), threads, 0, s>>>(partials, splits, d,
-                                                                                  static_cast<__half*>(out));
+        err = launch_pdl(attn_merge_kernel<__half>, grid, block, 0, s, 1, partials, splits, d,
+                         static_cast<__half*>(out));
     else
-        attn_merge_kernel<__nv_bfloat16><<<static_cast<unsigned>(rows), threads, 0, s>>>(
-            partials, splits, d, static_cast<__nv_bfloat16*>(out));
+        err = launch_pdl(attn_merge_kernel<__nv_bfloat16>, grid, block, 0, s, 1, partials, splits, d,
+                         static_cast<__nv_bfloat16*>(out));
+    if (err != cudaSuccess) return fail(POPKV_ERR_CUDA, "popkv_attn_merge: %s", cudaGetErrorString(err));
     return check_launch("popkv_attn_merge");
 }
 

@@ -39,6 +39,45 @@ int allow_dynamic_smem(Kernel kernel, int bytes) {
     return POPKV_OK;
 }
 
+// ---------------------------------------------------------------------------
+// Programmatic dependent launch (PDL) between the kernels of a decode step.
+// A kernel launched with launch_pdl may start while the previous kernel on the
+// stream is finishing; it calls pdl_wait() before its first global memory
+// access, which returns once the previous grid has completed and its writes
+// are visible.  pdl_launch_dependents() lets the next kernel start early.
+// Both are no-ops for a plain launch.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// cudaLaunchKernelEx with programmatic stream serialization (and a 1-D
+// cluster when cluster_x > 1).
+template <typename... ExpTypes, typename... ActTypes>
+cudaError_t launch_pdl(void (*kernel)(ExpTypes...), dim3 grid, dim3 block, size_t smem,
+                       cudaStream_t stream, unsigned cluster_x, ActTypes&&... args) {
+    cudaLaunchConfig_t config = {};
+    config.gridDim = grid;
+    config.blockDim = block;
+    config.dynamicSmemBytes = smem;
+    config.stream = stream;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    int n = 1;
+    if (cluster_x > 1) {
+        attr[1].id = cudaLaunchAttributeClusterDimension;
+        attr[1].val.clusterDim.x = cluster_x;
+        attr[1].val.clusterDim.y = 1;
+        attr[1].val.clusterDim.z = 1;
+        n = 2;
+    }
+    config.attrs = attr;
+    config.numAttrs = n;
+    return cudaLaunchKernelEx(&config, kernel, static_cast<ActTypes&&>(args)...);
+}
+
 inline bool aligned(const void* p, size_t bytes) {
     return (reinterpret_cast<uintptr_t>(p) % bytes) == 0;
 }

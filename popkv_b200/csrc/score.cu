@@ -76,6 +76,7 @@ __global__ void __launch_bounds__(kScoreThreads) score128_kernel(
     __shared__ QueryState<G> states[kMaxGroupHeads];
     __shared__ float scratch[kScoreThreads / 32][2 * 32 * 4];
 
+    pdl_wait();
     const int groups = q_heads / group_heads;
     const int64_t b = blockIdx.y / groups;
     const int grp = blockIdx.y % groups;
@@ -135,6 +136,7 @@ __global__ void __launch_bounds__(kScoreThreads) score128_kernel(
             }
         }
     }
+    pdl_launch_dependents();
     if constexpr (HIST) {
         __syncthreads();
         for (int i = threadIdx.x; i < group_heads * kHistBins11; i += kScoreThreads) {
@@ -214,10 +216,13 @@ int launch_score128_hist(const void* queries, int64_t batch, int64_t q_heads, co
     const int64_t tiles = (tokens + kScoreTile - 1) / kScoreTile;
     dim3 grid(static_cast<unsigned>(tiles), static_cast<unsigned>(batch * kv_heads));
     const size_t smem = sizeof(uint32_t) * kHistBins11 * group_heads;
-    score128_kernel<G, QT, RAW, true><<<grid, kScoreThreads, smem, stream>>>(
-        static_cast<const QT*>(queries), nullptr, nullptr, nullptr, nullptr, k_sign, k_mag, k_low,
-        k_delta, head_to_kv, scores, static_cast<int>(q_heads), group_heads, capacity, tokens,
-        score_scale_for(128), hist);
+    const cudaError_t err = launch_pdl(
+        score128_kernel<G, QT, RAW, true>, grid, dim3(kScoreThreads), smem, stream, 1,
+        static_cast<const QT*>(queries), static_cast<const int32_t*>(nullptr),
+        static_cast<const int32_t*>(nullptr), static_cast<const float*>(nullptr),
+        static_cast<const float*>(nullptr), k_sign, k_mag, k_low, k_delta, head_to_kv, scores,
+        static_cast<int>(q_heads), group_heads, capacity, tokens, score_scale_for(128), hist);
+    if (err != cudaSuccess) return fail(POPKV_ERR_CUDA, "popkv_score_hist: %s", cudaGetErrorString(err));
     return check_launch("popkv_score_hist");
 }
 
@@ -231,10 +236,12 @@ int launch_score128(const void* queries, const int32_t* q_sign, const int32_t* q
     const int group_heads = static_cast<int>(q_heads / kv_heads);
     const int64_t tiles = (tokens + kScoreTile - 1) / kScoreTile;
     dim3 grid(static_cast<unsigned>(tiles), static_cast<unsigned>(batch * kv_heads));
-    score128_kernel<G, QT, RAW><<<grid, kScoreThreads, 0, stream>>>(
+    const cudaError_t err = launch_pdl(
+        score128_kernel<G, QT, RAW, false>, grid, dim3(kScoreThreads), 0, stream, 1,
         static_cast<const QT*>(queries), q_sign, q_mag, q_low, q_delta, k_sign, k_mag, k_low,
         k_delta, head_to_kv, scores, static_cast<int>(q_heads), group_heads, capacity, tokens,
-        score_scale_for(128));
+        score_scale_for(128), static_cast<uint32_t*>(nullptr));
+    if (err != cudaSuccess) return fail(POPKV_ERR_CUDA, "popkv_score: %s", cudaGetErrorString(err));
     return check_launch("popkv_score");
 }
 

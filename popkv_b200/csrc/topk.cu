@@ -833,6 +833,8 @@ __global__ void __launch_bounds__(kClusterThreads) topk16_cluster_kernel(
     __shared__ uint32_t sel_b1, sel_above, sel_thr, sel_need;
 
     POPKV_TOPK_PHASE(0);
+    pdl_wait();
+    pdl_launch_dependents();
     cg::cluster_group cluster = cg::this_cluster();
     const int rank = static_cast<int>(cluster.block_rank());
     const int64_t row = blockIdx.x / CPR;
@@ -985,21 +987,10 @@ template <int CPR, int PER>
 int launch_cluster16(const void* scores, int64_t rows, int64_t tokens, int64_t row_stride, int64_t k,
                      int64_t current_index, int64_t* out, int64_t out_stride, bool vec_ok,
                      cudaStream_t stream) {
-    cudaLaunchConfig_t config = {};
-    config.gridDim = dim3(static_cast<unsigned>(rows * CPR), 1, 1);
-    config.blockDim = dim3(kClusterThreads, 1, 1);
-    config.dynamicSmemBytes = 0;
-    config.stream = stream;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = CPR;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    config.attrs = attr;
-    config.numAttrs = 1;
-    cudaError_t err = cudaLaunchKernelEx(&config, topk16_cluster_kernel<CPR, PER>,
-                                         static_cast<const uint16_t*>(scores), tokens, row_stride, k,
-                                         current_index, out, out_stride, vec_ok);
+    const cudaError_t err = launch_pdl(topk16_cluster_kernel<CPR, PER>,
+                                       dim3(static_cast<unsigned>(rows * CPR)), dim3(kClusterThreads), 0,
+                                       stream, CPR, static_cast<const uint16_t*>(scores), tokens,
+                                       row_stride, k, current_index, out, out_stride, vec_ok);
     if (err != cudaSuccess) return fail(POPKV_ERR_CUDA, "popkv_topk: %s", cudaGetErrorString(err));
     return check_launch("popkv_topk");
 }
