@@ -268,6 +268,7 @@ def algorithmic_bytes(args, layer, rows: int) -> dict:
         "query_encode": qio + B * qh * (32 + 8 * reps),
         "score": meta + scores + B * qh * (32 + 8 * reps),
         "score_fused": meta + scores + qio,
+        "score_tc": meta + scores + qio,
         "score_topk_hist": meta + 2 * scores + qio + idx + 2 * B * qh * 2048 * 4,
         "score_topk_radix": meta + 2 * scores + qio + idx,
         "topk": scores + idx,
@@ -479,6 +480,10 @@ def stage_breakdown(args, layer, steps, device):
         *(ptr(t) for t in st.cache.packed), st.kv_heads, int(st.cache.packed[0].shape[1]),
         ptr(st.head_to_kv), st.prefix_tokens, st.g, ptr(st.scores), s)))
     run("score_fused", lambda st: check(lib.popkv_score(
+        ptr(st.queries), _lib.BF16, B, st.q_heads, 128, *(ptr(t) for t in st.cache.packed),
+        st.kv_heads, int(st.cache.packed[0].shape[1]), ptr(st.head_to_kv), st.prefix_tokens, st.g,
+        ptr(st.scores), _lib.F16, s)))
+    run("score_tc", lambda st: check(lib.popkv_score_tc(
         ptr(st.queries), _lib.BF16, B, st.q_heads, 128, *(ptr(t) for t in st.cache.packed),
         st.kv_heads, int(st.cache.packed[0].shape[1]), ptr(st.head_to_kv), st.prefix_tokens, st.g,
         ptr(st.scores), _lib.F16, s)))

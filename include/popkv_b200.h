@@ -118,6 +118,23 @@ POPKV_API int popkv_score(const void* queries, int queries_dtype, int64_t batch,
                 int64_t dim_group_size, void* scores, int scores_dtype, void* stream);
 
 /*
+ * popkv_score for head_dim 128 on the 5th-generation tensor cores: the four
+ * per-group counts come from int8 matrix products (tcgen05.mma kind::i8,
+ * accumulators in tensor memory) of the key bit planes expanded to +-1/0
+ * bytes against the query coefficients, and the fp32 reconstruction is the
+ * same as popkv_score's, so the scores are bit-identical.  At most 4 query
+ * heads per KV head; POPKV_ERR_UNSUPPORTED otherwise or for other head dims.
+ *
+ * Same interface as popkv_score (and the same reference functions it replaces:
+ * ext.score, csrc/popkv_ext.cu:1208-1313, via popkv_cuda.score).
+ */
+POPKV_API int popkv_score_tc(const void* queries, int queries_dtype, int64_t batch, int64_t q_heads,
+                int64_t head_dim, const int32_t* k_sign, const int32_t* k_mag,
+                const uint16_t* k_low, const uint16_t* k_delta, int64_t kv_heads,
+                int64_t capacity, const int64_t* head_to_kv, int64_t tokens,
+                int64_t dim_group_size, void* scores, int scores_dtype, void* stream);
+
+/*
  * popkv_score plus the first radix pass of the top-k, for head_dim 128 and at
  * most 4 query heads per KV head: besides the fp16 scores it adds, for every
  * query row, the count of scores per top-11-bit key digit into hist

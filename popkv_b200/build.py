@@ -19,7 +19,7 @@ CSRC = PACKAGE / "csrc"
 INCLUDE = ROOT / "include"
 LIB_DIR = PACKAGE / "lib"
 LIB_PATH = LIB_DIR / "libpopkv_b200.so"
-SOURCES = ("abi.cu", "pack.cu", "score.cu", "topk.cu", "attention.cu", "attention_static.cu",
+SOURCES = ("abi.cu", "pack.cu", "score.cu", "score_mma.cu", "topk.cu", "attention.cu", "attention_static.cu",
            "retrieve.cu")
 
 NVCC_FLAGS = [

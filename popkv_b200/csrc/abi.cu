@@ -2,6 +2,7 @@
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
+#include <mutex>
 
 #include "common.cuh"
 
@@ -29,6 +30,41 @@ bool valid_dtype(int dtype) {
 }
 
 size_t dtype_size(int dtype) { return dtype == POPKV_DTYPE_F32 ? 4 : 2; }
+
+int allow_dynamic_smem_impl(const void* kernel, int bytes) {
+    // (kernel, device mask) pairs already configured; a handful of kernels use this.
+    constexpr int kSlots = 64;
+    static std::mutex mutex;
+    static const void* kernels[kSlots] = {};
+    static unsigned long long masks[kSlots] = {};
+    int device = 0;
+    if (cudaGetDevice(&device) != cudaSuccess) return fail(POPKV_ERR_CUDA, "cudaGetDevice failed");
+    const unsigned long long bit = 1ull << (device & 63);
+    std::lock_guard<std::mutex> lock(mutex);
+    int slot = -1;
+    for (int i = 0; i < kSlots; ++i) {
+        if (kernels[i] == kernel) {
+            slot = i;
+            break;
+        }
+        if (kernels[i] == nullptr) {
+            kernels[i] = kernel;
+            slot = i;
+            break;
+        }
+    }
+    if (slot >= 0 && (masks[slot] & bit)) return POPKV_OK;
+    cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (err != cudaSuccess)
+        return fail(POPKV_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(err));
+    // Prefer the largest shared-memory carveout so that several CTAs fit per SM.
+    err = cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                               cudaSharedmemCarveoutMaxShared);
+    if (err != cudaSuccess)
+        return fail(POPKV_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(err));
+    if (slot >= 0) masks[slot] |= bit;  // beyond kSlots kernels: set every call
+    return POPKV_OK;
+}
 
 float score_scale_for(int64_t head_dim) {
     volatile float root = std::sqrt(static_cast<float>(head_dim));

@@ -19,24 +19,14 @@ int check_launch(const char* what);
 bool valid_dtype(int dtype);
 size_t dtype_size(int dtype);
 
-// Raise a kernel's dynamic shared-memory limit once per device (needed above 48 KB).
+// Raise a kernel's dynamic shared-memory limit once per (kernel, device)
+// (needed above 48 KB).  Kernels are told apart by address: instantiations of
+// one template share a function type.
+int allow_dynamic_smem_impl(const void* kernel, int bytes);
+
 template <typename Kernel>
 int allow_dynamic_smem(Kernel kernel, int bytes) {
-    static unsigned long long done_mask = 0;  // bit d: device d configured
-    int device = 0;
-    if (cudaGetDevice(&device) != cudaSuccess) return fail(POPKV_ERR_CUDA, "cudaGetDevice failed");
-    const unsigned long long bit = 1ull << (device & 63);
-    if (__atomic_load_n(&done_mask, __ATOMIC_ACQUIRE) & bit) return POPKV_OK;
-    cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
-    if (err != cudaSuccess)
-        return fail(POPKV_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(err));
-    // Prefer the largest shared-memory carveout so that several CTAs fit per SM.
-    err = cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
-                               cudaSharedmemCarveoutMaxShared);
-    if (err != cudaSuccess)
-        return fail(POPKV_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(err));
-    __atomic_fetch_or(&done_mask, bit, __ATOMIC_RELEASE);
-    return POPKV_OK;
+    return allow_dynamic_smem_impl(reinterpret_cast<const void*>(kernel), bytes);
 }
 
 // ---------------------------------------------------------------------------

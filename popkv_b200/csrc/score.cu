@@ -25,6 +25,7 @@
 
 #include "common.cuh"
 #include "score_impl.cuh"
+#include "score_mma.cuh"
 
 namespace popkv {
 namespace {
@@ -265,6 +266,8 @@ int dispatch_score128(int64_t g, const void* queries, const int32_t* q_sign, con
                                         head_to_kv, tokens, scores, stream);
 }
 
+}  // namespace
+
 int check_score_common(int64_t batch, int64_t q_heads, int64_t kv_heads, int64_t capacity,
                        int64_t tokens, int64_t g, const void* head_to_kv) {
     if (g != 16 && g != 32 && g != 64)
@@ -280,7 +283,6 @@ int check_score_common(int64_t batch, int64_t q_heads, int64_t kv_heads, int64_t
     return POPKV_OK;
 }
 
-}  // namespace
 }  // namespace popkv
 
 extern "C" int popkv_query_encode(const void* queries, int queries_dtype, int64_t rows,

@@ -1,0 +1,515 @@
+// head_dim-128 popcount scorer on the 5th-generation tensor cores (tcgen05,
+// kind::i8, accumulators in tensor memory).
+//
+// The four counts of one (query head, key token, representative group r) are
+// small-integer dot products over the group's G dimensions
+// (csrc/popkv_ext.cu:502-515 forms them with popcounts):
+//   c_sign = sum_d uq(d) uk(d)          c_q  = sum_d [uq qm](d) uk(d)
+//   c_k    = sum_d uq(d) [uk km](d)     c_qk = sum_d [uq qm](d) [uk km](d)
+// with uq, uk = +1 where the sign bit is set and -1 elsewhere, and qm, km the
+// magnitude bits.  So for a tile of 128 key tokens the counts are one int8
+// matrix product per group: A = the tile's [uk | uk*km] bytes (128 x 2G,
+// K-major, expanded from the bit planes into shared memory), B = the query
+// coefficients (16 columns: 4 heads x 4 counts, 2G deep), D = 128 x 16 int32
+// in tensor memory.  Every count is exact; the epilogue then applies the
+// reference's fp32 chain unchanged (fma(ql*kl, c_sign, fma(dq*kl, c_q,
+// fma(ql*dk, c_k, (dq*dk)*c_qk))) summed over r in order, times the scale,
+// rounded to fp16), so the scores equal the popcount kernel's bit for bit.
+//
+// This moves the count work off the popcount pipe, which bounds the popcount
+// kernel, onto the tensor cores.
+#include <cstdint>
+
+#include "common.cuh"
+#include "score_impl.cuh"
+#include "score_mma.cuh"
+
+// Phase timestamps for profiling builds (-DPOPKV_SCORE_TIMING): thread 0 of
+// each CTA records %globaltimer at its phase boundaries (first tile in detail).
+#ifdef POPKV_SCORE_TIMING
+__device__ unsigned long long g_score_phase_ns[1024][8];
+#define POPKV_SCORE_PHASE(i)                                                             \
+    do {                                                                                 \
+        const unsigned cta_ = blockIdx.y * gridDim.x + blockIdx.x;                       \
+        if (threadIdx.x == 0 && cta_ < 1024) {                                           \
+            unsigned long long t_;                                                       \
+            asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_));                      \
+            g_score_phase_ns[cta_][i] = t_;                                              \
+        }                                                                                \
+    } while (0)
+extern "C" __attribute__((visibility("default"))) int popkv_score_phase_ns(unsigned long long* host, int ctas) {
+    return static_cast<int>(cudaMemcpyFromSymbol(host, g_score_phase_ns, sizeof(unsigned long long) * 8 * ctas));
+}
+#else
+#define POPKV_SCORE_PHASE(i) \
+    do {                     \
+    } while (0)
+#endif
+
+namespace popkv {
+namespace {
+
+constexpr int kMmaThreads = 128;  // thread t <-> token row t of the tile <-> TMEM lane t
+constexpr int kMmaTile = 128;     // MMA M
+constexpr int kMmaN = 16;         // 4 query heads x 4 counts
+constexpr int kKBlocks = 8;       // 128 dims x {uk, uk*km} bytes / 32 bytes per MMA
+constexpr int kABlockBytes = kMmaTile * 32;  // one k-block of A: 4 KB
+constexpr int kBBlockBytes = kMmaN * 32;     // one k-block of B: 512 B
+constexpr int kABytes = kKBlocks * kABlockBytes;
+static_assert(kABytes + kKBlocks * kBBlockBytes <= 48 * 1024, "A and B fit the dynamic shared memory");
+// 48 KB of dynamic shared memory (A, B and padding) holds residency at four
+// CTAs per SM, so four 128-column TMEM allocations fill the SM's 512 columns
+// and never wait on each other.
+constexpr size_t kMmaDynSmem = 48 * 1024;
+constexpr uint32_t kTmemCols = 128;
+constexpr int kMaxWaitPolls = 1 << 20;
+
+// ---------------------------------------------------------------------------
+// PTX wrappers.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// Shared-memory matrix descriptor, no swizzle, K-major: core matrices of 8 rows
+// x 16 bytes stored as 128 contiguous bytes; the next 16 bytes along K sit 128
+// bytes on (leading byte offset), the next 8 rows 256 bytes on (stride byte
+// offset).  Bits 46-47 hold the descriptor version (1).
+__device__ __forceinline__ uint64_t kmajor_desc(uint32_t addr) {
+    return static_cast<uint64_t>((addr >> 4) & 0x3FFFu) | (static_cast<uint64_t>(128 >> 4) << 16) |
+           (static_cast<uint64_t>(256 >> 4) << 32) | (1ull << 46);
+}
+
+// Instruction descriptor of kind::i8: s32 accumulator (bits 4-5 = 2), signed
+// A and B (bits 7-9, 10-12 = 1), both K-major, N >> 3 at bit 17, M >> 4 at bit 24.
+constexpr uint32_t kIdesc = (2u << 4) | (1u << 7) | (1u << 10) |
+                            (static_cast<uint32_t>(kMmaN >> 3) << 17) |
+                            (static_cast<uint32_t>(kMmaTile >> 4) << 24);
+
+__device__ __forceinline__ void tmem_alloc(uint32_t* dst, uint32_t cols) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
+                 :: "r"(smem_addr(dst)), "r"(cols) : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t cols) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" :: "r"(taddr), "r"(cols) : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() {
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+// Generic-proxy shared-memory writes become visible to the tensor cores.
+__device__ __forceinline__ void fence_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void mma_i8(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                       uint32_t accumulate) {
+    const uint32_t mask0 = 0, mask1 = 0, mask2 = 0, mask3 = 0;  // no output lane disabled
+    asm volatile(
+        "{\n\t"
+        ".reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t"
+        "}\n"
+        :: "r"(d_tmem), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(mask0), "r"(mask1),
+           "r"(mask2), "r"(mask3)
+        : "memory");
+}
+
+// Arrives on the mbarrier once every MMA this thread issued has completed.
+__device__ __forceinline__ void mma_commit(uint64_t* mbar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
+                 :: "r"(smem_addr(mbar)) : "memory");
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* mbar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" :: "r"(smem_addr(mbar)), "r"(count) : "memory");
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+// Bounded wait for the phase with the given parity; false if it gave up.
+__device__ __forceinline__ bool mbar_wait(uint64_t* mbar, uint32_t parity) {
+    const uint32_t addr = smem_addr(mbar);
+    for (int i = 0; i < kMaxWaitPolls; ++i) {
+        uint32_t done;
+        asm volatile(
+            "{\n\t"
+            ".reg .pred p;\n\t"
+            "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+            "selp.u32 %0, 1, 0, p;\n\t"
+            "}\n"
+            : "=r"(done) : "r"(addr), "r"(parity) : "memory");
+        if (done) return true;
+    }
+    return false;
+}
+
+// 32 consecutive TMEM columns of this warp's 32 lanes: c[j] = column col + j.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&c)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, "
+        "%12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, "
+        "%30, %31}, [%32];"
+        : "=r"(c[0]), "=r"(c[1]), "=r"(c[2]), "=r"(c[3]), "=r"(c[4]), "=r"(c[5]), "=r"(c[6]),
+          "=r"(c[7]), "=r"(c[8]), "=r"(c[9]), "=r"(c[10]), "=r"(c[11]), "=r"(c[12]), "=r"(c[13]),
+          "=r"(c[14]), "=r"(c[15]), "=r"(c[16]), "=r"(c[17]), "=r"(c[18]), "=r"(c[19]),
+          "=r"(c[20]), "=r"(c[21]), "=r"(c[22]), "=r"(c[23]), "=r"(c[24]), "=r"(c[25]),
+          "=r"(c[26]), "=r"(c[27]), "=r"(c[28]), "=r"(c[29]), "=r"(c[30]), "=r"(c[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// Byte offset of (row, 16-byte chunk c16 of a 32-byte k-block row) inside a
+// k-block laid out as described at kmajor_desc.
+__device__ __forceinline__ uint32_t kblock_offset(int row, int c16) {
+    return static_cast<uint32_t>((row >> 3) * 256 + c16 * 128 + (row & 7) * 16);
+}
+
+// Position of the 16 bytes for dims [16q, 16q + 16) of plane p (0: uk, 1: uk*km)
+// in the k-block sequence: group r = 16q / G keeps [uk (G bytes) | uk*km (G
+// bytes)] in k-blocks [r*G/16, (r+1)*G/16).
+template <int G>
+__device__ __forceinline__ void plane_slot(int q, int p, int& kb, int& c16) {
+    const int r = (16 * q) / G;
+    const int li = p * G + (16 * q) % G;  // byte inside the group's 2G bytes
+    kb = r * (G / 16) + li / 32;
+    c16 = (li % 32) / 16;
+}
+
+// One token's packed planes as loaded (R = 128 / G fp16 representatives).
+template <int G>
+struct RawToken {
+    static constexpr int R = 128 / G;
+    uint4 s, m;
+    uint32_t l[R / 2], d[R / 2];
+};
+
+template <int G>
+__device__ __forceinline__ void fetch_token(const uint4* __restrict__ sign4, const uint4* __restrict__ mag4,
+                                            const uint16_t* __restrict__ lowp,
+                                            const uint16_t* __restrict__ deltap, int64_t t, RawToken<G>& rt) {
+    constexpr int R = 128 / G;
+    rt.s = __ldg(sign4 + t);
+    rt.m = __ldg(mag4 + t);
+    if constexpr (R == 8) {
+        const uint4 l4 = __ldg(reinterpret_cast<const uint4*>(lowp) + t);
+        const uint4 d4 = __ldg(reinterpret_cast<const uint4*>(deltap) + t);
+        rt.l[0] = l4.x; rt.l[1] = l4.y; rt.l[2] = l4.z; rt.l[3] = l4.w;
+        rt.d[0] = d4.x; rt.d[1] = d4.y; rt.d[2] = d4.z; rt.d[3] = d4.w;
+    } else if constexpr (R == 4) {
+        const uint2 l2 = __ldg(reinterpret_cast<const uint2*>(lowp) + t);
+        const uint2 d2 = __ldg(reinterpret_cast<const uint2*>(deltap) + t);
+        rt.l[0] = l2.x; rt.l[1] = l2.y;
+        rt.d[0] = d2.x; rt.d[1] = d2.y;
+    } else {
+        rt.l[0] = __ldg(reinterpret_cast<const uint32_t*>(lowp) + t);
+        rt.d[0] = __ldg(reinterpret_cast<const uint32_t*>(deltap) + t);
+    }
+}
+
+// One CTA per (batch, KV head, run of `tiles_per_cta` 128-token tiles); up to
+// four query heads per KV head.
+template <int G, typename QT>
+__global__ void __launch_bounds__(kMmaThreads, 4) score128_mma_kernel(
+    const QT* __restrict__ queries, const int32_t* __restrict__ k_sign, const int32_t* __restrict__ k_mag,
+    const uint16_t* __restrict__ k_low, const uint16_t* __restrict__ k_delta,
+    const int64_t* __restrict__ head_to_kv, uint16_t* __restrict__ scores, int q_heads, int group_heads,
+    int64_t capacity, int64_t tokens, int tiles_per_cta, float scale) {
+    constexpr int R = 128 / G;
+    extern __shared__ __align__(1024) unsigned char mma_smem[];
+    unsigned char* sA = mma_smem;            // kKBlocks x [128 rows x 32 B]
+    unsigned char* sB = mma_smem + kABytes;  // kKBlocks x [16 rows x 32 B]
+    __shared__ QueryState<G> states[4];
+    __shared__ float scratch[4][2 * 32 * 4];
+    __shared__ uint32_t u_table[16], m_table[16];
+    __shared__ __align__(8) uint64_t mbar;
+    __shared__ uint32_t tmem_base;
+    __shared__ int s_failed;
+
+    POPKV_SCORE_PHASE(0);
+    pdl_wait();
+    pdl_launch_dependents();
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int groups = q_heads / group_heads;
+    const int64_t b = blockIdx.y / groups;
+    const int grp = blockIdx.y % groups;
+    const int qh0 = grp * group_heads;
+    const int64_t row0 = b * q_heads + qh0;
+    const int64_t kvh = head_to_kv[qh0];
+
+    if (warp == 0) tmem_alloc(&tmem_base, kTmemCols);
+    if (tid == 0) {
+        mbar_init(&mbar, 1);
+        s_failed = 0;
+    }
+    if (tid < 16) {
+        // A nibble of sign bits -> four int8 lanes of +1 (bit set) / -1; a nibble
+        // of magnitude bits -> 0xFF / 0x00 byte masks.
+        uint32_t u = 0, m = 0;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            u |= (((tid >> j) & 1) ? 0x01u : 0xFFu) << (8 * j);
+            m |= (((tid >> j) & 1) ? 0xFFu : 0x00u) << (8 * j);
+        }
+        u_table[tid] = u;
+        m_table[tid] = m;
+    }
+    if (warp < group_heads)
+        encode_query_row<QT, 4>(queries + (row0 + warp) * 128, 128, G, lane, scratch[warp], states[warp].qs,
+                                states[warp].qm, states[warp].ql, states[warp].dq);
+    __syncthreads();
+
+    // B: thread t fills column n = t / 8 (head n / 4, count n % 4) of k-block t % 8;
+    // each 16-byte half of a k-block row covers 16 consecutive dims of one plane.
+    {
+        const int n = tid >> 3, kb = tid & 7, h = n >> 2, cnt = n & 3;
+        const bool wants_k = cnt >= 2;  // c_k, c_qk pair with uk*km
+        const bool wants_qm = cnt & 1;  // c_q, c_qk use uq*qm
+        const int r = kb / (G / 16);
+        unsigned char* dstB = sB + kb * kBBlockBytes;
+#pragma unroll
+        for (int c16 = 0; c16 < 2; ++c16) {
+            const int li = (kb % (G / 16)) * 32 + 16 * c16;  // byte inside group r
+            const int p = li / G;
+            const int d0 = r * G + li % G;  // first of 16 dims, a multiple of 16
+            uint32_t w[4] = {0u, 0u, 0u, 0u};
+            if (h < group_heads && (p == 1) == wants_k) {
+                const uint32_t qs = states[h].qs[d0 >> 5] >> (d0 & 31);
+                const uint32_t qm = states[h].qm[d0 >> 5] >> (d0 & 31);
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const uint32_t u = u_table[(qs >> (4 * j)) & 15u];
+                    w[j] = wants_qm ? (u & m_table[(qm >> (4 * j)) & 15u]) : u;
+                }
+            }
+            *reinterpret_cast<uint4*>(dstB + kblock_offset(n, c16)) = make_uint4(w[0], w[1], w[2], w[3]);
+        }
+    }
+    if (tid < group_heads) finish_state<G>(states[tid]);
+    fence_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = tmem_base;
+    const uint32_t a_base = smem_addr(sA), b_base = smem_addr(sB);
+
+    const int64_t tiles = (tokens + kMmaTile - 1) / kMmaTile;
+    const int64_t first = static_cast<int64_t>(blockIdx.x) * tiles_per_cta;
+    const uint4* sign4 = reinterpret_cast<const uint4*>(k_sign) + kvh * capacity;
+    const uint4* mag4 = reinterpret_cast<const uint4*>(k_mag) + kvh * capacity;
+    const uint16_t* lowp = k_low + kvh * capacity * R;
+    const uint16_t* deltap = k_delta + kvh * capacity * R;
+    const int row = tid;
+    const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
+    POPKV_SCORE_PHASE(1);
+
+    uint32_t parity = 0;
+    RawToken<G> cur, nxt;
+    if (first < tiles) {
+        const int64_t t0 = first * kMmaTile + row;
+        fetch_token<G>(sign4, mag4, lowp, deltap, t0 < tokens ? t0 : 0, cur);
+    }
+    for (int it = 0; it < tiles_per_cta; ++it) {
+        const int64_t tile = first + it;
+        if (tile >= tiles) break;  // uniform across the CTA
+        const int64_t t = tile * kMmaTile + row;
+        const bool live = t < tokens;
+        if (it + 1 < tiles_per_cta && tile + 1 < tiles) {  // next tile's planes load under this tile
+            const int64_t tn = t + kMmaTile;
+            fetch_token<G>(sign4, mag4, lowp, deltap, tn < tokens ? tn : 0, nxt);
+        }
+        TokenPlanes<G> tp;
+        tp.ks[0] = cur.s.x; tp.ks[1] = cur.s.y; tp.ks[2] = cur.s.z; tp.ks[3] = cur.s.w;
+        tp.km[0] = cur.m.x; tp.km[1] = cur.m.y; tp.km[2] = cur.m.z; tp.km[3] = cur.m.w;
+#pragma unroll
+        for (int j = 0; j < R / 2; ++j) {
+            tp.kl[2 * j] = half_bits_to_float(static_cast<uint16_t>(cur.l[j] & 0xFFFFu));
+            tp.kl[2 * j + 1] = half_bits_to_float(static_cast<uint16_t>(cur.l[j] >> 16));
+            tp.dk[2 * j] = half_bits_to_float(static_cast<uint16_t>(cur.d[j] & 0xFFFFu));
+            tp.dk[2 * j + 1] = half_bits_to_float(static_cast<uint16_t>(cur.d[j] >> 16));
+        }
+        if (it == 0) POPKV_SCORE_PHASE(2);
+
+        // Expand this token's planes into row `row` of A.
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {  // dims [16q, 16q + 16)
+            const uint32_t sw = tp.ks[q >> 1] >> ((q & 1) * 16);
+            const uint32_t mw = tp.km[q >> 1] >> ((q & 1) * 16);
+            uint32_t u[4], w[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                u[j] = live ? u_table[(sw >> (4 * j)) & 15u] : 0u;
+                w[j] = u[j] & m_table[(mw >> (4 * j)) & 15u];
+            }
+            int kb, c16;
+            plane_slot<G>(q, 0, kb, c16);
+            *reinterpret_cast<uint4*>(sA + kb * kABlockBytes + kblock_offset(row, c16)) = make_uint4(u[0], u[1], u[2], u[3]);
+            plane_slot<G>(q, 1, kb, c16);
+            *reinterpret_cast<uint4*>(sA + kb * kABlockBytes + kblock_offset(row, c16)) = make_uint4(w[0], w[1], w[2], w[3]);
+        }
+        fence_async_smem();
+        tc_fence_before();  // previous tile's TMEM reads are ordered before the barrier
+        __syncthreads();
+        if (tid == 0) {
+            tc_fence_after();
+#pragma unroll
+            for (int r = 0; r < R; ++r) {
+#pragma unroll
+                for (int j = 0; j < G / 16; ++j) {
+                    const int kb = r * (G / 16) + j;
+                    mma_i8(tmem + static_cast<uint32_t>(r * kMmaN),
+                           kmajor_desc(a_base + static_cast<uint32_t>(kb * kABlockBytes)),
+                           kmajor_desc(b_base + static_cast<uint32_t>(kb * kBBlockBytes)), kIdesc, j > 0 ? 1u : 0u);
+                }
+            }
+            mma_commit(&mbar);
+        }
+        if (it == 0) POPKV_SCORE_PHASE(3);
+        const bool ok = mbar_wait(&mbar, parity);
+        parity ^= 1u;
+        if (!ok) s_failed = 1;
+        __syncthreads();
+        if (s_failed) break;  // uniform: every thread read the flag after the barrier
+        tc_fence_after();
+        if (it == 0) POPKV_SCORE_PHASE(4);
+
+        float total[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+        for (int r2 = 0; r2 < R; r2 += 2) {  // two groups (32 columns) per TMEM load
+            uint32_t c[32];
+            tmem_ld32(tmem + lane_base + static_cast<uint32_t>(r2 * kMmaN), c);
+#pragma unroll
+            for (int rr = 0; rr < 2; ++rr) {
+                const int r = r2 + rr;
+                const float kl = tp.kl[r], dk = tp.dk[r];
+#pragma unroll
+                for (int h = 0; h < 4; ++h) {
+                    if (h < group_heads) {
+                        const int* cc = reinterpret_cast<const int*>(c) + rr * kMmaN + h * 4;
+                        const float ql = states[h].ql[r], dq = states[h].dq[r];
+                        const float t1 = __fmul_rn(ql, kl);
+                        const float t2 = __fmul_rn(dq, kl);
+                        const float t3 = __fmul_rn(ql, dk);
+                        const float t4 = __fmul_rn(__fmul_rn(dq, dk), small_int_to_float(cc[3]));
+                        const float chain = __fmaf_rn(t1, small_int_to_float(cc[0]),
+                                                      __fmaf_rn(t2, small_int_to_float(cc[1]),
+                                                                __fmaf_rn(t3, small_int_to_float(cc[2]), t4)));
+                        total[h] = __fadd_rn(total[h], chain);
+                    }
+                }
+            }
+        }
+        if (live) {
+#pragma unroll
+            for (int h = 0; h < 4; ++h)
+                if (h < group_heads)
+                    scores[(row0 + h) * tokens + t] = float_to_half_bits(__fmul_rn(total[h], scale));
+        }
+        if (it == 0) POPKV_SCORE_PHASE(5);
+        cur = nxt;
+    }
+    POPKV_SCORE_PHASE(6);
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        tmem_dealloc(tmem, kTmemCols);
+    }
+    POPKV_SCORE_PHASE(7);
+}
+
+template <int G, typename QT>
+int launch_mma(const void* queries, int64_t batch, int64_t q_heads, const int32_t* k_sign,
+               const int32_t* k_mag, const uint16_t* k_low, const uint16_t* k_delta, int64_t kv_heads,
+               int64_t capacity, const int64_t* head_to_kv, int64_t tokens, uint16_t* scores,
+               cudaStream_t stream) {
+    auto kernel = score128_mma_kernel<G, QT>;
+    int st = allow_dynamic_smem(kernel, static_cast<int>(kMmaDynSmem));
+    if (st != POPKV_OK) return st;
+    const int group_heads = static_cast<int>(q_heads / kv_heads);
+    const int64_t tiles = (tokens + kMmaTile - 1) / kMmaTile;
+    const int64_t units = batch * kv_heads;
+    // About one wave of four CTAs per SM: each CTA takes a run of tiles.
+    const int64_t target = 4 * 148;
+    int64_t per = (tiles * units + target - 1) / target;
+    if (per < 1) per = 1;
+    const int64_t ctas_x = (tiles + per - 1) / per;
+    const cudaError_t err = launch_pdl(kernel, dim3(static_cast<unsigned>(ctas_x), static_cast<unsigned>(units)),
+                                       dim3(kMmaThreads), kMmaDynSmem, stream, 1,
+                                       static_cast<const QT*>(queries), k_sign, k_mag, k_low, k_delta,
+                                       head_to_kv, scores, static_cast<int>(q_heads), group_heads, capacity,
+                                       tokens, static_cast<int>(per), score_scale_for(128));
+    if (err != cudaSuccess) return fail(POPKV_ERR_CUDA, "popkv_score: %s", cudaGetErrorString(err));
+    return check_launch("popkv_score");
+}
+
+template <typename QT>
+int dispatch_mma(int64_t g, const void* queries, int64_t batch, int64_t q_heads, const int32_t* k_sign,
+                 const int32_t* k_mag, const uint16_t* k_low, const uint16_t* k_delta, int64_t kv_heads,
+                 int64_t capacity, const int64_t* head_to_kv, int64_t tokens, uint16_t* scores,
+                 cudaStream_t stream) {
+    if (g == 16)
+        return launch_mma<16, QT>(queries, batch, q_heads, k_sign, k_mag, k_low, k_delta, kv_heads,
+                                  capacity, head_to_kv, tokens, scores, stream);
+    if (g == 32)
+        return launch_mma<32, QT>(queries, batch, q_heads, k_sign, k_mag, k_low, k_delta, kv_heads,
+                                  capacity, head_to_kv, tokens, scores, stream);
+    return launch_mma<64, QT>(queries, batch, q_heads, k_sign, k_mag, k_low, k_delta, kv_heads, capacity,
+                              head_to_kv, tokens, scores, stream);
+}
+
+}  // namespace
+
+bool score_mma_applies(int64_t q_heads, int64_t kv_heads, int64_t dim_group_size, int64_t batch,
+                       int64_t tokens) {
+    const int64_t gh = q_heads / kv_heads;
+    return gh >= 1 && gh <= 4 && (dim_group_size == 16 || dim_group_size == 32 || dim_group_size == 64) &&
+           batch * kv_heads <= 65535 && tokens > 0 && (tokens + kMmaTile - 1) / kMmaTile < 0x7FFFFFFFll;
+}
+
+int launch_score_mma(const void* queries, int queries_dtype, int64_t batch, int64_t q_heads,
+                     const int32_t* k_sign, const int32_t* k_mag, const uint16_t* k_low,
+                     const uint16_t* k_delta, int64_t kv_heads, int64_t capacity,
+                     const int64_t* head_to_kv, int64_t tokens, int64_t dim_group_size, uint16_t* scores,
+                     cudaStream_t stream) {
+    if (queries_dtype == POPKV_DTYPE_F32)
+        return dispatch_mma<float>(dim_group_size, queries, batch, q_heads, k_sign, k_mag, k_low, k_delta,
+                                   kv_heads, capacity, head_to_kv, tokens, scores, stream);
+    if (queries_dtype == POPKV_DTYPE_F16)
+        return dispatch_mma<__half>(dim_group_size, queries, batch, q_heads, k_sign, k_mag, k_low, k_delta,
+                                    kv_heads, capacity, head_to_kv, tokens, scores, stream);
+    return dispatch_mma<__nv_bfloat16>(dim_group_size, queries, batch, q_heads, k_sign, k_mag, k_low,
+                                       k_delta, kv_heads, capacity, head_to_kv, tokens, scores, stream);
+}
+
+}  // namespace popkv
+
+extern "C" int popkv_score_tc(const void* queries, int queries_dtype, int64_t batch, int64_t q_heads,
+                              int64_t head_dim, const int32_t* k_sign, const int32_t* k_mag,
+                              const uint16_t* k_low, const uint16_t* k_delta, int64_t kv_heads,
+                              int64_t capacity, const int64_t* head_to_kv, int64_t tokens,
+                              int64_t dim_group_size, void* scores, int scores_dtype, void* stream) {
+    using namespace popkv;
+    if (!valid_dtype(queries_dtype)) return fail(POPKV_ERR_INVALID, "queries must be fp32/fp16/bf16");
+    int st = check_score_common(batch, q_heads, kv_heads, capacity, tokens, dim_group_size, head_to_kv);
+    if (st != POPKV_OK) return st;
+    if (head_dim != 128)
+        return fail(POPKV_ERR_UNSUPPORTED, "popkv_score_tc: head_dim must be 128");
+    if (scores_dtype != POPKV_DTYPE_F16) return fail(POPKV_ERR_INVALID, "head_dim 128 scores are fp16");
+    if (!score_mma_applies(q_heads, kv_heads, dim_group_size, batch, tokens))
+        return fail(POPKV_ERR_UNSUPPORTED, "popkv_score_tc: at most 4 query heads per KV head");
+    if (batch == 0) return POPKV_OK;
+    if (!queries || !k_sign || !k_mag || !k_low || !k_delta || !scores)
+        return fail(POPKV_ERR_INVALID, "popkv_score_tc: null pointer");
+    if (!aligned(k_sign, 16) || !aligned(k_mag, 16) || !aligned(k_low, 16) || !aligned(k_delta, 16))
+        return fail(POPKV_ERR_INVALID, "packed planes must be 16-byte aligned");
+    return launch_score_mma(queries, queries_dtype, batch, q_heads, k_sign, k_mag, k_low, k_delta, kv_heads,
+                            capacity, head_to_kv, tokens, dim_group_size, static_cast<uint16_t*>(scores),
+                            static_cast<cudaStream_t>(stream));
+}

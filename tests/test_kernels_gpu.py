@@ -192,6 +192,34 @@ def test_scores_match_reference_golden(cuda_device, golden, g, dim):
     np.testing.assert_allclose(got.float().cpu().numpy(), golden[f"score/{tag}"], atol=0.15, rtol=0.025)
 
 
+@pytest.mark.parametrize("g", GROUPS)
+@pytest.mark.parametrize("batch,tokens,group_heads,qdtype", [
+    (1, 1, 4, torch.bfloat16), (1, 127, 4, torch.bfloat16), (2, 129, 2, torch.float16),
+    (1, 4097, 1, torch.float32), (3, 1000, 4, torch.bfloat16), (1, 32768, 4, torch.bfloat16)])
+def test_tensor_core_score_matches_popcount_kernel(cuda_device, g, batch, tokens, group_heads, qdtype):
+    """popkv_score_tc (tcgen05 int8 counts) == popkv_score_encoded (popcounts), bit for bit."""
+    keys, q, mapping, packed = _score_case(cuda_device, g, batch, tokens, q_heads=2 * group_heads,
+                                           kv_heads=2, seed=tokens + 7 * g, qdtype=qdtype)
+    mma = C.score(q, packed, head_to_kv=mapping, tokens=tokens, dim_group_size=g, kernel="tensor_core")
+    enc = C.query_encode(q, dim_group_size=g)
+    popc = C.score_encoded(enc, packed, head_to_kv=mapping, tokens=tokens, dim_group_size=g)
+    assert torch.equal(mma.view(torch.int16), popc.view(torch.int16))
+    if tokens <= 1000:
+        arr, tag = to_oracle(q)
+        penc = oracle.query_encode(arr, tag, dim_group_size=g)
+        _, want = oracle.score(penc, planes_to_numpy(packed), head_to_kv=mapping.cpu().numpy(),
+                               tokens=tokens, dim_group_size=g, head_dim=128)
+        np.testing.assert_array_equal(bits(mma), want)
+
+
+def test_tensor_core_score_rejects_unsupported(cuda_device):
+    keys, q, mapping, packed = _score_case(cuda_device, 16, 1, 64, q_heads=16, kv_heads=2, seed=1)
+    with pytest.raises(RuntimeError, match="at most 4 query heads"):
+        C.score(q, packed, head_to_kv=mapping, tokens=64, dim_group_size=16, kernel="tensor_core")
+    with pytest.raises(ValueError, match="kernel must be"):
+        C.score(q, packed, head_to_kv=mapping, tokens=64, dim_group_size=16, kernel="mma")
+
+
 def test_score_dim_kernel_variants_agree(cuda_device):
     """g64-u32 and g64-u64 name the same arithmetic (reference test :320-331)."""
     keys, q, mapping, packed = _score_case(cuda_device, 64, 1, 257, seed=33)
