@@ -44,6 +44,17 @@ UNIT = "ms"
 # PopKV-Q at 32K, budget 4096, per token over 30 sparse layers:
 # score 1.365 + top-k 1.814 + partial 3.600 + merge 0.143 = 6.922 ms -> per layer.
 PUBLISHED_MS_PER_LAYER = (1.365 + 1.814 + 3.600 + 0.143) / 30.0
+
+# DRAM traffic per launch (dram__bytes_read.sum + dram__bytes_write.sum) of the
+# step's kernels at the default workload, from one ncu --set full capture of
+# this script (profiles/score128_popcount_config1.md,
+# profiles/attn_partial_pipe_config1.md, profiles/topk16_cluster_config1.md).
+NCU_TRAFFIC_CONFIG1 = {
+    "score_fused": 16_810_752,
+    "attn_partial": 55_847_168 + 1_044_224,
+    "topk": 2_136_832,
+}
+DEFAULT_WORKLOAD = {"context": 32768, "budget": 4096, "batch": 1, "preset": "popkv-q"}
 L2_BYTES = 126 * 1024 * 1024
 
 
@@ -387,7 +398,9 @@ def run_ours(args, world, rank, local):
             "roofline": {
                 "bound": "hbm", "kernel": dominant,
                 "achieved": dom.get("achieved_gbs"), "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                "frac": dom.get("frac_of_hbm"), "traffic": None,
+                "frac": dom.get("frac_of_hbm"),
+                "traffic": (NCU_TRAFFIC_CONFIG1.get(dominant) if world == 1 and all(
+                    getattr(args, k) == v for k, v in DEFAULT_WORKLOAD.items()) else None),
                 "algorithmic_bytes": dom.get("algorithmic_bytes"),
                 "peak_source": peaks["source"],
             },
