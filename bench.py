@@ -577,24 +577,48 @@ def stage_breakdown(args, layer, steps, device):
 
 
 def end_to_end(args, layer, steps, device, dist, gathered, world):
-    """Same step through the public API with pinned host inputs and a host read of the output."""
-    import torch
-    st = steps[0]
-    q_host = layer["queries"].cpu().pin_memory()
-    k_host = layer["cur_k"].cpu().pin_memory()
-    v_host = layer["cur_v"].cpu().pin_memory()
-    out_shape = (world * st.q_heads, 128) if dist is not None else tuple(st.output.shape)
-    out_host = torch.empty(out_shape, dtype=st.output.dtype).pin_memory()
-    stream = torch.cuda.current_stream(device)
+    """Same step through the public API with pinned host inputs and a host read of the output.
 
-    def e2e_step(i):
-        step = steps[i % len(steps)]
-        out = step(q_host, k_host, v_host)
-        if dist is not None:
-            dist.all_gather_into_tensor(gathered, out.view(step.q_heads, 128))
+    One GPU: a SparseAttentionStep with host_io, whose graph carries the
+    host-to-device copy of q | k | v and the device-to-host copy of the output.
+    Several GPUs: the step, then the all-gather, then the device-to-host copy.
+    """
+    import torch
+    from popkv_b200.decode import SparseAttentionStep
+    st = steps[0]
+    stream = torch.cuda.current_stream(device)
+    if dist is None:
+        # One host_io step per layer copy, cycled like the device-timed steps (> L2).
+        hsteps = []
+        for src in steps:
+            step = SparseAttentionStep(src.cache, src.prefix_keys, src.prefix_values, src.head_to_kv,
+                                       budget=args.budget, q_dtype=torch.bfloat16, batch=args.batch,
+                                       use_graph=not args.no_graph, select=args.select, host_io=True)
+            step.host_queries.copy_(layer["queries"].cpu())
+            step.host_current_keys.copy_(layer["cur_k"].cpu())
+            step.host_current_values.copy_(layer["cur_v"].cpu())
+            hsteps.append(step)
+
+        def e2e_step(i):
+            step = hsteps[i % len(hsteps)]
+            step(step.host_queries, step.host_current_keys, step.host_current_values)
+        h2d = hsteps[0]._in_bytes
+        d2h = hsteps[0].host_output.numel() * hsteps[0].host_output.element_size()
+        api = "popkv_b200.decode.SparseAttentionStep(host_io=True).__call__ (pinned host in/out)"
+    else:
+        q_host = layer["queries"].cpu().pin_memory()
+        k_host = layer["cur_k"].cpu().pin_memory()
+        v_host = layer["cur_v"].cpu().pin_memory()
+        out_host = torch.empty((world * st.q_heads, 128), dtype=st.output.dtype).pin_memory()
+
+        def e2e_step(i):
+            s2 = steps[i % len(steps)]
+            out = s2(q_host, k_host, v_host)
+            dist.all_gather_into_tensor(gathered, out.view(s2.q_heads, 128))
             out_host.copy_(gathered, non_blocking=True)
-        else:
-            out_host.copy_(out, non_blocking=True)
+        h2d = (q_host.numel() + k_host.numel() + v_host.numel()) * 2
+        d2h = out_host.numel() * 2
+        api = "popkv_b200.decode.SparseAttentionStep.__call__ + all_gather (pinned host in/out)"
 
     for i in range(min(args.warmup, 20)):
         e2e_step(i)
@@ -607,10 +631,8 @@ def end_to_end(args, layer, steps, device, dist, gathered, world):
     b.record(stream)
     torch.cuda.synchronize(device)
     ms = a.elapsed_time(b) / n
-    h2d = q_host.numel() * 2 + k_host.numel() * 2 + v_host.numel() * 2
     return {"value": round(ms, 5), "unit": UNIT, "h2d_bytes_per_step": h2d,
-            "d2h_bytes_per_step": out_host.numel() * 2,
-            "api": "popkv_b200.decode.SparseAttentionStep.__call__ (pinned host in/out)"}
+            "d2h_bytes_per_step": d2h, "api": api}
 
 
 def measured_peaks() -> dict:

@@ -38,6 +38,10 @@ class SparseAttentionStep:
             needs <= 4 query heads per KV head and <= 65536 tokens).  "auto" is
             "radix", the faster of the two on B200 at 32K tokens (57.5 vs 62.5
             us per graph-captured step).
+        host_io: keep pinned host staging buffers (``host_queries``,
+            ``host_current_keys``, ``host_current_values``, ``host_output``) and
+            capture their transfers in the graph: one host-to-device copy of
+            q | k | v and one device-to-host copy of the output per replay.
         chunks: split the step into this many KV-head chunks on forked streams
             so that one chunk's top-k and attention overlap the next chunk's
             score (batch 1 with the consecutive GQA mapping only).
@@ -47,7 +51,7 @@ class SparseAttentionStep:
                  head_to_kv: torch.Tensor, *, budget: int, q_heads: int | None = None,
                  q_dtype: torch.dtype = torch.bfloat16, split_tokens: int = 256,
                  batch: int = 1, use_graph: bool = True, fused: bool = False,
-                 select: str = "auto", chunks: int = 1) -> None:
+                 select: str = "auto", chunks: int = 1, host_io: bool = False) -> None:
         if prefix_keys.ndim == 3:
             prefix_keys, prefix_values = prefix_keys[None], prefix_values[None]
         if prefix_keys.stride(-1) != 1 or prefix_values.stride(-1) != 1:
@@ -76,11 +80,20 @@ class SparseAttentionStep:
         reps = 128 // self.g
         dev, B, QH, KVH, D = self.device, self.batch, self.q_heads, self.kv_heads, self.head_dim
         kv_dtype = prefix_keys.dtype
-        # Static inputs / outputs.
-        self.queries = torch.zeros((B, QH, D), device=dev, dtype=q_dtype)
-        self.current_keys = torch.zeros((B, KVH, D), device=dev, dtype=kv_dtype)
-        self.current_values = torch.zeros((B, KVH, D), device=dev, dtype=kv_dtype)
+        # Static inputs (q | current k | current v in one buffer, so one copy
+        # fills them) and output.
+        q_bytes = B * QH * D * torch.finfo(q_dtype).bits // 8
+        kv_bytes = B * KVH * D * torch.finfo(kv_dtype).bits // 8
+        self._in_bytes = q_bytes + 2 * kv_bytes
+        self._inputs = torch.zeros(self._in_bytes, device=dev, dtype=torch.uint8)
+        self.queries, self.current_keys, self.current_values = self._input_views(self._inputs, q_dtype, kv_dtype)
         self.output = torch.zeros((B, QH, D), device=dev, dtype=q_dtype)
+        self.host_io = bool(host_io)
+        if self.host_io:
+            self._host_inputs = torch.zeros(self._in_bytes, dtype=torch.uint8).pin_memory()
+            self.host_queries, self.host_current_keys, self.host_current_values = self._input_views(
+                self._host_inputs, q_dtype, kv_dtype)
+            self.host_output = torch.zeros((B, QH, D), dtype=q_dtype).pin_memory()
         # Intermediates.
         self.q_sign = torch.zeros((B, QH, 4), device=dev, dtype=torch.int32)
         self.q_mag = torch.zeros_like(self.q_sign)
@@ -122,8 +135,26 @@ class SparseAttentionStep:
         if use_graph:
             self.recapture()
 
+    def _input_views(self, buf: torch.Tensor, q_dtype: torch.dtype, kv_dtype: torch.dtype):
+        B, QH, KVH, D = self.batch, self.q_heads, self.kv_heads, self.head_dim
+        q_bytes = B * QH * D * torch.finfo(q_dtype).bits // 8
+        kv_bytes = B * KVH * D * torch.finfo(kv_dtype).bits // 8
+        q = buf[:q_bytes].view(q_dtype).view(B, QH, D)
+        k = buf[q_bytes:q_bytes + kv_bytes].view(kv_dtype).view(B, KVH, D)
+        v = buf[q_bytes + kv_bytes:q_bytes + 2 * kv_bytes].view(kv_dtype).view(B, KVH, D)
+        return q, k, v
+
     # -- launches ---------------------------------------------------------------
     def _launch(self, stream) -> None:
+        if self.host_io:
+            with torch.cuda.stream(stream):
+                self._inputs.copy_(self._host_inputs, non_blocking=True)
+        self._launch_kernels(stream)
+        if self.host_io:
+            with torch.cuda.stream(stream):
+                self.host_output.copy_(self.output, non_blocking=True)
+
+    def _launch_kernels(self, stream) -> None:
         lib, check, ptr = _lib.lib(), _lib.check, _lib.ptr
         s = ctypes_stream(stream)
         B, QH, KVH = self.batch, self.q_heads, self.kv_heads
@@ -231,10 +262,27 @@ class SparseAttentionStep:
 
     def __call__(self, queries: torch.Tensor, current_keys: torch.Tensor,
                  current_values: torch.Tensor) -> torch.Tensor:
-        """Copy the step's inputs (host or device) in, run, return the device output."""
+        """Copy the step's inputs (host or device) in, run, return the output.
+
+        With ``host_io`` and host inputs, the inputs go through the pinned
+        staging buffers (the graph moves them to the device) and the result is
+        ``host_output``, valid once the current stream has been synchronised.
+        Otherwise the result is the device tensor ``output``.
+        """
+        if self.host_io and not queries.is_cuda:
+            for dst, src in ((self.host_queries, queries), (self.host_current_keys, current_keys),
+                             (self.host_current_values, current_values)):
+                if src.data_ptr() != dst.data_ptr():
+                    dst.copy_(src.view_as(dst))
+            self.replay()
+            return self.host_output
         self.queries.copy_(queries.view_as(self.queries), non_blocking=True)
         self.current_keys.copy_(current_keys.view_as(self.current_keys), non_blocking=True)
         self.current_values.copy_(current_values.view_as(self.current_values), non_blocking=True)
+        if self.host_io:  # device inputs: skip the staging copy, keep the output on the device
+            with torch.cuda.device(self.device):
+                self._launch_kernels(torch.cuda.current_stream(self.device))
+            return self.output
         return self.replay()
 
 

@@ -138,3 +138,31 @@ def test_chunked_step_rejects_unsupported(cuda_device):
         SparseAttentionStep(cache, keys, keys, mapping, budget=64, chunks=3, use_graph=False)
     with pytest.raises(ValueError, match="consecutive"):
         SparseAttentionStep(cache, keys, keys, mapping.flip(0), budget=64, chunks=2, use_graph=False)
+
+
+def test_host_io_step_moves_inputs_and_output_in_the_graph(cuda_device):
+    """host_io: the captured graph copies q | k | v in and the output out."""
+    x = decode_inputs(context=3000, seed=21, dtype="bf16")
+    dev = cuda_device
+    to = lambda a: torch.from_numpy(a).to(torch.bfloat16)  # noqa: E731
+    keys, values = to(x.keys[0]).to(dev), to(x.values[0]).to(dev)
+    tg, g = P.POPKV_PRESETS["popkv-s"]
+    cache = P.build_popkv_cache(keys, group_size=tg, dim_group_size=g, reserve_tokens=8)
+    mapping = torch.from_numpy(head_to_kv(32, 8)).to(dev)
+    plain = SparseAttentionStep(cache, keys, values, mapping, budget=500)
+    want = plain(to(x.queries).to(dev), to(x.current_keys[0]).to(dev), to(x.current_values[0]).to(dev)).clone()
+    step = SparseAttentionStep(cache, keys, values, mapping, budget=500, host_io=True)
+    assert step.host_queries.is_pinned() and step.host_output.is_pinned()
+    for _ in range(2):
+        out = step(to(x.queries), to(x.current_keys[0]), to(x.current_values[0]))
+        torch.cuda.synchronize()
+        assert out.data_ptr() == step.host_output.data_ptr()
+        assert torch.equal(out, want.cpu())
+    # Writing the staging views directly, then calling with them, skips the host copy.
+    step.host_queries.copy_(to(x.queries))
+    out = step(step.host_queries, step.host_current_keys, step.host_current_values)
+    torch.cuda.synchronize()
+    assert torch.equal(out, want.cpu())
+    # Device inputs bypass the staging buffers and return the device output.
+    dev_out = step(to(x.queries).to(dev), to(x.current_keys[0]).to(dev), to(x.current_values[0]).to(dev))
+    assert dev_out.is_cuda and torch.equal(dev_out, want)
