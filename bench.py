@@ -71,6 +71,8 @@ def parse_args(argv=None):
     p.add_argument("--no-graph", action="store_true", help="launch eagerly instead of a CUDA graph")
     p.add_argument("--select", choices=("auto", "hist", "radix"), default="radix",
                    help="top-k path of the step (hist: score kernel builds the first radix histogram)")
+    p.add_argument("--gather", choices=("peer", "nccl"), default="peer",
+                   help="N>1: merge fused with the all-gather over NVLink peer memory, or NCCL all-gather")
     p.add_argument("--chunks", type=int, default=1,
                    help="KV-head chunks pipelined on forked streams inside the step graph")
     p.add_argument("--no-cpu-baseline", action="store_true")
@@ -205,7 +207,7 @@ def make_layer(args, world, rank, device):
     return layer
 
 
-def build_steps(args, layer, copies: int):
+def build_steps(args, layer, copies: int, gather=None):
     """`copies` independent layer instances (own cache + metadata), each a captured step."""
     import torch
     from popkv_b200 import popkv as P
@@ -224,7 +226,7 @@ def build_steps(args, layer, copies: int):
             raise SystemExit("batch > 1 benchmarking is not wired yet")
         step = SparseAttentionStep(caches[0], keys, values, layer["mapping"], budget=args.budget,
                                    q_dtype=torch.bfloat16, batch=B, use_graph=not args.no_graph,
-                                   select=args.select, chunks=args.chunks)
+                                   select=args.select, chunks=args.chunks, gather=gather)
         step.queries.copy_(layer["queries"])
         step.current_keys.copy_(layer["cur_k"])
         step.current_values.copy_(layer["cur_v"])
@@ -307,13 +309,17 @@ def run_ours(args, world, rank, local):
     layer = make_layer(args, world, rank, device)
     copies = max(2, math.ceil(3 * L2_BYTES / max(1, layer_bytes(args, layer))))
     copies = min(copies, 16)
-    steps = build_steps(args, layer, copies)
     q_local = layer["q_local"]
+    peer = None
+    if dist is not None and args.gather == "peer":
+        from popkv_b200.sharding import PeerGather
+        peer = PeerGather(args.batch * q_local, torch.bfloat16, device)
+    steps = build_steps(args, layer, copies, gather=peer)
     gathered = torch.empty((world * q_local, 128), device=device, dtype=torch.bfloat16) if dist else None
 
     def one_step(i):
         out = steps[i % copies].replay()
-        if dist is not None:
+        if dist is not None and peer is None:
             dist.all_gather_into_tensor(gathered, out.view(q_local, 128))
         return out
 
@@ -350,7 +356,7 @@ def run_ours(args, world, rank, local):
     ms_per_step = float(total.item()) / args.steps
 
     stages = stage_breakdown(args, layer, steps, device)
-    e2e = end_to_end(args, layer, steps, device, dist, gathered, world)
+    e2e = end_to_end(args, layer, steps, device, dist, gathered, world, peer)
     clocks = sampler.summary(t0, t1)
 
     if dist is not None:
@@ -391,7 +397,9 @@ def run_ours(args, world, rank, local):
                             f"32 q / 8 kv heads, head_dim 128, context {args.context}, budget {args.budget}",
                 "preset": args.preset, "token_group": layer["tg"], "dim_group": layer["g"],
                 "batch": args.batch, "context": args.context, "budget": args.budget,
-                "parallelism": f"kv-head shard x{world}" + (" + NCCL all-gather" if world > 1 else ""),
+                "parallelism": f"kv-head shard x{world}" + ("" if world == 1 else (
+                    " + merge fused with the all-gather over NVLink peer memory" if peer is not None
+                    else " + NCCL all-gather")),
                 "l2": f"steps cycle over {copies} layer copies ({copies * layer_bytes(args, layer) / 2**20:.0f} MiB) > L2",
                 "launch": "eager" if args.no_graph else "CUDA graph per layer step",
             },
@@ -422,6 +430,10 @@ def run_ours(args, world, rank, local):
     for st in steps:
         st.graph = None
     if dist is not None:
+        if peer is not None:
+            if peer.error():
+                print(f"rank {rank}: a peer-gather wait gave up", file=sys.stderr, flush=True)
+            peer.close()
         dist.barrier()
         dist.destroy_process_group()
 
@@ -533,6 +545,8 @@ def stage_breakdown(args, layer, steps, device):
             pv.stride(2), ptr(st.current_keys), ptr(st.current_values), ptr(st.indices), st.selected,
             None, ptr(st.head_to_kv), st.split_tokens, ptr(st.partials), s))
     run("attn_partial", partial)
+    if steps[0].gather is not None:
+        run("attn_merge_gather", lambda st: st.gather.launch(st.partials, st.splits, s))
     run("attn_merge", lambda st: check(lib.popkv_attn_merge(
         ptr(st.partials), B * st.q_heads, st.splits, 128, ptr(st.output), _lib.BF16, s)))
 
@@ -576,24 +590,26 @@ def stage_breakdown(args, layer, steps, device):
     return out
 
 
-def end_to_end(args, layer, steps, device, dist, gathered, world):
+def end_to_end(args, layer, steps, device, dist, gathered, world, peer=None):
     """Same step through the public API with pinned host inputs and a host read of the output.
 
-    One GPU: a SparseAttentionStep with host_io, whose graph carries the
-    host-to-device copy of q | k | v and the device-to-host copy of the output.
-    Several GPUs: the step, then the all-gather, then the device-to-host copy.
+    One GPU, or several with the peer-memory gather: SparseAttentionStep with
+    host_io, whose graph carries the host-to-device copy of q | k | v and the
+    device-to-host copy of the (gathered) output.  Several GPUs with NCCL: the
+    step, then the all-gather, then the device-to-host copy.
     """
     import torch
     from popkv_b200.decode import SparseAttentionStep
     st = steps[0]
     stream = torch.cuda.current_stream(device)
-    if dist is None:
+    if dist is None or peer is not None:
         # One host_io step per layer copy, cycled like the device-timed steps (> L2).
         hsteps = []
         for src in steps:
             step = SparseAttentionStep(src.cache, src.prefix_keys, src.prefix_values, src.head_to_kv,
                                        budget=args.budget, q_dtype=torch.bfloat16, batch=args.batch,
-                                       use_graph=not args.no_graph, select=args.select, host_io=True)
+                                       use_graph=not args.no_graph, select=args.select, host_io=True,
+                                       gather=peer)
             step.host_queries.copy_(layer["queries"].cpu())
             step.host_current_keys.copy_(layer["cur_k"].cpu())
             step.host_current_values.copy_(layer["cur_v"].cpu())
@@ -605,6 +621,8 @@ def end_to_end(args, layer, steps, device, dist, gathered, world):
         h2d = hsteps[0]._in_bytes
         d2h = hsteps[0].host_output.numel() * hsteps[0].host_output.element_size()
         api = "popkv_b200.decode.SparseAttentionStep(host_io=True).__call__ (pinned host in/out)"
+        if peer is not None:
+            api = api.replace("host_io=True", "host_io=True, gather=PeerGather")
     else:
         q_host = layer["queries"].cpu().pin_memory()
         k_host = layer["cur_k"].cpu().pin_memory()

@@ -294,6 +294,49 @@ POPKV_API int popkv_retrieve(
     const void* current_keys, const void* current_values, int64_t budget, void* out,
     uint16_t* scores_out, int64_t* indices_out, void* stream);
 
+/*
+ * Peer memory for the cross-GPU exchange (setup time, not per step).
+ * popkv_peer_alloc: cudaMalloc `bytes` (zeroed) on the current device and
+ * export it: `handle` receives the 64-byte CUDA IPC handle.  popkv_peer_open
+ * maps another process's handle on the current device (peer access enabled
+ * lazily); popkv_peer_close unmaps it; popkv_peer_free frees an allocation of
+ * popkv_peer_alloc.  A process cannot open its own handle.
+ *
+ * No counterpart in the reference, which gathers with NCCL.
+ */
+POPKV_API int popkv_peer_alloc(int64_t bytes, void** ptr, unsigned char* handle);
+POPKV_API int popkv_peer_open(const unsigned char* handle, void** ptr);
+POPKV_API int popkv_peer_close(void* ptr);
+POPKV_API int popkv_peer_free(void* ptr);
+
+/*
+ * Merge of split partials (as popkv_attn_merge, head_dim 128) fused with the
+ * all-gather of the merged rows across `world` GPUs over peer memory.
+ *
+ * Rank `rank` merges its `rows` local rows (one CTA per row).  Each element is
+ * stored into every peer's receive area as one 8-byte word (value bits, launch
+ * epoch).  The CTA then polls its own area for the same row of every peer,
+ * with a bounded wait, and writes the world*rows gathered rows, rank-major, to
+ * `out` [world*rows, 128] of `out_dtype`.
+ *
+ * Arguments:
+ * - peer_recv: device array [world] of each rank's receive area. An area is
+ *   2 x world x rows x 128 uint64, zero at setup, 8-byte aligned.
+ * - own_recv: this rank's area.
+ * - state: 3 uint32 in this rank's memory, zero at setup. state[2] becomes 1
+ *   when a wait for a peer gave up (the output is then incomplete).
+ *
+ * Every rank must issue the same sequence of these calls on one set of
+ * buffers.
+ *
+ * Replaces popkv_attn_merge followed by the per-layer NCCL all-gather of head
+ * outputs (the sharded plan of the survey; sparse_kernels.py:367-387 for the
+ * merge).
+ */
+POPKV_API int popkv_attn_merge_gather(const float* partials, int64_t rows, int64_t splits, int64_t head_dim,
+                                      int out_dtype, int64_t rank, int64_t world, uint64_t* const* peer_recv,
+                                      const uint64_t* own_recv, uint32_t* state, void* out, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -39,6 +39,11 @@ _SIGNATURES = {
                                   _P, _P, _P, _L, _P, _P, _L, _P, _P, _P, _I, _P], _I),
     "popkv_attn_partial_merge_static": ([_P, _I, _L, _L, _L, _P, _P, _I, _L, _L, _L, _L, _L, _L, _L, _L,
                                          _P, _P, _P, _L, _P, _P, _L, _P, _I, _P], _I),
+    "popkv_peer_alloc": ([_L, ctypes.POINTER(ctypes.c_void_p), ctypes.c_char_p], _I),
+    "popkv_peer_open": ([ctypes.c_char_p, ctypes.POINTER(ctypes.c_void_p)], _I),
+    "popkv_peer_close": ([_P], _I),
+    "popkv_peer_free": ([_P], _I),
+    "popkv_attn_merge_gather": ([_P, _L, _L, _L, _I, _L, _L, _P, _P, _P, _P, _P], _I),
     "popkv_retrieve": ([_P, _I, _L, _L, _L, _P, _P, _P, _P, _L, _L, _L, _L, _L, _P, _P, _P, _I,
                         _L, _L, _L, _L, _L, _L, _P, _P, _L, _P, _P, _P, _P], _I),
 }

@@ -42,6 +42,9 @@ class SparseAttentionStep:
             ``host_current_keys``, ``host_current_values``, ``host_output``) and
             capture their transfers in the graph: one host-to-device copy of
             q | k | v and one device-to-host copy of the output per replay.
+        gather: a ``sharding.PeerGather`` for batch * q_heads rows: the merge
+            also gathers every rank's rows over peer memory into
+            ``gather.output`` (the step's result; rank-major).
         chunks: split the step into this many KV-head chunks on forked streams
             so that one chunk's top-k and attention overlap the next chunk's
             score (batch 1 with the consecutive GQA mapping only).
@@ -51,7 +54,8 @@ class SparseAttentionStep:
                  head_to_kv: torch.Tensor, *, budget: int, q_heads: int | None = None,
                  q_dtype: torch.dtype = torch.bfloat16, split_tokens: int = 256,
                  batch: int = 1, use_graph: bool = True, fused: bool = False,
-                 select: str = "auto", chunks: int = 1, host_io: bool = False) -> None:
+                 select: str = "auto", chunks: int = 1, host_io: bool = False,
+                 gather=None) -> None:
         if prefix_keys.ndim == 3:
             prefix_keys, prefix_values = prefix_keys[None], prefix_values[None]
         if prefix_keys.stride(-1) != 1 or prefix_values.stride(-1) != 1:
@@ -88,12 +92,16 @@ class SparseAttentionStep:
         self._inputs = torch.zeros(self._in_bytes, device=dev, dtype=torch.uint8)
         self.queries, self.current_keys, self.current_values = self._input_views(self._inputs, q_dtype, kv_dtype)
         self.output = torch.zeros((B, QH, D), device=dev, dtype=q_dtype)
+        self.gather = gather
+        if gather is not None and (gather.rows != B * QH or gather.dtype != q_dtype or chunks != 1 or fused):
+            raise ValueError("gather needs batch * q_heads rows of the query dtype, no chunks, unfused")
+        self.result = gather.output if gather is not None else self.output
         self.host_io = bool(host_io)
         if self.host_io:
             self._host_inputs = torch.zeros(self._in_bytes, dtype=torch.uint8).pin_memory()
             self.host_queries, self.host_current_keys, self.host_current_values = self._input_views(
                 self._host_inputs, q_dtype, kv_dtype)
-            self.host_output = torch.zeros((B, QH, D), dtype=q_dtype).pin_memory()
+            self.host_output = torch.zeros(tuple(self.result.shape), dtype=q_dtype).pin_memory()
         # Intermediates.
         self.q_sign = torch.zeros((B, QH, 4), device=dev, dtype=torch.int32)
         self.q_mag = torch.zeros_like(self.q_sign)
@@ -152,7 +160,7 @@ class SparseAttentionStep:
         self._launch_kernels(stream)
         if self.host_io:
             with torch.cuda.stream(stream):
-                self.host_output.copy_(self.output, non_blocking=True)
+                self.host_output.copy_(self.result, non_blocking=True)
 
     def _launch_kernels(self, stream) -> None:
         lib, check, ptr = _lib.lib(), _lib.check, _lib.ptr
@@ -231,8 +239,11 @@ class SparseAttentionStep:
             _lib.dtype_code(pk), KVH, self.prefix_tokens, pk.stride(0), pk.stride(1), pk.stride(2),
             pv.stride(0), pv.stride(1), pv.stride(2), ptr(ck), ptr(cv), ptr(indices), self.selected,
             None, ptr(mapping), self.split_tokens, ptr(partials), s))
-        check(lib.popkv_attn_merge(ptr(partials), B * QH, self.splits, 128, ptr(output),
-                                   _lib.dtype_code(output), s))
+        if self.gather is not None:
+            self.gather.launch(partials, self.splits, s)
+        else:
+            check(lib.popkv_attn_merge(ptr(partials), B * QH, self.splits, 128, ptr(output),
+                                       _lib.dtype_code(output), s))
 
     def recapture(self) -> None:
         """(Re)build the CUDA graph of the step's launches for the current buffers."""
@@ -251,14 +262,14 @@ class SparseAttentionStep:
     def run_eager(self) -> torch.Tensor:
         with torch.cuda.device(self.device):
             self._launch(torch.cuda.current_stream(self.device))
-        return self.output
+        return self.result
 
     def replay(self) -> torch.Tensor:
         """Run the step on the static buffers; returns ``self.output``."""
         if self.graph is None:
             return self.run_eager()
         self.graph.replay()
-        return self.output
+        return self.result
 
     def __call__(self, queries: torch.Tensor, current_keys: torch.Tensor,
                  current_values: torch.Tensor) -> torch.Tensor:
@@ -282,7 +293,7 @@ class SparseAttentionStep:
         if self.host_io:  # device inputs: skip the staging copy, keep the output on the device
             with torch.cuda.device(self.device):
                 self._launch_kernels(torch.cuda.current_stream(self.device))
-            return self.output
+            return self.result
         return self.replay()
 
 

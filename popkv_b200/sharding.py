@@ -72,3 +72,81 @@ def gather_heads(local: torch.Tensor, group=None) -> torch.Tensor:
     flat = torch.empty((world * batch * q_local * dim,), device=local.device, dtype=local.dtype)
     dist.all_gather_into_tensor(flat, local.contiguous().view(-1), group=group)
     return flat.view(world, batch, q_local, dim).permute(1, 0, 2, 3).reshape(batch, world * q_local, dim)
+
+
+class PeerGather:
+    """Merge fused with the all-gather over NVLink peer memory (popkv_attn_merge_gather).
+
+    Every rank of ``group`` constructs one, collectively: each allocates its
+    receive area (popkv_peer_alloc), the 64-byte CUDA IPC
+    handles are exchanged with ``all_gather_object`` (any backend), and each
+    rank maps its peers' memory.  ``launch`` then merges this rank's ``rows``
+    split states and leaves all ranks' merged rows in ``output``
+    [world * rows, 128], rank-major.  Every rank must launch the same sequence
+    of steps; ``error()`` reports a wait for a peer that gave up.
+    """
+
+    HEAD_DIM = 128
+
+    def __init__(self, rows: int, dtype: torch.dtype, device, group=None) -> None:
+        import ctypes
+
+        import torch.distributed as dist
+
+        from . import _lib
+        self._lib = _lib
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.rows = int(rows)
+        self.dtype = dtype
+        self.device = torch.device(device)
+        lib = _lib.lib()
+        recv_bytes = 2 * self.world * self.rows * self.HEAD_DIM * 8  # (value, epoch) words
+        ptr = ctypes.c_void_p()
+        handle = ctypes.create_string_buffer(64)
+        with torch.cuda.device(self.device):
+            _lib.check(lib.popkv_peer_alloc(recv_bytes, ctypes.byref(ptr), handle))
+        self._own = ptr
+        self._opened: list = []
+        handles: list = [None] * self.world
+        dist.all_gather_object(handles, handle.raw, group=group)
+        bases = []
+        with torch.cuda.device(self.device):
+            for r, h in enumerate(handles):
+                if r == self.rank:
+                    bases.append(ptr.value)
+                    continue
+                p = ctypes.c_void_p()
+                _lib.check(lib.popkv_peer_open(h, ctypes.byref(p)))
+                self._opened.append(p)
+                bases.append(p.value)
+        self._recv_ptrs = torch.tensor(bases, dtype=torch.int64, device=self.device)
+        self.state = torch.zeros(4, dtype=torch.int32, device=self.device)
+        self.output = torch.empty((self.world * self.rows, self.HEAD_DIM), dtype=dtype, device=self.device)
+
+    def launch(self, partials: torch.Tensor, splits: int, stream) -> None:
+        """Merge ``partials`` [rows, splits, 130] and gather into ``output`` on ``stream``."""
+        import ctypes
+        lib, _lib = self._lib.lib(), self._lib
+        self._lib.check(lib.popkv_attn_merge_gather(
+            _lib.ptr(partials), self.rows, int(splits), self.HEAD_DIM, _lib.dtype_code(self.output),
+            self.rank, self.world, _lib.ptr(self._recv_ptrs), ctypes.c_void_p(self._own.value),
+            _lib.ptr(self.state), _lib.ptr(self.output), stream))
+
+    def error(self) -> bool:
+        return bool(int(self.state[2].item()))
+
+    def close(self) -> None:
+        """Unmap the peers and free this rank's area (collective: all ranks call it)."""
+        import torch.distributed as dist
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
+        lib = self._lib.lib()
+        with torch.cuda.device(self.device):
+            for p in self._opened:
+                self._lib.check(lib.popkv_peer_close(p))
+            self._opened = []
+            if self._own is not None:
+                self._lib.check(lib.popkv_peer_free(self._own))
+                self._own = None

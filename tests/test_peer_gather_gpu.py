@@ -1,0 +1,135 @@
+"""Merge fused with the cross-GPU all-gather over peer memory (needs 2 GPUs).
+
+Two processes, one per GPU, exchange CUDA IPC handles over a gloo group.  The
+gathered output must equal every rank's popkv_attn_merge of its own rows, bit
+for bit, over several launches (both receive-buffer parities), eagerly and
+inside a replayed CUDA graph; and a KV-head-sharded decode step must equal the
+unsharded step.
+"""
+from __future__ import annotations
+
+import os
+import socket
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+WORLD = 2
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _partials(rank: int, rows: int, splits: int) -> torch.Tensor:
+    gen = torch.Generator().manual_seed(1000 + rank)
+    p = torch.randn(rows, splits, 130, generator=gen)
+    p[..., 1] = torch.rand(rows, splits, generator=gen) * 2 + 0.5  # positive softmax sums
+    return p
+
+
+def _merge_worker(rank: int, port: int, rows: int, splits: int) -> None:
+    import torch.distributed as dist
+
+    from popkv_b200 import _lib
+    from popkv_b200.sharding import PeerGather
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("gloo", rank=rank, world_size=WORLD,
+                            timeout=__import__("datetime").timedelta(seconds=60))
+    try:
+        lib = _lib.lib()
+        want = []
+        for r in range(WORLD):  # every rank's rows merged locally with popkv_attn_merge
+            p = _partials(r, rows, splits).to(dev)
+            out = torch.empty(rows, 128, dtype=torch.bfloat16, device=dev)
+            _lib.check(lib.popkv_attn_merge(_lib.ptr(p), rows, splits, 128, _lib.ptr(out), _lib.BF16,
+                                            _lib.stream_of(dev)))
+            want.append(out)
+        want = torch.cat(want)
+        mine = _partials(rank, rows, splits).to(dev)
+        gather = PeerGather(rows, torch.bfloat16, dev)
+        for _ in range(3):
+            gather.output.zero_()
+            gather.launch(mine, splits, _lib.stream_of(dev))
+            torch.cuda.synchronize(dev)
+            assert not gather.error()
+            assert torch.equal(gather.output, want), "eager merge+gather differs"
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=side):
+            gather.launch(mine, splits, _lib.stream_of(dev))
+        for _ in range(3):
+            gather.output.zero_()
+            graph.replay()
+            torch.cuda.synchronize(dev)
+            assert not gather.error()
+            assert torch.equal(gather.output, want), "graph merge+gather differs"
+        del graph
+        gather.close()
+    finally:
+        dist.destroy_process_group()
+
+
+def _step_worker(rank: int, port: int) -> None:
+    import torch.distributed as dist
+
+    from popkv_b200 import popkv as P
+    from popkv_b200.decode import SparseAttentionStep
+    from popkv_b200.sharding import PeerGather, head_shard
+    from popkv_b200.workloads import decode_inputs, head_to_kv
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("gloo", rank=rank, world_size=WORLD,
+                            timeout=__import__("datetime").timedelta(seconds=60))
+    try:
+        x = decode_inputs(context=4000, seed=17, dtype="bf16")
+        to = lambda a: torch.from_numpy(a).to(torch.bfloat16).to(dev)  # noqa: E731
+        tg, g = P.POPKV_PRESETS["popkv-q"]
+        keys, values = to(x.keys[0]), to(x.values[0])
+        q, ck, cv = to(x.queries), to(x.current_keys[0]), to(x.current_values[0])
+        full_cache = P.build_popkv_cache(keys, group_size=tg, dim_group_size=g, reserve_tokens=0)
+        full = SparseAttentionStep(full_cache, keys, values, torch.from_numpy(head_to_kv(32, 8)).to(dev),
+                                   budget=512)
+        want = full(q, ck, cv).clone().view(32, 128)
+        sh = head_shard(32, 8, WORLD, rank)
+        lk, lv = keys[sh.kv_slice].contiguous(), values[sh.kv_slice].contiguous()
+        cache = P.build_popkv_cache(lk, group_size=tg, dim_group_size=g, reserve_tokens=0)
+        gather = PeerGather(sh.q_heads, torch.bfloat16, dev)
+        step = SparseAttentionStep(cache, lk, lv, sh.local_head_to_kv(dev), budget=512, gather=gather)
+        for _ in range(3):
+            got = step(q[:, sh.q_slice], ck[sh.kv_slice], cv[sh.kv_slice])
+            torch.cuda.synchronize(dev)
+            assert not gather.error()
+            assert torch.equal(got, want), "sharded step differs from the unsharded step"
+        step.graph = None
+        gather.close()
+    finally:
+        dist.destroy_process_group()
+
+
+def _need_two_gpus():
+    if not torch.cuda.is_available() or torch.cuda.device_count() < WORLD:
+        pytest.skip("needs 2 GPUs")
+
+
+@pytest.mark.parametrize("rows,splits", [(16, 16), (32, 3), (1, 1)])
+def test_merge_gather_equals_local_merges(rows, splits):
+    _need_two_gpus()
+    import torch.multiprocessing as mp
+    mp.spawn(_merge_worker, args=(_free_port(), rows, splits), nprocs=WORLD, join=True)
+
+
+def test_sharded_step_with_peer_gather_equals_unsharded_step():
+    _need_two_gpus()
+    import torch.multiprocessing as mp
+    mp.spawn(_step_worker, args=(_free_port(),), nprocs=WORLD, join=True)
