@@ -73,6 +73,7 @@ def parse_args(argv=None):
                    help="top-k path of the step (hist: score kernel builds the first radix histogram)")
     p.add_argument("--gather", choices=("peer", "nccl"), default="peer",
                    help="N>1: merge fused with the all-gather over NVLink peer memory, or NCCL all-gather")
+    p.add_argument("--split", type=int, default=256, help="selected slots per attention partial")
     p.add_argument("--chunks", type=int, default=1,
                    help="KV-head chunks pipelined on forked streams inside the step graph")
     p.add_argument("--no-cpu-baseline", action="store_true")
@@ -226,7 +227,8 @@ def build_steps(args, layer, copies: int, gather=None):
             raise SystemExit("batch > 1 benchmarking is not wired yet")
         step = SparseAttentionStep(caches[0], keys, values, layer["mapping"], budget=args.budget,
                                    q_dtype=torch.bfloat16, batch=B, use_graph=not args.no_graph,
-                                   select=args.select, chunks=args.chunks, gather=gather)
+                                   select=args.select, chunks=args.chunks, gather=gather,
+                                   split_tokens=args.split)
         step.queries.copy_(layer["queries"])
         step.current_keys.copy_(layer["cur_k"])
         step.current_values.copy_(layer["cur_v"])
@@ -270,7 +272,7 @@ def algorithmic_bytes(args, layer, rows: int) -> dict:
     reps = 128 // layer["g"]
     k = min(args.budget - 1, T)
     sel = k + 1
-    splits = math.ceil(sel / 256)
+    splits = math.ceil(sel / args.split)
     meta = B * kv * T * (32 + 4 * reps)
     scores = B * qh * T * 2
     idx = B * qh * sel * 8
@@ -609,7 +611,7 @@ def end_to_end(args, layer, steps, device, dist, gathered, world, peer=None):
             step = SparseAttentionStep(src.cache, src.prefix_keys, src.prefix_values, src.head_to_kv,
                                        budget=args.budget, q_dtype=torch.bfloat16, batch=args.batch,
                                        use_graph=not args.no_graph, select=args.select, host_io=True,
-                                       gather=peer)
+                                       gather=peer, split_tokens=args.split)
             step.host_queries.copy_(layer["queries"].cpu())
             step.host_current_keys.copy_(layer["cur_k"].cpu())
             step.host_current_values.copy_(layer["cur_v"].cpu())

@@ -52,7 +52,7 @@ __global__ void __launch_bounds__(kEncodeWarps * 32) query_encode_kernel(
 // ---------------------------------------------------------------------------
 
 constexpr int kScoreThreads = 256;
-constexpr int kTokensPerThread = 2;
+constexpr int kTokensPerThread = 1;
 constexpr int kScoreTile = kScoreThreads * kTokensPerThread;
 constexpr int kMaxGroupHeads = 16;
 
@@ -64,7 +64,7 @@ constexpr int kHistBins11 = 2048;
 constexpr int kMaxHistHeads = 4;
 
 template <int G, typename QT, bool RAW, bool HIST = false>
-__global__ void __launch_bounds__(kScoreThreads) score128_kernel(
+__global__ void __launch_bounds__(kScoreThreads, 4) score128_kernel(
     const QT* __restrict__ queries, const int32_t* __restrict__ q_sign,
     const int32_t* __restrict__ q_mag, const float* __restrict__ q_low,
     const float* __restrict__ q_delta, const int32_t* __restrict__ k_sign,
