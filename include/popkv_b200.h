@@ -295,6 +295,17 @@ POPKV_API int popkv_retrieve(
     uint16_t* scores_out, int64_t* indices_out, void* stream);
 
 /*
+ * Copy `bytes` (a multiple of 16) from `src` to `dst` with a kernel, so that
+ * the copy chains to the next kernel of the step by programmatic dependent
+ * launch.  `src` may be pinned host memory (device-addressable under unified
+ * addressing); both 16-byte aligned.  The captured decode step uses it to
+ * bring a step's q | current k | current v in from host staging.
+ *
+ * No counterpart in the reference (its inputs are device tensors already).
+ */
+POPKV_API int popkv_stage(const void* src, void* dst, int64_t bytes, void* stream);
+
+/*
  * Peer memory for the cross-GPU exchange (setup time, not per step).
  * popkv_peer_alloc: cudaMalloc `bytes` (zeroed) on the current device and
  * export it: `handle` receives the 64-byte CUDA IPC handle.  popkv_peer_open

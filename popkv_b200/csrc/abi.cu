@@ -76,3 +76,32 @@ float score_scale_for(int64_t head_dim) {
 extern "C" const char* popkv_last_error(void) { return popkv::g_message; }
 
 extern "C" int popkv_abi_version(void) { return POPKV_ABI_VERSION; }
+
+namespace popkv {
+namespace {
+
+// Copies `n16` 16-byte units from host-mapped (or device) memory to the device.
+__global__ void __launch_bounds__(256) stage_kernel(const uint4* __restrict__ src, uint4* __restrict__ dst,
+                                                    int64_t n16) {
+    pdl_wait();
+    pdl_launch_dependents();
+    for (int64_t i = blockIdx.x * 256ll + threadIdx.x; i < n16; i += gridDim.x * 256ll) dst[i] = src[i];
+}
+
+}  // namespace
+}  // namespace popkv
+
+extern "C" int popkv_stage(const void* src, void* dst, int64_t bytes, void* stream) {
+    using namespace popkv;
+    if (bytes < 0 || (bytes % 16) != 0)
+        return fail(POPKV_ERR_INVALID, "popkv_stage: bytes must be a non-negative multiple of 16");
+    if (bytes == 0) return POPKV_OK;
+    if (!src || !dst || !aligned(src, 16) || !aligned(dst, 16))
+        return fail(POPKV_ERR_INVALID, "popkv_stage: buffers must be non-null and 16-byte aligned");
+    const int64_t n16 = bytes / 16;
+    const unsigned blocks = static_cast<unsigned>(n16 > 256 * 64 ? 64 : (n16 + 255) / 256);
+    const cudaError_t err = launch_pdl(stage_kernel, dim3(blocks), dim3(256), 0, static_cast<cudaStream_t>(stream), 1,
+                                       static_cast<const uint4*>(src), static_cast<uint4*>(dst), n16);
+    if (err != cudaSuccess) return fail(POPKV_ERR_CUDA, "popkv_stage: %s", cudaGetErrorString(err));
+    return check_launch("popkv_stage");
+}

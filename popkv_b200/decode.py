@@ -102,6 +102,7 @@ class SparseAttentionStep:
             self.host_queries, self.host_current_keys, self.host_current_values = self._input_views(
                 self._host_inputs, q_dtype, kv_dtype)
             self.host_output = torch.zeros(tuple(self.result.shape), dtype=q_dtype).pin_memory()
+            self.result = self.host_output
         # Intermediates.
         self.q_sign = torch.zeros((B, QH, 4), device=dev, dtype=torch.int32)
         self.q_mag = torch.zeros_like(self.q_sign)
@@ -153,16 +154,24 @@ class SparseAttentionStep:
         return q, k, v
 
     # -- launches ---------------------------------------------------------------
+    def _direct_host_out(self) -> bool:
+        """host_io with the merge writing the pinned host output itself."""
+        return self.host_io and self.gather is None and not self.fused and self.chunks == 1
+
     def _launch(self, stream) -> None:
         if self.host_io:
+            # q | k | v from the pinned staging buffer by a copy kernel (chained to
+            # the score kernel by programmatic dependent launch).
+            _lib.check(_lib.lib().popkv_stage(_lib.ptr(self._host_inputs), _lib.ptr(self._inputs),
+                                              self._in_bytes, ctypes_stream(stream)))
+        direct = self._direct_host_out()
+        self._launch_kernels(stream, host_out=direct)
+        if self.host_io and not direct:
             with torch.cuda.stream(stream):
-                self._inputs.copy_(self._host_inputs, non_blocking=True)
-        self._launch_kernels(stream)
-        if self.host_io:
-            with torch.cuda.stream(stream):
-                self.host_output.copy_(self.result, non_blocking=True)
+                self.host_output.copy_(self.gather.output if self.gather is not None else self.output,
+                                       non_blocking=True)
 
-    def _launch_kernels(self, stream) -> None:
+    def _launch_kernels(self, stream, host_out: bool = False) -> None:
         lib, check, ptr = _lib.lib(), _lib.check, _lib.ptr
         s = ctypes_stream(stream)
         B, QH, KVH = self.batch, self.q_heads, self.kv_heads
@@ -179,7 +188,7 @@ class SparseAttentionStep:
                 None, ptr(self.indices), s))
             return
         if self.chunks == 1:
-            self._launch_chunk(s, 0, KVH)
+            self._launch_chunk(s, 0, KVH, host_out=host_out)
             return
         # KV-head chunks on forked streams: the scores run back to back on the
         # chunk streams (chunk c waits for chunk c-1's score), and each chunk's
@@ -199,7 +208,7 @@ class SparseAttentionStep:
         for end in done:
             stream.wait_event(end)
 
-    def _launch_chunk(self, s, h0: int, h1: int, scored_event=None) -> None:
+    def _launch_chunk(self, s, h0: int, h1: int, scored_event=None, host_out: bool = False) -> None:
         """Score, select and attend for KV heads [h0, h1) (all of them when unchunked)."""
         lib, check, ptr = _lib.lib(), _lib.check, _lib.ptr
         B, KVH = self.batch, h1 - h0
@@ -213,6 +222,10 @@ class SparseAttentionStep:
         queries = self.queries[:, q0:q1]
         scores, indices = self.scores[:, q0:q1], self.indices[:, q0:q1]
         partials, output = self.partials[:, q0:q1], self.output[:, q0:q1]
+        if host_out and self.gather is None:
+            # The merge writes the result straight into the pinned host output
+            # (device-addressable under unified addressing).
+            output = self.host_output[:, q0:q1]
         mapping = self.head_to_kv if (h0, h1) == (0, self.kv_heads) else self._chunk_map
         # Query encoding runs in the score kernel's prologue.
         if self.select == "hist":
@@ -293,7 +306,7 @@ class SparseAttentionStep:
         if self.host_io:  # device inputs: skip the staging copy, keep the output on the device
             with torch.cuda.device(self.device):
                 self._launch_kernels(torch.cuda.current_stream(self.device))
-            return self.result
+            return self.gather.output if self.gather is not None else self.output
         return self.replay()
 
 
