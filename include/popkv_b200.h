@@ -295,6 +295,14 @@ POPKV_API int popkv_retrieve(
     uint16_t* scores_out, int64_t* indices_out, void* stream);
 
 /*
+ * Number of popkv_score_tc threads, since the library was loaded on the current
+ * device, whose bounded wait for the tensor cores gave up (0 in a healthy
+ * run).  A nonzero count means those launches' scores are incomplete.
+ * Synchronises with the device.  No counterpart in the reference.
+ */
+POPKV_API int popkv_score_tc_timeouts(uint32_t* count);
+
+/*
  * Copy `bytes` (a multiple of 16) from `src` to `dst` with a kernel, so that
  * the copy chains to the next kernel of the step by programmatic dependent
  * launch.  `src` may be pinned host memory (device-addressable under unified

@@ -40,6 +40,7 @@ _SIGNATURES = {
     "popkv_attn_partial_merge_static": ([_P, _I, _L, _L, _L, _P, _P, _I, _L, _L, _L, _L, _L, _L, _L, _L,
                                          _P, _P, _P, _L, _P, _P, _L, _P, _I, _P], _I),
     "popkv_stage": ([_P, _P, _L, _P], _I),
+    "popkv_score_tc_timeouts": ([ctypes.POINTER(ctypes.c_uint32)], _I),
     "popkv_peer_alloc": ([_L, ctypes.POINTER(ctypes.c_void_p), ctypes.c_char_p], _I),
     "popkv_peer_open": ([ctypes.c_char_p, ctypes.POINTER(ctypes.c_void_p)], _I),
     "popkv_peer_close": ([_P], _I),

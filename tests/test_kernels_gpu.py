@@ -204,6 +204,11 @@ def test_tensor_core_score_matches_popcount_kernel(cuda_device, g, batch, tokens
     enc = C.query_encode(q, dim_group_size=g)
     popc = C.score_encoded(enc, packed, head_to_kv=mapping, tokens=tokens, dim_group_size=g)
     assert torch.equal(mma.view(torch.int16), popc.view(torch.int16))
+    import ctypes
+    from popkv_b200 import _lib
+    timeouts = ctypes.c_uint32(0)
+    _lib.check(_lib.lib().popkv_score_tc_timeouts(ctypes.byref(timeouts)))
+    assert timeouts.value == 0
     if tokens <= 1000:
         arr, tag = to_oracle(q)
         penc = oracle.query_encode(arr, tag, dim_group_size=g)
