@@ -32,14 +32,14 @@ bool valid_dtype(int dtype) {
 size_t dtype_size(int dtype) { return dtype == POPKV_DTYPE_F32 ? 4 : 2; }
 
 int allow_dynamic_smem_impl(const void* kernel, int bytes) {
-    // (kernel, device mask) pairs already configured; a handful of kernels use this.
-    constexpr int kSlots = 64;
+    // Dynamic shared-memory limit already set, per (kernel, device); a handful
+    // of kernels use this.  A larger request raises the limit again.
+    constexpr int kSlots = 64, kDevices = 64;
     static std::mutex mutex;
     static const void* kernels[kSlots] = {};
-    static unsigned long long masks[kSlots] = {};
+    static int configured[kSlots][kDevices] = {};
     int device = 0;
     if (cudaGetDevice(&device) != cudaSuccess) return fail(POPKV_ERR_CUDA, "cudaGetDevice failed");
-    const unsigned long long bit = 1ull << (device & 63);
     std::lock_guard<std::mutex> lock(mutex);
     int slot = -1;
     for (int i = 0; i < kSlots; ++i) {
@@ -53,7 +53,8 @@ int allow_dynamic_smem_impl(const void* kernel, int bytes) {
             break;
         }
     }
-    if (slot >= 0 && (masks[slot] & bit)) return POPKV_OK;
+    const bool known = slot >= 0 && device >= 0 && device < kDevices;
+    if (known && configured[slot][device] >= bytes) return POPKV_OK;
     cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
     if (err != cudaSuccess)
         return fail(POPKV_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(err));
@@ -62,7 +63,7 @@ int allow_dynamic_smem_impl(const void* kernel, int bytes) {
                                cudaSharedmemCarveoutMaxShared);
     if (err != cudaSuccess)
         return fail(POPKV_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(err));
-    if (slot >= 0) masks[slot] |= bit;  // beyond kSlots kernels: set every call
+    if (known) configured[slot][device] = bytes;  // otherwise: set on every call
     return POPKV_OK;
 }
 

@@ -6,9 +6,13 @@
 // (popkv_cuda.py:53-87).
 //
 // One CTA encodes one token group of one KV head:
-//   phase 1: per-dimension min/max over the group's tokens (coalesced loads,
-//            split across row slices, combined in shared memory), stored as the
-//            magnitude thresholds 0.5*max and 0.5*min;
+//   staging (when the group's rows fit and are 16-byte aligned): every thread
+//            issues its 16-byte loads of the group's rows at once, into shared
+//            memory, so the two phases below read shared memory instead of
+//            walking the rows with dependent global loads;
+//   phase 1: per-dimension min/max over the group's tokens (split across row
+//            slices, combined in shared memory), stored as the magnitude
+//            thresholds 0.5*max and 0.5*min;
 //   phase 2: one warp per token row, lane l owning dim 32*w + l of word w:
 //            two ballots give the sign and magnitude words, and the bucket sums
 //            of each representative group are reduced by a butterfly whose lane-0
@@ -23,7 +27,6 @@ namespace popkv {
 namespace {
 
 constexpr int kPackThreads = 256;
-constexpr int kMaxWords = 8;  // head_dim <= 256
 
 __device__ __forceinline__ float butterfly16(float x) {
 #pragma unroll
@@ -37,13 +40,13 @@ __device__ __forceinline__ float butterfly32(float x) {
     return x;
 }
 
-template <typename T, int G, int W>
+template <typename T, int G, int W, bool STAGED>
 __global__ void __launch_bounds__(kPackThreads) pack_kernel(
     const T* __restrict__ keys, int64_t head_stride, int64_t token_stride, int64_t tokens,
     int head_dim, int64_t token_group, int32_t* __restrict__ k_sign, int32_t* __restrict__ k_mag,
     uint16_t* __restrict__ k_low, uint16_t* __restrict__ k_delta, int64_t capacity,
     int64_t token_offset) {
-    extern __shared__ float smem[];
+    extern __shared__ __align__(16) float smem[];
     float* thr_hi = smem;                      // [head_dim]  0.5 * max
     float* thr_lo = smem + head_dim;           // [head_dim]  0.5 * min
     float* part = smem + 2 * head_dim;         // [slices][2][head_dim] partial extrema
@@ -53,6 +56,24 @@ __global__ void __launch_bounds__(kPackThreads) pack_kernel(
     const int64_t t1 = min(t0 + token_group, tokens);
     const T* head = keys + kvh * head_stride;
     const int tid = threadIdx.x;
+    const int slices0 = max(1, kPackThreads / head_dim);
+    // Staged rows [t1 - t0][head_dim] after the extrema scratch, 16-byte aligned.
+    T* tile = reinterpret_cast<T*>(smem + ((2 + 2 * slices0) * head_dim + 3) / 4 * 4);
+    if constexpr (STAGED) {
+        const int chunks = head_dim * static_cast<int>(sizeof(T)) / 16;  // per row
+        const int total = static_cast<int>(t1 - t0) * chunks;
+#pragma unroll 4
+        for (int i = tid; i < total; i += kPackThreads) {
+            const int r = i / chunks, c = i % chunks;
+            const uint4 v = __ldg(reinterpret_cast<const uint4*>(head + (t0 + r) * token_stride) + c);
+            reinterpret_cast<uint4*>(tile + static_cast<int64_t>(r) * head_dim)[c] = v;
+        }
+        __syncthreads();
+    }
+    auto row_ptr = [&](int64_t t) -> const T* {
+        if constexpr (STAGED) return tile + (t - t0) * head_dim;
+        else return head + t * token_stride;
+    };
 
     // Phase 1: extrema.  `slices` row slices of head_dim threads each
     // (head_dim <= 256 == kPackThreads, so every dim has a thread).
@@ -62,7 +83,7 @@ __global__ void __launch_bounds__(kPackThreads) pack_kernel(
         float mn = INFINITY, mx = -INFINITY;
 #pragma unroll 4
         for (int64_t t = t0 + s; t < t1; t += slices) {
-            float v = load_float(head + t * token_stride + d);
+            float v = load_float(row_ptr(t) + d);
             mn = fminf(mn, v);
             mx = fmaxf(mx, v);
         }
@@ -86,7 +107,7 @@ __global__ void __launch_bounds__(kPackThreads) pack_kernel(
     constexpr int kWarps = kPackThreads / 32;
     const int reps = (head_dim + G - 1) / G;
     for (int64_t t = t0 + warp; t < t1; t += kWarps) {
-        const T* row = head + t * token_stride;
+        const T* row = row_ptr(t);
         const int64_t out_row = kvh * capacity + token_offset + t;
         float a_low[W], a_high[W];
         uint32_t sw[W], mw[W], vw[W];
@@ -170,6 +191,197 @@ __global__ void __launch_bounds__(kPackThreads) pack_kernel(
     }
 }
 
+// ---------------------------------------------------------------------------
+// head_dim 128, staged rows: one thread per token row in phase 2.
+//
+// The warp-per-row phase above spends ~300 warp instructions per row on
+// ballots and shuffle trees, only 32 values per instruction.  Here each
+// thread encodes a whole row from shared memory (rows padded by 16 bytes so a
+// warp's 16-byte loads of 32 different rows spread over the banks), builds the
+// sign/magnitude words with shifts, and reproduces the reference's lane-0
+// shuffle-down tree (s[i] += s[i + o], o = 16 .. 1, width 16 for G16) with
+// in-register pairwise adds, so the sums are the same bit for bit.
+// ---------------------------------------------------------------------------
+template <int N>
+__device__ __forceinline__ float tree_sum(float* a) {  // lane-0 result of a width-N shuffle-down tree
+#pragma unroll
+    for (int o = N / 2; o > 0; o >>= 1)
+#pragma unroll
+        for (int i = 0; i < o; ++i) a[i] = __fadd_rn(a[i], a[i + o]);
+    return a[0];
+}
+
+template <typename T>
+__device__ __forceinline__ void load32(const unsigned char* p, float* v) {  // 32 consecutive elements
+    if constexpr (sizeof(T) == 4) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const uint4 u = *reinterpret_cast<const uint4*>(p + 16 * j);
+            v[4 * j] = __uint_as_float(u.x); v[4 * j + 1] = __uint_as_float(u.y);
+            v[4 * j + 2] = __uint_as_float(u.z); v[4 * j + 3] = __uint_as_float(u.w);
+        }
+    } else {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const uint4 u = *reinterpret_cast<const uint4*>(p + 16 * j);
+            const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+                    v[8 * j + 2 * e] = bf16_lo(w[e]);
+                    v[8 * j + 2 * e + 1] = bf16_hi(w[e]);
+                } else {
+                    const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[e]));
+                    v[8 * j + 2 * e] = f.x;
+                    v[8 * j + 2 * e + 1] = f.y;
+                }
+            }
+        }
+    }
+}
+
+template <typename T, int G>
+__global__ void __launch_bounds__(kPackThreads) pack_rows_kernel(
+    const T* __restrict__ keys, int64_t head_stride, int64_t token_stride, int64_t tokens,
+    int64_t token_group, int32_t* __restrict__ k_sign, int32_t* __restrict__ k_mag,
+    uint16_t* __restrict__ k_low, uint16_t* __restrict__ k_delta, int64_t capacity,
+    int64_t token_offset) {
+    constexpr int D = 128, R = D / G, kSlices = kPackThreads / D;
+    constexpr int kRowBytes = D * static_cast<int>(sizeof(T)) + 16;
+    constexpr int kChunks = D * static_cast<int>(sizeof(T)) / 16;
+    extern __shared__ __align__(16) float smem[];
+    float* thr_hi = smem;                // [D]
+    float* thr_lo = smem + D;            // [D]
+    float* part = smem + 2 * D;          // [kSlices][2][D]
+    unsigned char* tile = reinterpret_cast<unsigned char*>(smem + (2 + 2 * kSlices) * D);
+
+    const int64_t kvh = blockIdx.y;
+    const int64_t t0 = static_cast<int64_t>(blockIdx.x) * token_group;
+    const int64_t t1 = min(t0 + token_group, tokens);
+    const int rows = static_cast<int>(t1 - t0);
+    const T* head = keys + kvh * head_stride;
+    const int tid = threadIdx.x;
+
+    for (int i = tid; i < rows * kChunks; i += kPackThreads) {
+        const int r = i / kChunks, c = i % kChunks;
+        const uint4 v = __ldg(reinterpret_cast<const uint4*>(head + (t0 + r) * token_stride) + c);
+        *reinterpret_cast<uint4*>(tile + r * kRowBytes + c * 16) = v;
+    }
+    __syncthreads();
+
+    // Phase 1: extrema per dim.
+    {
+        const int d = tid % D, sl = tid / D;
+        float mn = INFINITY, mx = -INFINITY;
+        for (int r = sl; r < rows; r += kSlices) {
+            const float v = load_float(reinterpret_cast<const T*>(tile + r * kRowBytes) + d);
+            mn = fminf(mn, v);
+            mx = fmaxf(mx, v);
+        }
+        part[(sl * 2 + 0) * D + d] = mn;
+        part[(sl * 2 + 1) * D + d] = mx;
+    }
+    __syncthreads();
+    if (tid < D) {
+        float mn = part[tid], mx = part[D + tid];
+#pragma unroll
+        for (int sl = 1; sl < kSlices; ++sl) {
+            mn = fminf(mn, part[(sl * 2 + 0) * D + tid]);
+            mx = fmaxf(mx, part[(sl * 2 + 1) * D + tid]);
+        }
+        thr_lo[tid] = __fmul_rn(mn, 0.5f);
+        thr_hi[tid] = __fmul_rn(mx, 0.5f);
+    }
+    __syncthreads();
+
+    // Phase 2: one thread per row.
+    for (int r = tid; r < rows; r += kPackThreads) {
+        const unsigned char* rowp = tile + r * kRowBytes;
+        const int64_t out_row = kvh * capacity + token_offset + t0 + r;
+        uint32_t sw[4], mw[4];
+        float lows[R], deltas[R];
+        float pend_lo[32], pend_hi[32];  // G64: the first word of a pair, summed per lane with the second
+#pragma unroll
+        for (int w = 0; w < 4; ++w) {
+            float v[32];
+            load32<T>(rowp + w * 32 * static_cast<int>(sizeof(T)), v);
+            uint32_t sb = 0, mb = 0;
+            float lo[32], hi[32];
+#pragma unroll
+            for (int l = 0; l < 32; ++l) {
+                const int d = w * 32 + l;
+                const bool sign = v[l] >= 0.0f;
+                const bool mag = sign ? (v[l] > thr_hi[d]) : (v[l] < thr_lo[d]);
+                sb |= static_cast<uint32_t>(sign) << l;
+                mb |= static_cast<uint32_t>(mag) << l;
+                const float a = fabsf(v[l]);
+                lo[l] = mag ? 0.0f : a;
+                hi[l] = mag ? a : 0.0f;
+            }
+            sw[w] = sb;
+            mw[w] = mb;
+            if constexpr (G == 16) {
+#pragma unroll
+                for (int half = 0; half < 2; ++half) {
+                    const uint32_t m = half ? 0xFFFF0000u : 0x0000FFFFu;
+                    const float ls = tree_sum<16>(lo + 16 * half);
+                    const float hs = tree_sum<16>(hi + 16 * half);
+                    float low, delta;
+                    bucket_means(ls, __popc(~mb & m), hs, __popc(mb & m), low, delta);
+                    lows[2 * w + half] = low;
+                    deltas[2 * w + half] = delta;
+                }
+            } else if constexpr (G == 32) {
+                const float ls = tree_sum<32>(lo), hs = tree_sum<32>(hi);
+                float low, delta;
+                bucket_means(ls, __popc(~mb), hs, __popc(mb), low, delta);
+                lows[w] = low;
+                deltas[w] = delta;
+            } else {
+                if ((w & 1) == 0) {
+#pragma unroll
+                    for (int l = 0; l < 32; ++l) {
+                        pend_lo[l] = lo[l];
+                        pend_hi[l] = hi[l];
+                    }
+                } else {
+#pragma unroll
+                    for (int l = 0; l < 32; ++l) {
+                        pend_lo[l] = __fadd_rn(pend_lo[l], lo[l]);
+                        pend_hi[l] = __fadd_rn(pend_hi[l], hi[l]);
+                    }
+                    const float ls = tree_sum<32>(pend_lo), hs = tree_sum<32>(pend_hi);
+                    float low, delta;
+                    bucket_means(ls, __popc(~mw[w - 1]) + __popc(~mb), hs, __popc(mw[w - 1]) + __popc(mb),
+                                 low, delta);
+                    lows[w / 2] = low;
+                    deltas[w / 2] = delta;
+                }
+            }
+        }
+        reinterpret_cast<uint4*>(k_sign)[out_row] = make_uint4(sw[0], sw[1], sw[2], sw[3]);
+        reinterpret_cast<uint4*>(k_mag)[out_row] = make_uint4(mw[0], mw[1], mw[2], mw[3]);
+        uint32_t lw[R / 2], dw[R / 2];
+#pragma unroll
+        for (int j = 0; j < R / 2; ++j) {
+            lw[j] = static_cast<uint32_t>(float_to_half_bits(lows[2 * j])) |
+                    (static_cast<uint32_t>(float_to_half_bits(lows[2 * j + 1])) << 16);
+            dw[j] = static_cast<uint32_t>(float_to_half_bits(deltas[2 * j])) |
+                    (static_cast<uint32_t>(float_to_half_bits(deltas[2 * j + 1])) << 16);
+        }
+        if constexpr (R == 8) {
+            reinterpret_cast<uint4*>(k_low)[out_row] = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+            reinterpret_cast<uint4*>(k_delta)[out_row] = make_uint4(dw[0], dw[1], dw[2], dw[3]);
+        } else if constexpr (R == 4) {
+            reinterpret_cast<uint2*>(k_low)[out_row] = make_uint2(lw[0], lw[1]);
+            reinterpret_cast<uint2*>(k_delta)[out_row] = make_uint2(dw[0], dw[1]);
+        } else {
+            reinterpret_cast<uint32_t*>(k_low)[out_row] = lw[0];
+            reinterpret_cast<uint32_t*>(k_delta)[out_row] = dw[0];
+        }
+    }
+}
+
 template <typename T, int G>
 int launch_pack_g(const void* keys, int64_t kv_heads, int64_t tokens, int64_t head_dim,
                   int64_t hs, int64_t ts, int32_t* k_sign, int32_t* k_mag, uint16_t* k_low,
@@ -178,14 +390,40 @@ int launch_pack_g(const void* keys, int64_t kv_heads, int64_t tokens, int64_t he
     const int64_t groups = (tokens + tg - 1) / tg;
     const int words = static_cast<int>((head_dim + 31) / 32);
     const int slices = head_dim >= kPackThreads ? 1 : kPackThreads / static_cast<int>(head_dim);
-    const size_t smem = sizeof(float) * static_cast<size_t>(head_dim) * (2 + 2 * slices);
+    const size_t scratch = sizeof(float) * ((static_cast<size_t>(head_dim) * (2 + 2 * slices) + 3) / 4 * 4);
+    const int64_t group_rows = tg < tokens ? tg : tokens;
+    const size_t tile = sizeof(T) * static_cast<size_t>(group_rows) * static_cast<size_t>(head_dim);
+    const bool staged = (head_dim * static_cast<int64_t>(sizeof(T))) % 16 == 0 &&
+                        (ts * static_cast<int64_t>(sizeof(T))) % 16 == 0 &&
+                        (hs * static_cast<int64_t>(sizeof(T))) % 16 == 0 && aligned(keys, 16) &&
+                        tile <= 96 * 1024;
+    const size_t smem = scratch + (staged ? tile : 0);
     dim3 grid(static_cast<unsigned>(groups), static_cast<unsigned>(kv_heads));
     const T* k = static_cast<const T*>(keys);
-#define POPKV_PACK_CASE(NW)                                                                   \
-    case NW:                                                                                  \
-        pack_kernel<T, G, NW><<<grid, kPackThreads, smem, stream>>>(                          \
-            k, hs, ts, tokens, static_cast<int>(head_dim), tg, k_sign, k_mag, k_low, k_delta, \
-            capacity, token_offset);                                                          \
+    if (staged && head_dim == 128) {  // thread-per-row encoder
+        const size_t rows_smem = sizeof(float) * 128 * (2 + 2 * (kPackThreads / 128)) +
+                                 static_cast<size_t>(group_rows) * (128 * sizeof(T) + 16);
+        if (rows_smem <= 96 * 1024) {
+            const int st = allow_dynamic_smem(pack_rows_kernel<T, G>, static_cast<int>(rows_smem));
+            if (st != POPKV_OK) return st;
+            pack_rows_kernel<T, G><<<grid, kPackThreads, rows_smem, stream>>>(
+                k, hs, ts, tokens, tg, k_sign, k_mag, k_low, k_delta, capacity, token_offset);
+            return check_launch("popkv_pack");
+        }
+    }
+#define POPKV_PACK_CASE(NW)                                                                          \
+    case NW:                                                                                         \
+        if (staged) {                                                                                \
+            const int st = allow_dynamic_smem(pack_kernel<T, G, NW, true>, static_cast<int>(smem));  \
+            if (st != POPKV_OK) return st;                                                           \
+            pack_kernel<T, G, NW, true><<<grid, kPackThreads, smem, stream>>>(                       \
+                k, hs, ts, tokens, static_cast<int>(head_dim), tg, k_sign, k_mag, k_low, k_delta,    \
+                capacity, token_offset);                                                             \
+        } else {                                                                                     \
+            pack_kernel<T, G, NW, false><<<grid, kPackThreads, smem, stream>>>(                      \
+                k, hs, ts, tokens, static_cast<int>(head_dim), tg, k_sign, k_mag, k_low, k_delta,    \
+                capacity, token_offset);                                                             \
+        }                                                                                            \
         break;
     switch (words) {
         POPKV_PACK_CASE(1)
