@@ -589,6 +589,17 @@ def stage_breakdown(args, layer, steps, device):
     occ = max(1, tg // 2)
     out["append"] = {"us": round(time_events(lambda: pack(keys0, occ), reps, device), 2),
                      "occupancy": occ}
+    # The decoded token's KV append fused with the re-encode of its open group
+    # (row occ - 1 of a group starting at 0), on a scratch copy of the caches.
+    if tg <= 128:
+        kc, vc = keys0.clone(), layer["values"][0].clone()
+        nk, nv = keys0[:, occ - 1].contiguous(), layer["values"][0][:, occ - 1].contiguous()
+
+        def append_kv():
+            check(lib.popkv_append_kv(ptr(nk), ptr(nv), _lib.BF16, kvh, 128, ptr(kc), ptr(vc), kc.stride(0),
+                                      kc.stride(1), vc.stride(0), vc.stride(1), occ - 1,
+                                      *(ptr(t) for t in planes), cap, 0, tg, g, s))
+        out["append_kv"] = {"us": round(time_events(append_kv, reps, device), 2), "occupancy": occ}
     return out
 
 

@@ -77,6 +77,34 @@ POPKV_API int popkv_pack(const void* keys, int keys_dtype, int64_t kv_heads, int
                int64_t dim_group_size, void* stream);
 
 /*
+ * Append of one decoded token fused with its metadata re-encode (head_dim
+ * 128, token groups of at most 128).
+ *
+ * What one launch does:
+ * - It writes new_keys[h] and new_values[h] ([kv_heads, 128], contiguous)
+ *   into the static caches at row `position`. cache_keys[h, t, d] is at
+ *   cache_keys + h*k_head_stride + t*k_token_stride + d; likewise the values.
+ * - It re-encodes the open token group, rows [sealed, position] of the key
+ *   cache, into the planes at the same token rows. The new key comes straight
+ *   from registers.
+ *
+ * `sealed` is the first row of the open group, a multiple of
+ * token_group_size, and position - sealed < token_group_size. The planes
+ * equal popkv_pack over the same rows.
+ *
+ * Replaces append_popkv's staging of active_keys (torch.cat) and
+ * pack_keys_into (popkv.py:438-459, popkv_cuda.py:72-87,
+ * csrc/popkv_ext.cu:1177-1206), together with the KV-cache append of the same
+ * token.
+ */
+POPKV_API int popkv_append_kv(const void* new_keys, const void* new_values, int dtype, int64_t kv_heads,
+                              int64_t head_dim, void* cache_keys, void* cache_values, int64_t k_head_stride,
+                              int64_t k_token_stride, int64_t v_head_stride, int64_t v_token_stride,
+                              int64_t position, int32_t* k_sign, int32_t* k_mag, uint16_t* k_low,
+                              uint16_t* k_delta, int64_t capacity, int64_t sealed, int64_t token_group_size,
+                              int64_t dim_group_size, void* stream);
+
+/*
  * Query bit-planes and representatives of `rows` = batch*q_heads queries
  * [rows, head_dim] (contiguous).
  *

@@ -25,6 +25,7 @@ _SIGNATURES = {
     "popkv_abi_version": ([], _I),
     "popkv_last_error": ([], ctypes.c_char_p),
     "popkv_pack": ([_P, _I, _L, _L, _L, _L, _L, _P, _P, _P, _P, _L, _L, _L, _L, _P], _I),
+    "popkv_append_kv": ([_P, _P, _I, _L, _L, _P, _P, _L, _L, _L, _L, _L, _P, _P, _P, _P, _L, _L, _L, _L, _P], _I),
     "popkv_query_encode": ([_P, _I, _L, _L, _L, _P, _P, _P, _P, _P], _I),
     "popkv_score_encoded": ([_P, _P, _P, _P, _L, _L, _P, _P, _P, _P, _L, _L, _P, _L, _L, _P, _P], _I),
     "popkv_score": ([_P, _I, _L, _L, _L, _P, _P, _P, _P, _L, _L, _P, _L, _L, _P, _I, _P], _I),

@@ -20,6 +20,7 @@
 //            (s[i] += s[i + o], o = 16, 8, 4, 2, 1; width 16 for G16).
 // Counts come from popcounts of the ballots, so only the two sums need shuffles.
 #include <cstdint>
+#include <type_traits>
 
 #include "common.cuh"
 
@@ -240,13 +241,20 @@ __device__ __forceinline__ void load32(const unsigned char* p, float* v) {  // 3
     }
 }
 
+constexpr int kRowThreads = 128;  // one thread per token row of a group of up to 128
+
+// With `new_keys` set (append): the group is rows [t0, tokens) of `keys` where
+// the last row, index tokens - 1, is taken from new_keys [KVH, 128] instead and
+// written to `keys`, and new_values to `values` at that row (the KV append of
+// the decoded token, fused with its re-encode).
 template <typename T, int G>
-__global__ void __launch_bounds__(kPackThreads) pack_rows_kernel(
+__global__ void __launch_bounds__(kRowThreads) pack_rows_kernel(
     const T* __restrict__ keys, int64_t head_stride, int64_t token_stride, int64_t tokens,
     int64_t token_group, int32_t* __restrict__ k_sign, int32_t* __restrict__ k_mag,
     uint16_t* __restrict__ k_low, uint16_t* __restrict__ k_delta, int64_t capacity,
-    int64_t token_offset) {
-    constexpr int D = 128, R = D / G, kSlices = kPackThreads / D;
+    int64_t token_offset, const T* __restrict__ new_keys = nullptr, const T* __restrict__ new_values = nullptr,
+    T* __restrict__ values = nullptr, int64_t v_head_stride = 0, int64_t v_token_stride = 0) {
+    constexpr int D = 128, R = D / G, kSlices = kRowThreads / D;
     constexpr int kRowBytes = D * static_cast<int>(sizeof(T)) + 16;
     constexpr int kChunks = D * static_cast<int>(sizeof(T)) / 16;
     extern __shared__ __align__(16) float smem[];
@@ -262,10 +270,23 @@ __global__ void __launch_bounds__(kPackThreads) pack_rows_kernel(
     const T* head = keys + kvh * head_stride;
     const int tid = threadIdx.x;
 
-    for (int i = tid; i < rows * kChunks; i += kPackThreads) {
+    const int cached_rows = new_keys ? rows - 1 : rows;
+    for (int i = tid; i < cached_rows * kChunks; i += kRowThreads) {
         const int r = i / kChunks, c = i % kChunks;
         const uint4 v = __ldg(reinterpret_cast<const uint4*>(head + (t0 + r) * token_stride) + c);
         *reinterpret_cast<uint4*>(tile + r * kRowBytes + c * 16) = v;
+    }
+    if (new_keys && tid < 2 * kChunks) {  // the appended token: stage its key, store its key and value
+        const int c = tid % kChunks;
+        const int64_t t = t1 - 1;
+        if (tid < kChunks) {
+            const uint4 v = __ldg(reinterpret_cast<const uint4*>(new_keys + kvh * D) + c);
+            *reinterpret_cast<uint4*>(tile + (rows - 1) * kRowBytes + c * 16) = v;
+            reinterpret_cast<uint4*>(const_cast<T*>(head) + t * token_stride)[c] = v;
+        } else {
+            const uint4 v = __ldg(reinterpret_cast<const uint4*>(new_values + kvh * D) + c);
+            reinterpret_cast<uint4*>(values + kvh * v_head_stride + t * v_token_stride)[c] = v;
+        }
     }
     __syncthreads();
 
@@ -295,7 +316,7 @@ __global__ void __launch_bounds__(kPackThreads) pack_rows_kernel(
     __syncthreads();
 
     // Phase 2: one thread per row.
-    for (int r = tid; r < rows; r += kPackThreads) {
+    for (int r = tid; r < rows; r += kRowThreads) {
         const unsigned char* rowp = tile + r * kRowBytes;
         const int64_t out_row = kvh * capacity + token_offset + t0 + r;
         uint32_t sw[4], mw[4];
@@ -401,12 +422,12 @@ int launch_pack_g(const void* keys, int64_t kv_heads, int64_t tokens, int64_t he
     dim3 grid(static_cast<unsigned>(groups), static_cast<unsigned>(kv_heads));
     const T* k = static_cast<const T*>(keys);
     if (staged && head_dim == 128) {  // thread-per-row encoder
-        const size_t rows_smem = sizeof(float) * 128 * (2 + 2 * (kPackThreads / 128)) +
+        const size_t rows_smem = sizeof(float) * 128 * (2 + 2 * (kRowThreads / 128)) +
                                  static_cast<size_t>(group_rows) * (128 * sizeof(T) + 16);
         if (rows_smem <= 96 * 1024) {
             const int st = allow_dynamic_smem(pack_rows_kernel<T, G>, static_cast<int>(rows_smem));
             if (st != POPKV_OK) return st;
-            pack_rows_kernel<T, G><<<grid, kPackThreads, rows_smem, stream>>>(
+            pack_rows_kernel<T, G><<<grid, kRowThreads, rows_smem, stream>>>(
                 k, hs, ts, tokens, tg, k_sign, k_mag, k_low, k_delta, capacity, token_offset);
             return check_launch("popkv_pack");
         }
@@ -498,4 +519,56 @@ extern "C" int popkv_pack(const void* keys, int keys_dtype, int64_t kv_heads, in
                                               capacity, token_offset, token_group_size,
                                               dim_group_size, s);
     }
+}
+
+extern "C" int popkv_append_kv(const void* new_keys, const void* new_values, int dtype, int64_t kv_heads,
+                               int64_t head_dim, void* cache_keys, void* cache_values, int64_t k_head_stride,
+                               int64_t k_token_stride, int64_t v_head_stride, int64_t v_token_stride,
+                               int64_t position, int32_t* k_sign, int32_t* k_mag, uint16_t* k_low,
+                               uint16_t* k_delta, int64_t capacity, int64_t sealed, int64_t token_group_size,
+                               int64_t dim_group_size, void* stream) {
+    using namespace popkv;
+    if (!valid_dtype(dtype)) return fail(POPKV_ERR_INVALID, "popkv_append_kv: keys must be fp32/fp16/bf16");
+    if (head_dim != 128) return fail(POPKV_ERR_UNSUPPORTED, "popkv_append_kv: head_dim must be 128");
+    if (kv_heads <= 0 || kv_heads > 65535) return fail(POPKV_ERR_INVALID, "popkv_append_kv: invalid KV head count");
+    if (dim_group_size != 16 && dim_group_size != 32 && dim_group_size != 64)
+        return fail(POPKV_ERR_INVALID, "dim_group_size must be 16, 32, or 64");
+    if (token_group_size < 1 || token_group_size > 128)
+        return fail(POPKV_ERR_UNSUPPORTED, "popkv_append_kv: token_group_size must be at most 128");
+    if (sealed < 0 || sealed % token_group_size || position < sealed || position - sealed >= token_group_size)
+        return fail(POPKV_ERR_INVALID, "popkv_append_kv: position must lie in the open group after `sealed`");
+    if (position >= capacity) return fail(POPKV_ERR_CAPACITY, "Pop-KV cache capacity exceeded");
+    if (!new_keys || !new_values || !cache_keys || !cache_values || !k_sign || !k_mag || !k_low || !k_delta)
+        return fail(POPKV_ERR_INVALID, "popkv_append_kv: null pointer");
+    const int64_t es = static_cast<int64_t>(dtype_size(dtype));
+    if (!aligned(new_keys, 16) || !aligned(new_values, 16) || !aligned(cache_keys, 16) ||
+        !aligned(cache_values, 16) || (k_head_stride * es) % 16 || (k_token_stride * es) % 16 ||
+        (v_head_stride * es) % 16 || (v_token_stride * es) % 16 || !aligned(k_sign, 16) || !aligned(k_mag, 16))
+        return fail(POPKV_ERR_INVALID, "popkv_append_kv: buffers and strides must be 16-byte aligned");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const int64_t rows = position - sealed + 1;
+    const dim3 grid(1, static_cast<unsigned>(kv_heads));
+    auto run = [&](auto tag, auto gtag) -> int {
+        using T = decltype(tag);
+        constexpr int G = decltype(gtag)::value;
+        const size_t smem = sizeof(float) * 128 * (2 + 2 * (kRowThreads / 128)) +
+                            static_cast<size_t>(rows) * (128 * sizeof(T) + 16);
+        const int st = allow_dynamic_smem(pack_rows_kernel<T, G>, static_cast<int>(smem));
+        if (st != POPKV_OK) return st;
+        // One group of `rows` rows starting at row `sealed` of the caches.
+        pack_rows_kernel<T, G><<<grid, kRowThreads, smem, s>>>(
+            static_cast<const T*>(cache_keys) + sealed * k_token_stride, k_head_stride, k_token_stride, rows,
+            rows, k_sign, k_mag, k_low, k_delta, capacity, sealed, static_cast<const T*>(new_keys),
+            static_cast<const T*>(new_values), static_cast<T*>(cache_values) + sealed * v_token_stride,
+            v_head_stride, v_token_stride);
+        return check_launch("popkv_append_kv");
+    };
+    auto by_g = [&](auto tag) -> int {
+        if (dim_group_size == 16) return run(tag, std::integral_constant<int, 16>{});
+        if (dim_group_size == 32) return run(tag, std::integral_constant<int, 32>{});
+        return run(tag, std::integral_constant<int, 64>{});
+    };
+    if (dtype == POPKV_DTYPE_F32) return by_g(float{});
+    if (dtype == POPKV_DTYPE_F16) return by_g(__half{});
+    return by_g(__nv_bfloat16{});
 }

@@ -127,6 +127,39 @@ def append_popkv(cache: PopKVCache, keys: torch.Tensor, timer=None) -> None:
     if timer: timer.mark("group_sealing")
 
 
+def append_popkv_kv(cache: PopKVCache, key_cache: torch.Tensor, value_cache: torch.Tensor,
+                    new_keys: torch.Tensor, new_values: torch.Tensor) -> None:
+    """Append one decoded token to the static K/V caches and re-encode its group, in one launch.
+
+    ``key_cache`` / ``value_cache`` [KVH, T, 128] (strided views allowed, head
+    dim contiguous) hold the cached tokens; the new token goes to row
+    ``cache.token_count``.  Unlike :func:`append_popkv` (popkv.py:438-459) no
+    ``active_keys`` copy is staged: the open group is re-encoded straight from
+    the key cache (popkv_append_kv).  ``cache.active_keys`` becomes a view of the
+    open group's rows.
+    """
+    from . import _lib
+    if key_cache.ndim != 3 or value_cache.ndim != 3 or key_cache.stride(-1) != 1 or value_cache.stride(-1) != 1:
+        raise ValueError("key/value caches must be [KV heads, tokens, head dim] with a contiguous head dim")
+    kv_heads, rows, head_dim = (int(x) for x in key_cache.shape)
+    position = cache.token_count
+    if position >= rows or position >= int(cache.packed[0].shape[1]):
+        raise RuntimeError("Pop-KV cache reserve exhausted")
+    nk = new_keys.reshape(kv_heads, head_dim).to(key_cache.dtype).contiguous()
+    nv = new_values.reshape(kv_heads, head_dim).to(value_cache.dtype).contiguous()
+    with torch.cuda.device(key_cache.device):
+        _lib.check(_lib.lib().popkv_append_kv(
+            _lib.ptr(nk), _lib.ptr(nv), _lib.dtype_code(key_cache), kv_heads, head_dim, _lib.ptr(key_cache),
+            _lib.ptr(value_cache), key_cache.stride(0), key_cache.stride(1), value_cache.stride(0),
+            value_cache.stride(1), position, *(_lib.ptr(t) for t in cache.packed),
+            int(cache.packed[0].shape[1]), cache.sealed_tokens, cache.group_size, cache.dim_group_size,
+            _lib.stream_of(key_cache.device)))
+    cache.token_count += 1
+    if cache.token_count - cache.sealed_tokens == cache.group_size:
+        cache.sealed_tokens += cache.group_size
+    cache.active_keys = key_cache[:, cache.sealed_tokens:cache.token_count]
+
+
 def topk(scores: torch.Tensor, k: int) -> torch.Tensor:
     """Deterministic replacement of torch.topk(scores, k, sorted=False).indices.
 

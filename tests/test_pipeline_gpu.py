@@ -17,7 +17,7 @@ from popkv_b200 import popkv as P
 from popkv_b200 import popkv_cuda as C
 from popkv_b200 import sparse_kernels as S
 from popkv_b200.workloads import decode_inputs, head_to_kv
-from tests.helpers import bits, planes_to_numpy, to_oracle
+from tests.helpers import bits, planes_to_numpy, random_keys, to_oracle
 
 pytestmark = pytest.mark.gpu
 
@@ -106,3 +106,27 @@ def test_sparse_attention_full_size_reference_case(cuda_device):
     dense = (torch.softmax(logits, -1)[:, None] @ sel_v)[:, 0]
     err = (out.float() - dense).abs()
     assert err.max().item() <= 2e-2 and err.mean().item() <= 2e-3
+
+
+@pytest.mark.parametrize("g,tg", [(16, 128), (64, 64), (32, 32)])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_append_kv_from_static_cache_matches_prepack(cuda_device, g, tg, dtype):
+    """popkv_append_kv (KV append fused with the re-encode) == prepack of all tokens, across a seal."""
+    gen = torch.Generator().manual_seed(g + tg)
+    kvh, t0, extra = 4, 3 * tg - 5, 9
+    full_k = random_keys(gen, (kvh, t0 + extra, 128), dtype, cuda_device)
+    full_v = torch.randn(kvh, t0 + extra, 128, generator=gen).to(dtype).to(cuda_device)
+    key_cache = torch.zeros(kvh, t0 + extra + 7, 128, dtype=dtype, device=cuda_device)
+    value_cache = torch.zeros_like(key_cache)
+    key_cache[:, :t0] = full_k[:, :t0]
+    value_cache[:, :t0] = full_v[:, :t0]
+    cache = P.build_popkv_cache(full_k[:, :t0], group_size=tg, dim_group_size=g, reserve_tokens=extra + 7)
+    for i in range(extra):
+        P.append_popkv_kv(cache, key_cache, value_cache, full_k[:, t0 + i], full_v[:, t0 + i])
+    torch.cuda.synchronize()
+    n = t0 + extra
+    assert cache.token_count == n and cache.sealed_tokens == (n // tg) * tg
+    assert torch.equal(key_cache[:, :n], full_k) and torch.equal(value_cache[:, :n], full_v)
+    want = C.pack_keys(full_k.contiguous(), token_group_size=tg, dim_group_size=g)
+    for got, exp in zip(cache.packed, want):
+        assert torch.equal(got[:, :n], exp[:, :n])
