@@ -48,11 +48,13 @@ PUBLISHED_MS_PER_LAYER = (1.365 + 1.814 + 3.600 + 0.143) / 30.0
 # DRAM traffic per launch (dram__bytes_read.sum + dram__bytes_write.sum) of the
 # step's kernels at the default workload, from one ncu --set full capture of
 # this script (profiles/score128_popcount_config1.md,
-# profiles/attn_partial_pipe_config1.md, profiles/topk16_cluster_config1.md).
+# profiles/attn_partial_pipe_config1.md, profiles/topk16_cluster_config1.md,
+# profiles/pack_rows_prepack_config1.md).
 NCU_TRAFFIC_CONFIG1 = {
-    "score_fused": 16_810_752,
+    "score_fused": 16_805_632,
     "attn_partial": 55_847_168 + 1_044_224,
     "topk": 2_136_832,
+    "prepack": 67_169_024 + 4_106_752,
 }
 DEFAULT_WORKLOAD = {"context": 32768, "budget": 4096, "batch": 1, "preset": "popkv-q"}
 L2_BYTES = 126 * 1024 * 1024
