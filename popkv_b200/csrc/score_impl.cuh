@@ -201,7 +201,19 @@ __device__ __forceinline__ float score_token(const QueryState<G>& st, const Toke
             const uint32_t qm = st.qm[w] & m;
             const uint32_t kmr = tp.km[w] & m;
             const uint32_t both = qm & kmr;
-            c_sign = 2 * __popc(match) - G;
+            if constexpr (G == 16) {
+                // Sign agreements of both 16-dim groups of word w at once on the
+                // integer pipe (SWAR popcount: byte 0 / byte 2 of `v` count the low
+                // / high half), leaving the popcount pipe to the other counts.
+                const uint32_t x = ~(st.qs[w] ^ tp.ks[w]);
+                uint32_t v = x - ((x >> 1) & 0x55555555u);
+                v = (v & 0x33333333u) + ((v >> 2) & 0x33333333u);
+                v = (v + (v >> 4)) & 0x0F0F0F0Fu;
+                v = v + (v >> 8);
+                c_sign = 2 * static_cast<int>((r & 1) ? ((v >> 16) & 0xFFu) : (v & 0xFFu)) - G;
+            } else {
+                c_sign = 2 * __popc(match) - G;
+            }
             c_q = 2 * __popc(match & qm) - st.pq[r];
             c_k = 2 * __popc(match & kmr) - tp.pk[r];
             c_qk = 2 * __popc(match & both) - __popc(both);
