@@ -167,6 +167,15 @@ __device__ __forceinline__ void load_token(const uint4* __restrict__ sign4, cons
     }
 }
 
+// Popcounts of the two 16-bit halves of x, in bytes 0 and 2 of the result,
+// computed on the integer pipe.
+__device__ __forceinline__ uint32_t swar_half_counts(uint32_t x) {
+    uint32_t v = x - ((x >> 1) & 0x55555555u);
+    v = (v & 0x33333333u) + ((v >> 2) & 0x33333333u);
+    v = (v + (v >> 4)) & 0x0F0F0F0Fu;
+    return v + (v >> 8);
+}
+
 // Unscaled score of one (query head, key token) pair: the sum over
 // representative groups of fma(ql*kl, c_sign, fma(dq*kl, c_q, fma(ql*dk, c_k,
 // (dq*dk)*c_qk))), every operation rounded as written.
@@ -174,6 +183,13 @@ template <int G>
 __device__ __forceinline__ float score_token(const QueryState<G>& st, const TokenPlanes<G>& tp) {
     constexpr int R = 128 / G;
     float total = 0.0f;
+    // G16: the two groups of each 32-bit word share one SWAR popcount of the
+    // sign agreements (on the integer pipe, not the popcount pipe).
+    uint32_t agree[4] = {0u, 0u, 0u, 0u};
+    if constexpr (G == 16) {
+#pragma unroll
+        for (int w = 0; w < 4; ++w) agree[w] = swar_half_counts(~(st.qs[w] ^ tp.ks[w]));
+    }
 #pragma unroll
     for (int r = 0; r < R; ++r) {
         int c_sign, c_q, c_k, c_qk;
@@ -202,14 +218,7 @@ __device__ __forceinline__ float score_token(const QueryState<G>& st, const Toke
             const uint32_t kmr = tp.km[w] & m;
             const uint32_t both = qm & kmr;
             if constexpr (G == 16) {
-                // Sign agreements of both 16-dim groups of word w at once on the
-                // integer pipe (SWAR popcount: byte 0 / byte 2 of `v` count the low
-                // / high half), leaving the popcount pipe to the other counts.
-                const uint32_t x = ~(st.qs[w] ^ tp.ks[w]);
-                uint32_t v = x - ((x >> 1) & 0x55555555u);
-                v = (v & 0x33333333u) + ((v >> 2) & 0x33333333u);
-                v = (v + (v >> 4)) & 0x0F0F0F0Fu;
-                v = v + (v >> 8);
+                const uint32_t v = agree[w];
                 c_sign = 2 * static_cast<int>((r & 1) ? ((v >> 16) & 0xFFu) : (v & 0xFFu)) - G;
             } else {
                 c_sign = 2 * __popc(match) - G;
