@@ -634,6 +634,15 @@ __global__ void attn_merge_kernel(const float* __restrict__ partials, int64_t sp
     const int64_t state = head_dim + 2;
     const float* p = partials + row * splits * state;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarps = blockDim.x >> 5;
+    // Up to 16 splits: each thread loads its dim of every split's accumulator up
+    // front, so those loads overlap the max/sum pass instead of following it.
+    constexpr int kPre = 16;
+    const bool pre = splits <= kPre && head_dim <= static_cast<int>(blockDim.x);
+    float acc_pre[kPre];
+    if (pre && tid < head_dim) {
+#pragma unroll
+        for (int sp = 0; sp < kPre; ++sp) acc_pre[sp] = sp < splits ? p[sp * state + 2 + tid] : 0.0f;
+    }
     float gm = -INFINITY;
     for (int64_t sp = tid; sp < splits; sp += blockDim.x) gm = fmaxf(gm, p[sp * state]);
 #pragma unroll
@@ -662,8 +671,14 @@ __global__ void attn_merge_kernel(const float* __restrict__ partials, int64_t sp
     den = s_den;
     for (int d = tid; d < head_dim; d += blockDim.x) {
         float num = 0.0f;
+        if (pre) {
+#pragma unroll
+            for (int sp = 0; sp < kPre; ++sp)
+                if (sp < splits) num = __fmaf_rn(acc_pre[sp], s_w[sp], num);
+        } else {
 #pragma unroll 4
-        for (int64_t sp = 0; sp < splits; ++sp) num = __fmaf_rn(p[sp * state + 2 + d], s_w[sp], num);
+            for (int64_t sp = 0; sp < splits; ++sp) num = __fmaf_rn(p[sp * state + 2 + d], s_w[sp], num);
+        }
         const float v = num / den;
         if constexpr (std::is_same<OT, float>::value) out[row * head_dim + d] = v;
         else if constexpr (std::is_same<OT, __half>::value) out[row * head_dim + d] = __float2half_rn(v);

@@ -78,6 +78,15 @@ __global__ void __launch_bounds__(kGatherThreads) merge_gather_kernel(
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     constexpr int nwarps = kGatherThreads / 32;
     if (tid == 0) s_failed = 0;
+    // Up to 16 splits: this thread's dim of every split's accumulator is loaded
+    // up front, overlapping the max/sum pass.
+    constexpr int kPre = 16;
+    const bool pre = splits <= kPre;
+    float acc_pre[kPre];
+    if (pre) {
+#pragma unroll
+        for (int sp = 0; sp < kPre; ++sp) acc_pre[sp] = sp < splits ? p[sp * state_len + 2 + tid] : 0.0f;
+    }
     float gm = -INFINITY;
     for (int64_t sp = tid; sp < splits; sp += kGatherThreads) gm = fmaxf(gm, p[sp * state_len]);
 #pragma unroll
@@ -105,8 +114,14 @@ __global__ void __launch_bounds__(kGatherThreads) merge_gather_kernel(
     __syncthreads();
     den = s_den;
     float num = 0.0f;
+    if (pre) {
+#pragma unroll
+        for (int sp = 0; sp < kPre; ++sp)
+            if (sp < splits) num = __fmaf_rn(acc_pre[sp], s_w[sp], num);
+    } else {
 #pragma unroll 4
-    for (int64_t sp = 0; sp < splits; ++sp) num = __fmaf_rn(p[sp * state_len + 2 + tid], s_w[sp], num);
+        for (int64_t sp = 0; sp < splits; ++sp) num = __fmaf_rn(p[sp * state_len + 2 + tid], s_w[sp], num);
+    }
     const uint32_t bits = out_bits<OT>(num / den);
 
     // Send: this row to every peer, as (bits, epoch) words.

@@ -61,19 +61,12 @@ extern "C" __attribute__((visibility("default"))) int popkv_score_phase_ns(unsig
 namespace popkv {
 namespace {
 
-constexpr int kMmaThreads = 128;  // thread t <-> token row t of the tile <-> TMEM lane t
 constexpr int kMmaTile = 128;     // MMA M
 constexpr int kMmaN = 16;         // 4 query heads x 4 counts
 constexpr int kKBlocks = 8;       // 128 dims x {uk, uk*km} bytes / 32 bytes per MMA
 constexpr int kABlockBytes = kMmaTile * 32;  // one k-block of A: 4 KB
 constexpr int kBBlockBytes = kMmaN * 32;     // one k-block of B: 512 B
 constexpr int kABytes = kKBlocks * kABlockBytes;
-static_assert(kABytes + kKBlocks * kBBlockBytes <= 48 * 1024, "A and B fit the dynamic shared memory");
-// 48 KB of dynamic shared memory (A, B and padding) holds residency at four
-// CTAs per SM, so four 128-column TMEM allocations fill the SM's 512 columns
-// and never wait on each other.
-constexpr size_t kMmaDynSmem = 48 * 1024;
-constexpr uint32_t kTmemCols = 128;
 constexpr int kMaxWaitPolls = 1 << 20;
 
 // ---------------------------------------------------------------------------
@@ -162,21 +155,6 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* mbar, uint32_t parity) {
     return false;
 }
 
-// 32 consecutive TMEM columns of this warp's 32 lanes: c[j] = column col + j.
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&c)[32]) {
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, "
-        "%12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, "
-        "%30, %31}, [%32];"
-        : "=r"(c[0]), "=r"(c[1]), "=r"(c[2]), "=r"(c[3]), "=r"(c[4]), "=r"(c[5]), "=r"(c[6]),
-          "=r"(c[7]), "=r"(c[8]), "=r"(c[9]), "=r"(c[10]), "=r"(c[11]), "=r"(c[12]), "=r"(c[13]),
-          "=r"(c[14]), "=r"(c[15]), "=r"(c[16]), "=r"(c[17]), "=r"(c[18]), "=r"(c[19]),
-          "=r"(c[20]), "=r"(c[21]), "=r"(c[22]), "=r"(c[23]), "=r"(c[24]), "=r"(c[25]),
-          "=r"(c[26]), "=r"(c[27]), "=r"(c[28]), "=r"(c[29]), "=r"(c[30]), "=r"(c[31])
-        : "r"(taddr));
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-}
-
 // Byte offset of (row, 16-byte chunk c16 of a 32-byte k-block row) inside a
 // k-block laid out as described at kmajor_desc.
 __device__ __forceinline__ uint32_t kblock_offset(int row, int c16) {
@@ -192,248 +170,6 @@ __device__ __forceinline__ void plane_slot(int q, int p, int& kb, int& c16) {
     const int li = p * G + (16 * q) % G;  // byte inside the group's 2G bytes
     kb = r * (G / 16) + li / 32;
     c16 = (li % 32) / 16;
-}
-
-// One token's packed planes as loaded (R = 128 / G fp16 representatives).
-template <int G>
-struct RawToken {
-    static constexpr int R = 128 / G;
-    uint4 s, m;
-    uint32_t l[R / 2], d[R / 2];
-};
-
-template <int G>
-__device__ __forceinline__ void fetch_token(const uint4* __restrict__ sign4, const uint4* __restrict__ mag4,
-                                            const uint16_t* __restrict__ lowp,
-                                            const uint16_t* __restrict__ deltap, int64_t t, RawToken<G>& rt) {
-    constexpr int R = 128 / G;
-    rt.s = __ldg(sign4 + t);
-    rt.m = __ldg(mag4 + t);
-    if constexpr (R == 8) {
-        const uint4 l4 = __ldg(reinterpret_cast<const uint4*>(lowp) + t);
-        const uint4 d4 = __ldg(reinterpret_cast<const uint4*>(deltap) + t);
-        rt.l[0] = l4.x; rt.l[1] = l4.y; rt.l[2] = l4.z; rt.l[3] = l4.w;
-        rt.d[0] = d4.x; rt.d[1] = d4.y; rt.d[2] = d4.z; rt.d[3] = d4.w;
-    } else if constexpr (R == 4) {
-        const uint2 l2 = __ldg(reinterpret_cast<const uint2*>(lowp) + t);
-        const uint2 d2 = __ldg(reinterpret_cast<const uint2*>(deltap) + t);
-        rt.l[0] = l2.x; rt.l[1] = l2.y;
-        rt.d[0] = d2.x; rt.d[1] = d2.y;
-    } else {
-        rt.l[0] = __ldg(reinterpret_cast<const uint32_t*>(lowp) + t);
-        rt.d[0] = __ldg(reinterpret_cast<const uint32_t*>(deltap) + t);
-    }
-}
-
-// One CTA per (batch, KV head, run of `tiles_per_cta` 128-token tiles); up to
-// four query heads per KV head.
-template <int G, typename QT>
-__global__ void __launch_bounds__(kMmaThreads, 4) score128_mma_kernel(
-    const QT* __restrict__ queries, const int32_t* __restrict__ k_sign, const int32_t* __restrict__ k_mag,
-    const uint16_t* __restrict__ k_low, const uint16_t* __restrict__ k_delta,
-    const int64_t* __restrict__ head_to_kv, uint16_t* __restrict__ scores, int q_heads, int group_heads,
-    int64_t capacity, int64_t tokens, int tiles_per_cta, float scale) {
-    constexpr int R = 128 / G;
-    extern __shared__ __align__(1024) unsigned char mma_smem[];
-    unsigned char* sA = mma_smem;            // kKBlocks x [128 rows x 32 B]
-    unsigned char* sB = mma_smem + kABytes;  // kKBlocks x [16 rows x 32 B]
-    __shared__ QueryState<G> states[4];
-    __shared__ float scratch[4][2 * 32 * 4];
-    __shared__ uint32_t u_table[16], m_table[16];
-    __shared__ __align__(8) uint64_t mbar;
-    __shared__ uint32_t tmem_base;
-    __shared__ int s_failed;
-
-    POPKV_SCORE_PHASE(0);
-    pdl_wait();
-    pdl_launch_dependents();
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int groups = q_heads / group_heads;
-    const int64_t b = blockIdx.y / groups;
-    const int grp = blockIdx.y % groups;
-    const int qh0 = grp * group_heads;
-    const int64_t row0 = b * q_heads + qh0;
-    const int64_t kvh = head_to_kv[qh0];
-
-    if (warp == 0) tmem_alloc(&tmem_base, kTmemCols);
-    if (tid == 0) {
-        mbar_init(&mbar, 1);
-        s_failed = 0;
-    }
-    if (tid < 16) {
-        // A nibble of sign bits -> four int8 lanes of +1 (bit set) / -1; a nibble
-        // of magnitude bits -> 0xFF / 0x00 byte masks.
-        uint32_t u = 0, m = 0;
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            u |= (((tid >> j) & 1) ? 0x01u : 0xFFu) << (8 * j);
-            m |= (((tid >> j) & 1) ? 0xFFu : 0x00u) << (8 * j);
-        }
-        u_table[tid] = u;
-        m_table[tid] = m;
-    }
-    if (warp < group_heads)
-        encode_query_row<QT, 4>(queries + (row0 + warp) * 128, 128, G, lane, scratch[warp], states[warp].qs,
-                                states[warp].qm, states[warp].ql, states[warp].dq);
-    __syncthreads();
-
-    // B: thread t fills column n = t / 8 (head n / 4, count n % 4) of k-block t % 8;
-    // each 16-byte half of a k-block row covers 16 consecutive dims of one plane.
-    {
-        const int n = tid >> 3, kb = tid & 7, h = n >> 2, cnt = n & 3;
-        const bool wants_k = cnt >= 2;  // c_k, c_qk pair with uk*km
-        const bool wants_qm = cnt & 1;  // c_q, c_qk use uq*qm
-        const int r = kb / (G / 16);
-        unsigned char* dstB = sB + kb * kBBlockBytes;
-#pragma unroll
-        for (int c16 = 0; c16 < 2; ++c16) {
-            const int li = (kb % (G / 16)) * 32 + 16 * c16;  // byte inside group r
-            const int p = li / G;
-            const int d0 = r * G + li % G;  // first of 16 dims, a multiple of 16
-            uint32_t w[4] = {0u, 0u, 0u, 0u};
-            if (h < group_heads && (p == 1) == wants_k) {
-                const uint32_t qs = states[h].qs[d0 >> 5] >> (d0 & 31);
-                const uint32_t qm = states[h].qm[d0 >> 5] >> (d0 & 31);
-#pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    const uint32_t u = u_table[(qs >> (4 * j)) & 15u];
-                    w[j] = wants_qm ? (u & m_table[(qm >> (4 * j)) & 15u]) : u;
-                }
-            }
-            *reinterpret_cast<uint4*>(dstB + kblock_offset(n, c16)) = make_uint4(w[0], w[1], w[2], w[3]);
-        }
-    }
-    if (tid < group_heads) finish_state<G>(states[tid]);
-    fence_async_smem();
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
-    const uint32_t tmem = tmem_base;
-    const uint32_t a_base = smem_addr(sA), b_base = smem_addr(sB);
-
-    const int64_t tiles = (tokens + kMmaTile - 1) / kMmaTile;
-    const int64_t first = static_cast<int64_t>(blockIdx.x) * tiles_per_cta;
-    const uint4* sign4 = reinterpret_cast<const uint4*>(k_sign) + kvh * capacity;
-    const uint4* mag4 = reinterpret_cast<const uint4*>(k_mag) + kvh * capacity;
-    const uint16_t* lowp = k_low + kvh * capacity * R;
-    const uint16_t* deltap = k_delta + kvh * capacity * R;
-    const int row = tid;
-    const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
-    POPKV_SCORE_PHASE(1);
-
-    uint32_t parity = 0;
-    RawToken<G> cur, nxt;
-    if (first < tiles) {
-        const int64_t t0 = first * kMmaTile + row;
-        fetch_token<G>(sign4, mag4, lowp, deltap, t0 < tokens ? t0 : 0, cur);
-    }
-    for (int it = 0; it < tiles_per_cta; ++it) {
-        const int64_t tile = first + it;
-        if (tile >= tiles) break;  // uniform across the CTA
-        const int64_t t = tile * kMmaTile + row;
-        const bool live = t < tokens;
-        if (it + 1 < tiles_per_cta && tile + 1 < tiles) {  // next tile's planes load under this tile
-            const int64_t tn = t + kMmaTile;
-            fetch_token<G>(sign4, mag4, lowp, deltap, tn < tokens ? tn : 0, nxt);
-        }
-        TokenPlanes<G> tp;
-        tp.ks[0] = cur.s.x; tp.ks[1] = cur.s.y; tp.ks[2] = cur.s.z; tp.ks[3] = cur.s.w;
-        tp.km[0] = cur.m.x; tp.km[1] = cur.m.y; tp.km[2] = cur.m.z; tp.km[3] = cur.m.w;
-#pragma unroll
-        for (int j = 0; j < R / 2; ++j) {
-            tp.kl[2 * j] = half_bits_to_float(static_cast<uint16_t>(cur.l[j] & 0xFFFFu));
-            tp.kl[2 * j + 1] = half_bits_to_float(static_cast<uint16_t>(cur.l[j] >> 16));
-            tp.dk[2 * j] = half_bits_to_float(static_cast<uint16_t>(cur.d[j] & 0xFFFFu));
-            tp.dk[2 * j + 1] = half_bits_to_float(static_cast<uint16_t>(cur.d[j] >> 16));
-        }
-        if (it == 0) POPKV_SCORE_PHASE(2);
-
-        // Expand this token's planes into row `row` of A.
-#pragma unroll
-        for (int q = 0; q < 8; ++q) {  // dims [16q, 16q + 16)
-            const uint32_t sw = tp.ks[q >> 1] >> ((q & 1) * 16);
-            const uint32_t mw = tp.km[q >> 1] >> ((q & 1) * 16);
-            uint32_t u[4], w[4];
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                u[j] = live ? u_table[(sw >> (4 * j)) & 15u] : 0u;
-                w[j] = u[j] & m_table[(mw >> (4 * j)) & 15u];
-            }
-            int kb, c16;
-            plane_slot<G>(q, 0, kb, c16);
-            *reinterpret_cast<uint4*>(sA + kb * kABlockBytes + kblock_offset(row, c16)) = make_uint4(u[0], u[1], u[2], u[3]);
-            plane_slot<G>(q, 1, kb, c16);
-            *reinterpret_cast<uint4*>(sA + kb * kABlockBytes + kblock_offset(row, c16)) = make_uint4(w[0], w[1], w[2], w[3]);
-        }
-        fence_async_smem();
-        tc_fence_before();  // previous tile's TMEM reads are ordered before the barrier
-        __syncthreads();
-        if (tid == 0) {
-            tc_fence_after();
-#pragma unroll
-            for (int r = 0; r < R; ++r) {
-#pragma unroll
-                for (int j = 0; j < G / 16; ++j) {
-                    const int kb = r * (G / 16) + j;
-                    mma_i8(tmem + static_cast<uint32_t>(r * kMmaN),
-                           kmajor_desc(a_base + static_cast<uint32_t>(kb * kABlockBytes)),
-                           kmajor_desc(b_base + static_cast<uint32_t>(kb * kBBlockBytes)), kIdesc, j > 0 ? 1u : 0u);
-                }
-            }
-            mma_commit(&mbar);
-        }
-        if (it == 0) POPKV_SCORE_PHASE(3);
-        const bool ok = mbar_wait(&mbar, parity);
-        parity ^= 1u;
-        if (!ok) s_failed = 1;
-        __syncthreads();
-        if (s_failed) break;  // uniform: every thread read the flag after the barrier
-        tc_fence_after();
-        if (it == 0) POPKV_SCORE_PHASE(4);
-
-        float total[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-#pragma unroll
-        for (int r2 = 0; r2 < R; r2 += 2) {  // two groups (32 columns) per TMEM load
-            uint32_t c[32];
-            tmem_ld32(tmem + lane_base + static_cast<uint32_t>(r2 * kMmaN), c);
-#pragma unroll
-            for (int rr = 0; rr < 2; ++rr) {
-                const int r = r2 + rr;
-                const float kl = tp.kl[r], dk = tp.dk[r];
-#pragma unroll
-                for (int h = 0; h < 4; ++h) {
-                    if (h < group_heads) {
-                        const int* cc = reinterpret_cast<const int*>(c) + rr * kMmaN + h * 4;
-                        const float ql = states[h].ql[r], dq = states[h].dq[r];
-                        const float t1 = __fmul_rn(ql, kl);
-                        const float t2 = __fmul_rn(dq, kl);
-                        const float t3 = __fmul_rn(ql, dk);
-                        const float t4 = __fmul_rn(__fmul_rn(dq, dk), small_int_to_float(cc[3]));
-                        const float chain = __fmaf_rn(t1, small_int_to_float(cc[0]),
-                                                      __fmaf_rn(t2, small_int_to_float(cc[1]),
-                                                                __fmaf_rn(t3, small_int_to_float(cc[2]), t4)));
-                        total[h] = __fadd_rn(total[h], chain);
-                    }
-                }
-            }
-        }
-        if (live) {
-#pragma unroll
-            for (int h = 0; h < 4; ++h)
-                if (h < group_heads)
-                    scores[(row0 + h) * tokens + t] = float_to_half_bits(__fmul_rn(total[h], scale));
-        }
-        if (it == 0) POPKV_SCORE_PHASE(5);
-        cur = nxt;
-    }
-    POPKV_SCORE_PHASE(6);
-    tc_fence_before();
-    __syncthreads();
-    if (warp == 0) {
-        tc_fence_after();
-        tmem_dealloc(tmem, kTmemCols);
-    }
-    POPKV_SCORE_PHASE(7);
 }
 
 // ---------------------------------------------------------------------------
@@ -531,7 +267,7 @@ __global__ void __launch_bounds__(kWsThreads, 2) score128_ws_kernel(
         encode_query_row<QT, 4>(queries + (row0 + warp) * 128, 128, G, lane, scratch[warp], states[warp].qs,
                                 states[warp].qm, states[warp].ql, states[warp].dq);
     __syncthreads();
-    if (tid < 128) {  // B, as in score128_mma_kernel
+    if (tid < 128) {  // B: thread t fills column t / 8 (head, count) of k-block t % 8
         const int n = tid >> 3, kb = tid & 7, h = n >> 2, cnt = n & 3;
         const bool wants_k = cnt >= 2;
         const bool wants_qm = cnt & 1;
