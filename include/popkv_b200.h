@@ -376,13 +376,119 @@ POPKV_API int popkv_peer_free(void* ptr);
  * Every rank must issue the same sequence of these calls on one set of
  * buffers.
  *
- * Replaces popkv_attn_merge followed by the per-layer NCCL all-gather of head
- * outputs (the sharded plan of the survey; sparse_kernels.py:367-387 for the
- * merge).
+ * Replaces popkv_attn_merge followed by a per-layer NCCL all-gather of the
+ * KV-head shards' attention outputs (sparse_kernels.py:367-387 for the merge).
  */
 POPKV_API int popkv_attn_merge_gather(const float* partials, int64_t rows, int64_t splits, int64_t head_dim,
                                       int out_dtype, int64_t rank, int64_t world, uint64_t* const* peer_recv,
                                       const uint64_t* own_recv, uint32_t* state, void* out, void* stream);
+
+/*
+ * Device-resident step lengths.  The reference passes the cache length as a
+ * Python integer on every decode call (popkv.py:1079-1099), so each token's
+ * launches differ.  The *_dyn entry points read it from device memory at run
+ * time instead (`tokens_dev` / `position_dev`: one int64, the number of cached
+ * prefix tokens = the current token's position).  One captured CUDA graph then
+ * serves every decode step while a kernel of the step advances the count.
+ * Host-side arguments give the upper bounds the launch is sized for; a device
+ * value outside [0, bound] is clamped to it.
+ */
+
+/*
+ * popkv_score (raw queries, head_dim 128, fp16 scores) over the first
+ * *tokens_dev <= max_tokens cached tokens.  Score row r starts at
+ * scores + r * score_stride (score_stride >= max_tokens).
+ * Replaces ext.score via popkv_cuda.score (csrc/popkv_ext.cu:1208-1313).
+ */
+POPKV_API int popkv_score_dyn(const void* queries, int queries_dtype, int64_t batch, int64_t q_heads,
+                              const int32_t* k_sign, const int32_t* k_mag, const uint16_t* k_low,
+                              const uint16_t* k_delta, int64_t kv_heads, int64_t capacity,
+                              const int64_t* head_to_kv, const int64_t* tokens_dev, int64_t max_tokens,
+                              int64_t dim_group_size, uint16_t* scores, int64_t score_stride, void* stream);
+
+/*
+ * popkv_topk over fp16 rows of t = *tokens_dev scores with k = min(k_max, t)
+ * and the current slot t at out[r*out_stride + k] (out_stride >= k_max + 1).
+ * max_tokens <= 131072.  Replaces torch.topk + _append_current
+ * (popkv.py:1090-1099, :287-291).
+ */
+POPKV_API int popkv_topk_dyn(const uint16_t* scores, int64_t rows, const int64_t* tokens_dev,
+                             int64_t max_tokens, int64_t row_stride, int64_t k_max, int64_t* out,
+                             int64_t out_stride, void* stream);
+
+/*
+ * Split partials + merge (popkv_attn_partial + popkv_attn_merge) for
+ * head_dim 128 and fp16/bf16 queries, K/V of the query dtype, with
+ * t = *tokens_dev prefix tokens.
+ *
+ * With `indices` (rows of index_stride >= k_max + 1 int64, as written by
+ * popkv_topk_dyn) a row attends over its min(k_max, t) + 1 selected slots;
+ * with indices NULL it attends over every prefix token plus the current one
+ * (the dense layers; as the reference's full-attention branch, popkv.py:1023-1036).
+ * partials holds batch * q_heads * S * 130 fp32, S = ceil(m / split_tokens)
+ * with m = min(k_max, max_tokens) + 1 (indices) or max_tokens + 1 (dense);
+ * out [batch, q_heads, 128] of out_dtype, or NULL to leave the merge to the
+ * caller (popkv_attn_merge_gather on several GPUs).
+ * Replaces sparse_kernels.indexed_attention_split_partial + _merge
+ * (sparse_kernels.py:321-387).
+ */
+POPKV_API int popkv_attn_dyn(const void* queries, int queries_dtype, int64_t batch, int64_t q_heads,
+                             const void* prefix_keys, const void* prefix_values, int kv_dtype,
+                             int64_t kv_heads, int64_t max_tokens, int64_t k_batch_stride,
+                             int64_t k_head_stride, int64_t k_token_stride, int64_t v_batch_stride,
+                             int64_t v_head_stride, int64_t v_token_stride, const void* current_keys,
+                             const void* current_values, const int64_t* tokens_dev,
+                             const int64_t* indices, int64_t index_stride, int64_t k_max,
+                             const int64_t* head_to_kv, int64_t split_tokens, float* partials,
+                             void* out, int out_dtype, void* stream);
+
+/*
+ * popkv_append_kv at position p = *position_dev (< max_tokens <= capacity):
+ * re-encodes the open token group [p - p % token_group_size, p] of the key
+ * cache into the packed planes.  With new_keys/new_values [kv_heads, 128] the
+ * row p of the caches is written from them first; with both NULL the caller
+ * has already written row p (popkv_rope_append does).
+ * Replaces append_kv + append_retrieval_caches (popkv.py:965-972, :884-943).
+ */
+POPKV_API int popkv_append_kv_dyn(const void* new_keys, const void* new_values, int dtype,
+                                  int64_t kv_heads, int64_t head_dim, void* cache_keys,
+                                  void* cache_values, int64_t k_head_stride, int64_t k_token_stride,
+                                  int64_t v_head_stride, int64_t v_token_stride,
+                                  const int64_t* position_dev, int64_t max_tokens, int32_t* k_sign,
+                                  int32_t* k_mag, uint16_t* k_low, uint16_t* k_delta,
+                                  int64_t capacity, int64_t token_group_size,
+                                  int64_t dim_group_size, void* stream);
+
+/*
+ * Decode-loop glue for a Llama-shaped model, bf16 only.
+ *
+ * popkv_rms_norm: per row of `dim`, with delta non-NULL hidden <- hidden +
+ * delta first (the residual add, written back), then out = RMSNorm(hidden) *
+ * weight.  Follows transformers' LlamaRMSNorm as called by the reference
+ * decoder (popkv.py:1011, :1109; decode_runtime.py:39) with the rounding points
+ * of its eager ops.
+ *
+ * popkv_rope_append: qkv [batch, (q_heads + 2 kv_heads) * 128] (q | k | v rows
+ * of the fused projection); rotary embedding at position p = *position_dev
+ * (clamped to max_position) from bf16 tables cos/sin [max_position + 1, 64];
+ * writes the rotated queries to q_out [batch, q_heads, 128], the rotated keys
+ * and the values to k_cur/v_cur [batch, kv_heads, 128] and to row p of the
+ * caches.  Replaces _apply_rope (popkv.py:745-749) and append_kv
+ * (popkv.py:965-972).
+ *
+ * popkv_silu_mul: act [rows, inter] = silu(gate) * up for gate_up
+ * [rows, 2 * inter] = [gate | up] (the reference model's LlamaMLP).
+ */
+POPKV_API int popkv_rms_norm(const void* delta, void* hidden, const void* weight, int64_t rows,
+                             int64_t dim, float eps, void* out, void* stream);
+POPKV_API int popkv_rope_append(const void* qkv, int64_t batch, int64_t q_heads, int64_t kv_heads,
+                                int64_t head_dim, const void* cos_table, const void* sin_table,
+                                const int64_t* position_dev, int64_t max_position, void* q_out,
+                                void* k_cur, void* v_cur, void* k_cache, void* v_cache,
+                                int64_t k_batch_stride, int64_t k_head_stride, int64_t k_token_stride,
+                                int64_t v_batch_stride, int64_t v_head_stride, int64_t v_token_stride,
+                                void* stream);
+POPKV_API int popkv_silu_mul(const void* gate_up, int64_t rows, int64_t inter, void* act, void* stream);
 
 #ifdef __cplusplus
 }

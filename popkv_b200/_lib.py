@@ -49,6 +49,16 @@ _SIGNATURES = {
     "popkv_attn_merge_gather": ([_P, _L, _L, _L, _I, _L, _L, _P, _P, _P, _P, _P], _I),
     "popkv_retrieve": ([_P, _I, _L, _L, _L, _P, _P, _P, _P, _L, _L, _L, _L, _L, _P, _P, _P, _I,
                         _L, _L, _L, _L, _L, _L, _P, _P, _L, _P, _P, _P, _P], _I),
+    "popkv_score_dyn": ([_P, _I, _L, _L, _P, _P, _P, _P, _L, _L, _P, _P, _L, _L, _P, _L, _P], _I),
+    "popkv_topk_dyn": ([_P, _L, _P, _L, _L, _L, _P, _L, _P], _I),
+    "popkv_attn_dyn": ([_P, _I, _L, _L, _P, _P, _I, _L, _L, _L, _L, _L, _L, _L, _L, _P, _P, _P,
+                        _P, _L, _L, _P, _L, _P, _P, _I, _P], _I),
+    "popkv_append_kv_dyn": ([_P, _P, _I, _L, _L, _P, _P, _L, _L, _L, _L, _P, _L, _P, _P, _P, _P,
+                             _L, _L, _L, _P], _I),
+    "popkv_rms_norm": ([_P, _P, _P, _L, _L, ctypes.c_float, _P, _P], _I),
+    "popkv_rope_append": ([_P, _L, _L, _L, _L, _P, _P, _P, _L, _P, _P, _P, _P, _P, _L, _L, _L,
+                           _L, _L, _L, _P], _I),
+    "popkv_silu_mul": ([_P, _L, _L, _P, _P], _I),
 }
 
 _lock = threading.Lock()

@@ -321,11 +321,19 @@ __global__ void __launch_bounds__(kAttnThreads, 4) attn_partial_pipe_kernel(
     float* __restrict__ partials, int q_heads, int kv_heads, int64_t prefix_tokens,
     int64_t kbs, int64_t khs, int64_t kts, int64_t vbs, int64_t vhs, int64_t vts,
     int64_t selected, int64_t split_tokens, int splits, float scale, int* __restrict__ counters,
-    OT* __restrict__ merged) {
+    OT* __restrict__ merged, int64_t index_stride, const int64_t* __restrict__ dyn_tokens) {
     extern __shared__ __align__(16) unsigned char ring[];  // [stage][K|V][32 rows][256 B]
     POPKV_ATTN_PHASE(0);
     pdl_wait();
     pdl_launch_dependents();
+    if (dyn_tokens) {
+        // Device-resident prefix length: `prefix_tokens` and `selected` are the
+        // upper bounds the grid was sized for.  Without indices every prefix
+        // token is a slot (dense attention), plus the current one.
+        const int64_t t = *dyn_tokens;
+        prefix_tokens = t < 0 ? 0 : (t < prefix_tokens ? t : prefix_tokens);
+        selected = indices ? min(selected - 1, prefix_tokens) + 1 : prefix_tokens + 1;
+    }
     __shared__ float s_m[kAttnThreads / 32], s_s[kAttnThreads / 32];
     __shared__ float s_acc[kAttnThreads / 32][8][16];
 
@@ -338,7 +346,7 @@ __global__ void __launch_bounds__(kAttnThreads, 4) attn_partial_pipe_kernel(
     const int split = blockIdx.x;
     const int64_t slot0 = static_cast<int64_t>(split) * split_tokens;
     const int64_t slot_end = min(slot0 + split_tokens, selected);
-    const int nsub = static_cast<int>((slot_end - slot0 + kPipeRows - 1) / kPipeRows);
+    const int nsub = slot_end > slot0 ? static_cast<int>((slot_end - slot0 + kPipeRows - 1) / kPipeRows) : 0;
 
     const unsigned char* kb = reinterpret_cast<const unsigned char*>(prefix_k + b * kbs + kvh * khs) + c * 16;
     const unsigned char* vb = reinterpret_cast<const unsigned char*>(prefix_v + b * vbs + kvh * vhs) + c * 16;
@@ -352,8 +360,8 @@ __global__ void __launch_bounds__(kAttnThreads, 4) attn_partial_pipe_kernel(
     for (int j = tid; j < kPipeRows * kPipeMaxSub; j += kAttnThreads) {
         const int64_t slot = slot0 + j;
         int id = kSlotMasked;
-        if (slot < slot_end && (!valid || valid[row * selected + slot])) {
-            const int64_t idx = __ldg(indices + row * selected + slot);
+        if (slot < slot_end && (!valid || valid[row * index_stride + slot])) {
+            const int64_t idx = indices ? __ldg(indices + row * index_stride + slot) : slot;
             id = idx == prefix_tokens ? kSlotCurrent
                                       : static_cast<int>(idx < 0 ? 0 : (idx > prefix_tokens - 1 ? prefix_tokens - 1 : idx));
         }
@@ -711,7 +719,8 @@ int launch_partial(const void* queries, int64_t batch, int64_t q_heads, int64_t 
             static_cast<const KT*>(ck), static_cast<const KT*>(cv), indices, valid, head_to_kv,
             partials, static_cast<int>(q_heads), static_cast<int>(kv_heads), prefix_tokens, kbs,
             khs, kts, vbs, vhs, vts, selected, split_tokens, static_cast<int>(splits), scale,
-            static_cast<int*>(nullptr), static_cast<void*>(nullptr));
+            static_cast<int*>(nullptr), static_cast<void*>(nullptr), selected,
+            static_cast<const int64_t*>(nullptr));
         if (err != cudaSuccess)
             return fail(POPKV_ERR_CUDA, "popkv_attn_partial: %s", cudaGetErrorString(err));
     } else if (vec_ok) {
@@ -760,7 +769,8 @@ int launch_partial_merged(const void* queries, int64_t batch, int64_t q_heads, i
             static_cast<const KT*>(ck), static_cast<const KT*>(cv), indices, valid, head_to_kv,
             partials, static_cast<int>(q_heads), static_cast<int>(kv_heads), prefix_tokens, kbs,
             khs, kts, vbs, vhs, vts, selected, split_tokens, static_cast<int>(splits),
-            score_scale_for(head_dim), counters, static_cast<OT*>(out));
+            score_scale_for(head_dim), counters, static_cast<OT*>(out), selected,
+            static_cast<const int64_t*>(nullptr));
         return check_launch("popkv_attn_partial_merge");
     }
     return POPKV_ERR_UNSUPPORTED;
@@ -913,4 +923,86 @@ extern "C" int popkv_attn_partial_merge(
     if (st != POPKV_OK) return st;
     return popkv_attn_merge(partials, batch * q_heads, (selected + split_tokens - 1) / split_tokens,
                             head_dim, out, out_dtype, stream);
+}
+
+namespace popkv {
+namespace {
+
+template <typename QT, typename KT>
+int launch_partial_dyn(const void* queries, int64_t batch, int64_t q_heads, const void* pk,
+                       const void* pv, int64_t kv_heads, int64_t max_tokens, int64_t kbs, int64_t khs,
+                       int64_t kts, int64_t vbs, int64_t vhs, int64_t vts, const void* ck,
+                       const void* cv, const int64_t* tokens_dev, const int64_t* indices,
+                       int64_t index_stride, int64_t max_selected, const int64_t* head_to_kv,
+                       int64_t split_tokens, int64_t splits, float* partials, cudaStream_t stream) {
+    constexpr size_t ring_bytes = static_cast<size_t>(kPipeStages) * 2 * kPipeRows * kRowBytes;
+    const int st = allow_dynamic_smem(attn_partial_pipe_kernel<QT, KT, void>, static_cast<int>(ring_bytes));
+    if (st != POPKV_OK) return st;
+    const dim3 grid(static_cast<unsigned>(splits), static_cast<unsigned>(batch * q_heads));
+    const cudaError_t err = launch_pdl(
+        attn_partial_pipe_kernel<QT, KT, void>, grid, dim3(kAttnThreads), ring_bytes, stream, 1,
+        static_cast<const QT*>(queries), static_cast<const KT*>(pk), static_cast<const KT*>(pv),
+        static_cast<const KT*>(ck), static_cast<const KT*>(cv), indices,
+        static_cast<const uint8_t*>(nullptr), head_to_kv, partials, static_cast<int>(q_heads),
+        static_cast<int>(kv_heads), max_tokens, kbs, khs, kts, vbs, vhs, vts, max_selected,
+        split_tokens, static_cast<int>(splits), score_scale_for(128), static_cast<int*>(nullptr),
+        static_cast<void*>(nullptr), index_stride, tokens_dev);
+    if (err != cudaSuccess) return fail(POPKV_ERR_CUDA, "popkv_attn_dyn: %s", cudaGetErrorString(err));
+    return check_launch("popkv_attn_dyn");
+}
+
+}  // namespace
+}  // namespace popkv
+
+extern "C" int popkv_attn_dyn(const void* queries, int queries_dtype, int64_t batch, int64_t q_heads,
+                              const void* prefix_keys, const void* prefix_values, int kv_dtype,
+                              int64_t kv_heads, int64_t max_tokens, int64_t k_batch_stride,
+                              int64_t k_head_stride, int64_t k_token_stride, int64_t v_batch_stride,
+                              int64_t v_head_stride, int64_t v_token_stride, const void* current_keys,
+                              const void* current_values, const int64_t* tokens_dev,
+                              const int64_t* indices, int64_t index_stride, int64_t k_max,
+                              const int64_t* head_to_kv, int64_t split_tokens, float* partials,
+                              void* out, int out_dtype, void* stream) {
+    using namespace popkv;
+    if (queries_dtype != POPKV_DTYPE_BF16 && queries_dtype != POPKV_DTYPE_F16)
+        return fail(POPKV_ERR_UNSUPPORTED, "popkv_attn_dyn: queries must be fp16/bf16");
+    if (kv_dtype != queries_dtype)
+        return fail(POPKV_ERR_UNSUPPORTED, "popkv_attn_dyn: keys/values must have the query dtype");
+    if (!valid_dtype(out_dtype)) return fail(POPKV_ERR_INVALID, "popkv_attn_dyn: output must be fp32/fp16/bf16");
+    if (batch < 0 || q_heads <= 0 || kv_heads <= 0 || max_tokens < 0 || split_tokens <= 0)
+        return fail(POPKV_ERR_INVALID, "popkv_attn_dyn: invalid shape");
+    if (split_tokens > kPipeRows * kPipeMaxSub)
+        return fail(POPKV_ERR_UNSUPPORTED, "popkv_attn_dyn: split_tokens above %d", kPipeRows * kPipeMaxSub);
+    if (indices && (k_max < 0 || index_stride < k_max + 1))
+        return fail(POPKV_ERR_INVALID, "popkv_attn_dyn: index rows must hold k_max + 1 slots");
+    const int64_t max_selected = indices ? (k_max < max_tokens ? k_max : max_tokens) + 1 : max_tokens + 1;
+    const int64_t splits = (max_selected + split_tokens - 1) / split_tokens;
+    if (splits > kMergeMaxSplits)
+        return fail(POPKV_ERR_UNSUPPORTED, "popkv_attn_dyn: more than %d splits", kMergeMaxSplits);
+    if (batch * q_heads > 65535) return fail(POPKV_ERR_UNSUPPORTED, "popkv_attn_dyn: batch * q_heads above 65535");
+    if (batch == 0) return POPKV_OK;
+    if (!queries || !prefix_keys || !prefix_values || !current_keys || !current_values || !tokens_dev ||
+        !head_to_kv || !partials)
+        return fail(POPKV_ERR_INVALID, "popkv_attn_dyn: null pointer");
+    const int64_t es = 2;
+    if (!aligned(prefix_keys, 16) || !aligned(prefix_values, 16) || !aligned(current_keys, 16) ||
+        !aligned(current_values, 16) || (k_batch_stride * es) % 16 || (k_head_stride * es) % 16 ||
+        (k_token_stride * es) % 16 || (v_batch_stride * es) % 16 || (v_head_stride * es) % 16 ||
+        (v_token_stride * es) % 16)
+        return fail(POPKV_ERR_INVALID, "popkv_attn_dyn: K/V buffers and strides must be 16-byte aligned");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const int st =
+        queries_dtype == POPKV_DTYPE_BF16
+            ? launch_partial_dyn<__nv_bfloat16, __nv_bfloat16>(
+                  queries, batch, q_heads, prefix_keys, prefix_values, kv_heads, max_tokens,
+                  k_batch_stride, k_head_stride, k_token_stride, v_batch_stride, v_head_stride,
+                  v_token_stride, current_keys, current_values, tokens_dev, indices, index_stride,
+                  max_selected, head_to_kv, split_tokens, splits, partials, s)
+            : launch_partial_dyn<__half, __half>(
+                  queries, batch, q_heads, prefix_keys, prefix_values, kv_heads, max_tokens,
+                  k_batch_stride, k_head_stride, k_token_stride, v_batch_stride, v_head_stride,
+                  v_token_stride, current_keys, current_values, tokens_dev, indices, index_stride,
+                  max_selected, head_to_kv, split_tokens, splits, partials, s);
+    if (st != POPKV_OK || !out) return st;
+    return popkv_attn_merge(partials, batch * q_heads, splits, 128, out, out_dtype, stream);
 }

@@ -253,7 +253,8 @@ __global__ void __launch_bounds__(kRowThreads) pack_rows_kernel(
     int64_t token_group, int32_t* __restrict__ k_sign, int32_t* __restrict__ k_mag,
     uint16_t* __restrict__ k_low, uint16_t* __restrict__ k_delta, int64_t capacity,
     int64_t token_offset, const T* __restrict__ new_keys = nullptr, const T* __restrict__ new_values = nullptr,
-    T* __restrict__ values = nullptr, int64_t v_head_stride = 0, int64_t v_token_stride = 0) {
+    T* __restrict__ values = nullptr, int64_t v_head_stride = 0, int64_t v_token_stride = 0,
+    const int64_t* __restrict__ dyn_position = nullptr) {
     constexpr int D = 128, R = D / G, kSlices = kRowThreads / D;
     constexpr int kRowBytes = D * static_cast<int>(sizeof(T)) + 16;
     constexpr int kChunks = D * static_cast<int>(sizeof(T)) / 16;
@@ -263,6 +264,18 @@ __global__ void __launch_bounds__(kRowThreads) pack_rows_kernel(
     float* part = smem + 2 * D;          // [kSlices][2][D]
     unsigned char* tile = reinterpret_cast<unsigned char*>(smem + (2 + 2 * kSlices) * D);
 
+    if (dyn_position) {
+        // Append at a device-resident position (one CTA column, the graph-replayed
+        // decode loop): `tokens` bounds the position; the open group runs from
+        // the last group boundary to it.
+        int64_t pos = *dyn_position;
+        pos = pos < 0 ? 0 : (pos < tokens ? pos : tokens - 1);
+        const int64_t sealed = pos - pos % token_group;
+        keys += sealed * token_stride;
+        if (values) values += sealed * v_token_stride;
+        token_offset = sealed;
+        tokens = pos - sealed + 1;
+    }
     const int64_t kvh = blockIdx.y;
     const int64_t t0 = static_cast<int64_t>(blockIdx.x) * token_group;
     const int64_t t1 = min(t0 + token_group, tokens);
@@ -562,6 +575,59 @@ extern "C" int popkv_append_kv(const void* new_keys, const void* new_values, int
             static_cast<const T*>(new_values), static_cast<T*>(cache_values) + sealed * v_token_stride,
             v_head_stride, v_token_stride);
         return check_launch("popkv_append_kv");
+    };
+    auto by_g = [&](auto tag) -> int {
+        if (dim_group_size == 16) return run(tag, std::integral_constant<int, 16>{});
+        if (dim_group_size == 32) return run(tag, std::integral_constant<int, 32>{});
+        return run(tag, std::integral_constant<int, 64>{});
+    };
+    if (dtype == POPKV_DTYPE_F32) return by_g(float{});
+    if (dtype == POPKV_DTYPE_F16) return by_g(__half{});
+    return by_g(__nv_bfloat16{});
+}
+
+extern "C" int popkv_append_kv_dyn(const void* new_keys, const void* new_values, int dtype,
+                                   int64_t kv_heads, int64_t head_dim, void* cache_keys,
+                                   void* cache_values, int64_t k_head_stride, int64_t k_token_stride,
+                                   int64_t v_head_stride, int64_t v_token_stride,
+                                   const int64_t* position_dev, int64_t max_tokens, int32_t* k_sign,
+                                   int32_t* k_mag, uint16_t* k_low, uint16_t* k_delta,
+                                   int64_t capacity, int64_t token_group_size,
+                                   int64_t dim_group_size, void* stream) {
+    using namespace popkv;
+    if (!valid_dtype(dtype)) return fail(POPKV_ERR_INVALID, "popkv_append_kv_dyn: keys must be fp32/fp16/bf16");
+    if (head_dim != 128) return fail(POPKV_ERR_UNSUPPORTED, "popkv_append_kv_dyn: head_dim must be 128");
+    if (kv_heads <= 0 || kv_heads > 65535) return fail(POPKV_ERR_INVALID, "popkv_append_kv_dyn: invalid KV head count");
+    if (dim_group_size != 16 && dim_group_size != 32 && dim_group_size != 64)
+        return fail(POPKV_ERR_INVALID, "dim_group_size must be 16, 32, or 64");
+    if (token_group_size < 1 || token_group_size > 128)
+        return fail(POPKV_ERR_UNSUPPORTED, "popkv_append_kv_dyn: token_group_size must be at most 128");
+    if (max_tokens <= 0 || max_tokens > capacity)
+        return fail(POPKV_ERR_CAPACITY, "popkv_append_kv_dyn: max_tokens must be in [1, capacity]");
+    if ((new_keys == nullptr) != (new_values == nullptr))
+        return fail(POPKV_ERR_INVALID, "popkv_append_kv_dyn: new keys and values go together");
+    if (!cache_keys || !cache_values || !k_sign || !k_mag || !k_low || !k_delta || !position_dev)
+        return fail(POPKV_ERR_INVALID, "popkv_append_kv_dyn: null pointer");
+    const int64_t es = static_cast<int64_t>(dtype_size(dtype));
+    if ((new_keys && (!aligned(new_keys, 16) || !aligned(new_values, 16))) || !aligned(cache_keys, 16) ||
+        !aligned(cache_values, 16) || (k_head_stride * es) % 16 || (k_token_stride * es) % 16 ||
+        (v_head_stride * es) % 16 || (v_token_stride * es) % 16 || !aligned(k_sign, 16) || !aligned(k_mag, 16))
+        return fail(POPKV_ERR_INVALID, "popkv_append_kv_dyn: buffers and strides must be 16-byte aligned");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const dim3 grid(1, static_cast<unsigned>(kv_heads));
+    auto run = [&](auto tag, auto gtag) -> int {
+        using T = decltype(tag);
+        constexpr int G = decltype(gtag)::value;
+        const size_t smem = sizeof(float) * 128 * (2 + 2 * (kRowThreads / 128)) +
+                            static_cast<size_t>(token_group_size) * (128 * sizeof(T) + 16);
+        const int st = allow_dynamic_smem(pack_rows_kernel<T, G>, static_cast<int>(smem));
+        if (st != POPKV_OK) return st;
+        pack_rows_kernel<T, G><<<grid, kRowThreads, smem, s>>>(
+            static_cast<const T*>(cache_keys), k_head_stride, k_token_stride, max_tokens, token_group_size,
+            k_sign, k_mag, k_low, k_delta, capacity, 0, static_cast<const T*>(new_keys),
+            static_cast<const T*>(new_values), static_cast<T*>(cache_values), v_head_stride,
+            v_token_stride, position_dev);
+        return check_launch("popkv_append_kv_dyn");
     };
     auto by_g = [&](auto tag) -> int {
         if (dim_group_size == 16) return run(tag, std::integral_constant<int, 16>{});

@@ -71,13 +71,21 @@ __global__ void __launch_bounds__(kScoreThreads, 4) score128_kernel(
     const int32_t* __restrict__ k_mag, const uint16_t* __restrict__ k_low,
     const uint16_t* __restrict__ k_delta, const int64_t* __restrict__ head_to_kv,
     uint16_t* __restrict__ scores, int q_heads, int group_heads, int64_t capacity,
-    int64_t tokens, float scale, uint32_t* __restrict__ hist = nullptr) {
+    int64_t tokens, float scale, uint32_t* __restrict__ hist, int64_t score_stride,
+    const int64_t* __restrict__ dyn_tokens) {
     constexpr int R = 128 / G;
     extern __shared__ uint32_t hist_s[];  // [group_heads][2048] when HIST
     __shared__ QueryState<G> states[kMaxGroupHeads];
     __shared__ float scratch[kScoreThreads / 32][2 * 32 * 4];
 
     pdl_wait();
+    if (dyn_tokens) {
+        // Device-resident token count (the graph-replayed decode loop); the grid
+        // and `tokens` cover its upper bound.
+        const int64_t t = *dyn_tokens;
+        tokens = t < 0 ? 0 : (t < tokens ? t : tokens);
+        if (static_cast<int64_t>(blockIdx.x) * kScoreTile >= tokens) return;
+    }
     const int groups = q_heads / group_heads;
     const int64_t b = blockIdx.y / groups;
     const int grp = blockIdx.y % groups;
@@ -125,7 +133,7 @@ __global__ void __launch_bounds__(kScoreThreads, 4) score128_kernel(
 
     for (int h = 0; h < group_heads; ++h) {
         const QueryState<G>& st = states[h];
-        uint16_t* out = scores + (row0 + h) * tokens;
+        uint16_t* out = scores + (row0 + h) * score_stride;
 #pragma unroll
         for (int i = 0; i < kTokensPerThread; ++i) {
             const float total = score_token<G>(st, tp[i]);
@@ -222,7 +230,8 @@ int launch_score128_hist(const void* queries, int64_t batch, int64_t q_heads, co
         static_cast<const QT*>(queries), static_cast<const int32_t*>(nullptr),
         static_cast<const int32_t*>(nullptr), static_cast<const float*>(nullptr),
         static_cast<const float*>(nullptr), k_sign, k_mag, k_low, k_delta, head_to_kv, scores,
-        static_cast<int>(q_heads), group_heads, capacity, tokens, score_scale_for(128), hist);
+        static_cast<int>(q_heads), group_heads, capacity, tokens, score_scale_for(128), hist, tokens,
+        static_cast<const int64_t*>(nullptr));
     if (err != cudaSuccess) return fail(POPKV_ERR_CUDA, "popkv_score_hist: %s", cudaGetErrorString(err));
     return check_launch("popkv_score_hist");
 }
@@ -233,7 +242,8 @@ int launch_score128(const void* queries, const int32_t* q_sign, const int32_t* q
                     const int32_t* k_sign, const int32_t* k_mag, const uint16_t* k_low,
                     const uint16_t* k_delta, int64_t kv_heads, int64_t capacity,
                     const int64_t* head_to_kv, int64_t tokens, uint16_t* scores,
-                    cudaStream_t stream) {
+                    cudaStream_t stream, int64_t score_stride = -1,
+                    const int64_t* dyn_tokens = nullptr) {
     const int group_heads = static_cast<int>(q_heads / kv_heads);
     const int64_t tiles = (tokens + kScoreTile - 1) / kScoreTile;
     dim3 grid(static_cast<unsigned>(tiles), static_cast<unsigned>(batch * kv_heads));
@@ -241,7 +251,8 @@ int launch_score128(const void* queries, const int32_t* q_sign, const int32_t* q
         score128_kernel<G, QT, RAW, false>, grid, dim3(kScoreThreads), 0, stream, 1,
         static_cast<const QT*>(queries), q_sign, q_mag, q_low, q_delta, k_sign, k_mag, k_low,
         k_delta, head_to_kv, scores, static_cast<int>(q_heads), group_heads, capacity, tokens,
-        score_scale_for(128), static_cast<uint32_t*>(nullptr));
+        score_scale_for(128), static_cast<uint32_t*>(nullptr), score_stride < 0 ? tokens : score_stride,
+        dyn_tokens);
     if (err != cudaSuccess) return fail(POPKV_ERR_CUDA, "popkv_score: %s", cudaGetErrorString(err));
     return check_launch("popkv_score");
 }
@@ -452,4 +463,40 @@ extern "C" int popkv_score_hist(const void* queries, int queries_dtype, int64_t 
     POPKV_SH_T(__nv_bfloat16)
 #undef POPKV_SH_T
 #undef POPKV_SH
+}
+
+extern "C" int popkv_score_dyn(const void* queries, int queries_dtype, int64_t batch, int64_t q_heads,
+                               const int32_t* k_sign, const int32_t* k_mag, const uint16_t* k_low,
+                               const uint16_t* k_delta, int64_t kv_heads, int64_t capacity,
+                               const int64_t* head_to_kv, const int64_t* tokens_dev,
+                               int64_t max_tokens, int64_t dim_group_size, uint16_t* scores,
+                               int64_t score_stride, void* stream) {
+    using namespace popkv;
+    if (!valid_dtype(queries_dtype)) return fail(POPKV_ERR_INVALID, "queries must be fp32/fp16/bf16");
+    int st = check_score_common(batch, q_heads, kv_heads, capacity, max_tokens, dim_group_size, head_to_kv);
+    if (st != POPKV_OK) return st;
+    if (q_heads / kv_heads > kMaxGroupHeads)
+        return fail(POPKV_ERR_UNSUPPORTED, "more than %d query heads per KV head", kMaxGroupHeads);
+    if (score_stride < max_tokens) return fail(POPKV_ERR_INVALID, "popkv_score_dyn: score_stride < max_tokens");
+    if (batch == 0) return POPKV_OK;
+    if (!queries || !k_sign || !k_mag || !k_low || !k_delta || !scores || !tokens_dev)
+        return fail(POPKV_ERR_INVALID, "popkv_score_dyn: null pointer");
+    if (!aligned(k_sign, 16) || !aligned(k_mag, 16) || !aligned(k_low, 16) || !aligned(k_delta, 16))
+        return fail(POPKV_ERR_INVALID, "packed planes must be 16-byte aligned");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    auto by_g = [&](auto tag) -> int {
+        using QT = decltype(tag);
+        const QT* q = static_cast<const QT*>(queries);
+#define POPKV_SD(G_)                                                                                  \
+    return launch_score128<G_, QT, true>(q, nullptr, nullptr, nullptr, nullptr, batch, q_heads, k_sign, \
+                                         k_mag, k_low, k_delta, kv_heads, capacity, head_to_kv,         \
+                                         max_tokens, scores, s, score_stride, tokens_dev)
+        if (dim_group_size == 16) POPKV_SD(16);
+        if (dim_group_size == 32) POPKV_SD(32);
+        POPKV_SD(64);
+#undef POPKV_SD
+    };
+    if (queries_dtype == POPKV_DTYPE_F32) return by_g(float{});
+    if (queries_dtype == POPKV_DTYPE_F16) return by_g(__half{});
+    return by_g(__nv_bfloat16{});
 }

@@ -823,7 +823,8 @@ __device__ __forceinline__ uint32_t cta_exclusive_scan32(uint32_t x, uint32_t* w
 template <int CPR, int PER>
 __global__ void __launch_bounds__(kClusterThreads) topk16_cluster_kernel(
     const uint16_t* __restrict__ scores, int64_t tokens, int64_t row_stride, int64_t k,
-    int64_t current_index, int64_t* __restrict__ out, int64_t out_stride, bool vec_ok) {
+    int64_t current_index, int64_t* __restrict__ out, int64_t out_stride, bool vec_ok,
+    const int64_t* __restrict__ dyn_tokens) {
     static_assert(PER % 8 == 0 && PER <= 32, "PER keys per thread, whole uint4 loads");
     constexpr int64_t kSlice = static_cast<int64_t>(kClusterThreads) * PER;
     __shared__ __align__(16) uint32_t hist[kHistBins];
@@ -835,6 +836,14 @@ __global__ void __launch_bounds__(kClusterThreads) topk16_cluster_kernel(
     POPKV_TOPK_PHASE(0);
     pdl_wait();
     pdl_launch_dependents();
+    if (dyn_tokens) {
+        // Device-resident token count: `tokens` and `k` are upper bounds, the
+        // current token's index is the count itself.
+        const int64_t t = *dyn_tokens;
+        tokens = t < 0 ? 0 : (t < tokens ? t : tokens);
+        k = k < tokens ? k : tokens;
+        current_index = tokens;
+    }
     cg::cluster_group cluster = cg::this_cluster();
     const int rank = static_cast<int>(cluster.block_rank());
     const int64_t row = blockIdx.x / CPR;
@@ -986,11 +995,11 @@ __global__ void __launch_bounds__(kClusterThreads) topk16_cluster_kernel(
 template <int CPR, int PER>
 int launch_cluster16(const void* scores, int64_t rows, int64_t tokens, int64_t row_stride, int64_t k,
                      int64_t current_index, int64_t* out, int64_t out_stride, bool vec_ok,
-                     cudaStream_t stream) {
+                     cudaStream_t stream, const int64_t* dyn_tokens) {
     const cudaError_t err = launch_pdl(topk16_cluster_kernel<CPR, PER>,
                                        dim3(static_cast<unsigned>(rows * CPR)), dim3(kClusterThreads), 0,
                                        stream, CPR, static_cast<const uint16_t*>(scores), tokens,
-                                       row_stride, k, current_index, out, out_stride, vec_ok);
+                                       row_stride, k, current_index, out, out_stride, vec_ok, dyn_tokens);
     if (err != cudaSuccess) return fail(POPKV_ERR_CUDA, "popkv_topk: %s", cudaGetErrorString(err));
     return check_launch("popkv_topk");
 }
@@ -1000,7 +1009,7 @@ int launch_cluster16(const void* scores, int64_t rows, int64_t tokens, int64_t r
 // thread that cover the row.  Returns -1 when the shape does not apply.
 int try_launch_cluster16(const void* scores, int64_t rows, int64_t tokens, int64_t row_stride,
                          int64_t k, int64_t current_index, int64_t* out, int64_t out_stride,
-                         bool vec_ok, cudaStream_t stream) {
+                         bool vec_ok, cudaStream_t stream, const int64_t* dyn_tokens = nullptr) {
     if (k <= 0 || k > tokens || rows > 0x7FFFFFF) return -1;
     // Up to 4 CTAs per row while the rows leave SMs idle (larger clusters cost
     // more in DSMEM reads and barrier latency than they save), more only when a
@@ -1014,7 +1023,7 @@ int try_launch_cluster16(const void* scores, int64_t rows, int64_t tokens, int64
 #define POPKV_C16(CPR_, PER_)                                                                      \
     if (cpr == CPR_ && per == PER_)                                                                \
         return launch_cluster16<CPR_, PER_>(scores, rows, tokens, row_stride, k, current_index, out, \
-                                            out_stride, vec_ok, stream);
+                                            out_stride, vec_ok, stream, dyn_tokens);
 #define POPKV_C16_CPR(CPR_) POPKV_C16(CPR_, 8) POPKV_C16(CPR_, 16) POPKV_C16(CPR_, 32)
     POPKV_C16_CPR(1)
     POPKV_C16_CPR(2)
@@ -1120,4 +1129,24 @@ extern "C" int popkv_topk_hist(const uint16_t* scores, uint32_t* hist, int64_t r
     else
         topk_hist_kernel<64><<<grid, kHistThreads, 0, s>>>(scores, hist, tokens, row_stride, k, current_index, out, out_stride, vec_ok);
     return check_launch("popkv_topk_hist");
+}
+
+extern "C" int popkv_topk_dyn(const uint16_t* scores, int64_t rows, const int64_t* tokens_dev,
+                              int64_t max_tokens, int64_t row_stride, int64_t k_max, int64_t* out,
+                              int64_t out_stride, void* stream) {
+    using namespace popkv;
+    if (rows < 0 || max_tokens <= 0) return fail(POPKV_ERR_INVALID, "popkv_topk_dyn: invalid shape");
+    if (k_max <= 0 || k_max > max_tokens)
+        return fail(POPKV_ERR_INVALID, "popkv_topk_dyn: k_max must be between 1 and max_tokens");
+    if (row_stride < max_tokens) return fail(POPKV_ERR_INVALID, "popkv_topk_dyn: row_stride < max_tokens");
+    if (out_stride < k_max + 1) return fail(POPKV_ERR_INVALID, "popkv_topk_dyn: out_stride too small");
+    if (rows == 0) return POPKV_OK;
+    if (!scores || !out || !tokens_dev) return fail(POPKV_ERR_INVALID, "popkv_topk_dyn: null pointer");
+    const bool vec_ok = aligned(scores, 16) && (row_stride * 2) % 16 == 0;
+    const int st = try_launch_cluster16(scores, rows, max_tokens, row_stride, k_max, max_tokens, out,
+                                        out_stride, vec_ok, static_cast<cudaStream_t>(stream), tokens_dev);
+    if (st < 0)
+        return fail(POPKV_ERR_UNSUPPORTED, "popkv_topk_dyn: at most %d tokens and %d rows per launch",
+                    8 * kClusterThreads * 32, 0x7FFFFFF);
+    return st;
 }

@@ -142,3 +142,14 @@ def test_install_as_reference_modules():
                 sys.modules.pop(n, None)
             else:
                 sys.modules[n] = m
+
+
+def test_ctypes_signatures_match_the_header():
+    """Every declared entry point is bound with the header's argument count."""
+    from popkv_b200 import _lib
+    text = HEADER.read_text()
+    for m in re.finditer(r"POPKV_API\s+[\w\s\*]+?\b(popkv_\w+)\s*\(([^;]*?)\)\s*;", text, re.S):
+        name, params = m.group(1), m.group(2).strip()
+        count = 0 if params in ("", "void") else params.count(",") + 1
+        assert name in _lib._SIGNATURES, name
+        assert len(_lib._SIGNATURES[name][0]) == count, name

@@ -1,0 +1,368 @@
+"""Device-resident step lengths and the graph-replayed full-model decode.
+
+* Each ``*_dyn`` kernel equals its static-length counterpart bit for bit (the
+  static kernels are themselves pinned to the CPU oracle elsewhere).
+* The model-loop glue kernels follow the reference model's eager ops.
+* ``LlamaSparseDecoder`` (one CUDA graph per token, device-side position)
+  produces bit-identical logits and tokens to the same loop run eagerly with
+  the static-length kernels and Python-integer lengths (the reference decoder's
+  launch pattern, popkv.py:988-1115), across token-group boundaries.
+* With every layer dense it matches transformers' LlamaForCausalLM on the same
+  weights within bf16 tolerance.
+"""
+from __future__ import annotations
+
+import math
+
+import pytest
+import torch
+import torch.nn.functional as F
+
+from popkv_b200 import _lib, popkv_cuda
+from popkv_b200.decoder import (LlamaConfig, LlamaSparseDecoder, LlamaWeights, apply_rope, rms_norm,
+                                rope_tables)
+from popkv_b200.popkv import RetrievalConfig
+
+pytestmark = pytest.mark.gpu
+
+TINY = LlamaConfig(hidden_size=1024, num_attention_heads=8, num_key_value_heads=2, head_dim=128,
+                   intermediate_size=2048, vocab_size=2000, num_hidden_layers=4)
+
+
+def _stream(dev):
+    return _lib.stream_of(dev)
+
+
+def _planes(dev, kvh, cap, g, keys, tg):
+    packed = popkv_cuda.pack_keys(keys, token_capacity=cap, token_group_size=tg, dim_group_size=g)
+    return packed
+
+
+@pytest.mark.parametrize("g,tg", [(16, 128), (64, 64), (32, 32)])
+def test_score_and_topk_dyn_match_static(cuda_device, g, tg):
+    dev = cuda_device
+    gen = torch.Generator().manual_seed(g)
+    kvh, qh, T, max_tokens = 2, 8, 1000, 1200
+    keys = torch.randn(kvh, T, 128, generator=gen).to(torch.bfloat16).to(dev)
+    cap = math.ceil(max_tokens / tg) * tg
+    packed = _planes(dev, kvh, cap, g, keys, tg)
+    q = torch.randn(1, qh, 128, generator=gen).to(torch.bfloat16).to(dev)
+    h2k = torch.arange(qh, device=dev) // (qh // kvh)
+    lib, check, ptr = _lib.lib(), _lib.check, _lib.ptr
+    for t, k_max in ((T, 255), (137, 255), (1, 7), (0, 7)):
+        pos = torch.tensor([t], device=dev, dtype=torch.int64)
+        stride = 1208
+        scores = torch.full((qh, stride), -7.0, device=dev, dtype=torch.float16)
+        check(lib.popkv_score_dyn(ptr(q), _lib.BF16, 1, qh, *(ptr(x) for x in packed), kvh, cap, ptr(h2k),
+                                  ptr(pos), max_tokens, g, ptr(scores), stride, _stream(dev)))
+        out = torch.full((qh, k_max + 1), -5, device=dev, dtype=torch.int64)
+        check(lib.popkv_topk_dyn(ptr(scores), qh, ptr(pos), max_tokens, stride, k_max, ptr(out), k_max + 1,
+                                 _stream(dev)))
+        torch.cuda.synchronize()
+        assert torch.all(scores[:, t:] == -7.0), "scores past the device count were written"
+        k = min(k_max, t)
+        if t > 0:
+            ref = popkv_cuda.score(q, packed, head_to_kv=h2k, tokens=t, dim_group_size=g)[0]
+            assert torch.equal(scores[:, :t], ref)
+            ref_idx = torch.empty((qh, k + 1), device=dev, dtype=torch.int64)
+            check(lib.popkv_topk(ptr(ref), _lib.F16, qh, t, t, k, t, ptr(ref_idx), k + 1, _stream(dev)))
+            torch.cuda.synchronize()
+            assert torch.equal(out[:, :k + 1], ref_idx)
+        else:
+            assert torch.all(out[:, 0] == 0)
+        assert torch.all(out[:, k + 1:] == -5)
+
+
+def _attn_static(q, pk, pv, ck, cv, idx, t, h2k, splits_tokens=256):
+    lib, check, ptr = _lib.lib(), _lib.check, _lib.ptr
+    dev = q.device
+    rows, sel = idx.shape
+    kvh = pk.shape[0]
+    partials = torch.empty((rows, math.ceil(sel / splits_tokens), 130), device=dev, dtype=torch.float32)
+    out = torch.empty((rows, 128), device=dev, dtype=q.dtype)
+    check(lib.popkv_attn_partial(ptr(q), _lib.dtype_code(q), 1, rows, 128, ptr(pk), ptr(pv), _lib.dtype_code(pk),
+                                 kvh, t, 0, pk.stride(0), pk.stride(1), 0, pv.stride(0), pv.stride(1), ptr(ck),
+                                 ptr(cv), ptr(idx), sel, None, ptr(h2k), splits_tokens, ptr(partials),
+                                 _stream(dev)))
+    check(lib.popkv_attn_merge(ptr(partials), rows, partials.shape[1], 128, ptr(out), _lib.dtype_code(out),
+                               _stream(dev)))
+    return out
+
+
+@pytest.mark.parametrize("t", [1, 300, 700, 2049])
+def test_attention_dyn_matches_static(cuda_device, t):
+    dev = cuda_device
+    gen = torch.Generator().manual_seed(t)
+    kvh, qh, cap = 2, 8, 2100
+    pk = torch.randn(kvh, cap, 128, generator=gen).to(torch.bfloat16).to(dev)
+    pv = torch.randn(kvh, cap, 128, generator=gen).to(torch.bfloat16).to(dev)
+    ck = torch.randn(kvh, 128, generator=gen).to(torch.bfloat16).to(dev)
+    cv = torch.randn(kvh, 128, generator=gen).to(torch.bfloat16).to(dev)
+    q = torch.randn(qh, 128, generator=gen).to(torch.bfloat16).to(dev)
+    h2k = torch.arange(qh, device=dev) // (qh // kvh)
+    lib, check, ptr = _lib.lib(), _lib.check, _lib.ptr
+    pos = torch.tensor([t], device=dev, dtype=torch.int64)
+    max_tokens = cap - 1
+    # Dense: every prefix row plus the current token.
+    dense_splits = math.ceil((max_tokens + 1) / 256)
+    partials = torch.empty((qh, dense_splits, 130), device=dev, dtype=torch.float32)
+    out = torch.empty((qh, 128), device=dev, dtype=torch.bfloat16)
+    check(lib.popkv_attn_dyn(ptr(q), _lib.BF16, 1, qh, ptr(pk), ptr(pv), _lib.BF16, kvh, max_tokens, 0,
+                             pk.stride(0), pk.stride(1), 0, pv.stride(0), pv.stride(1), ptr(ck), ptr(cv), ptr(pos),
+                             None, 0, 0, ptr(h2k), 256, ptr(partials), ptr(out), _lib.BF16, _stream(dev)))
+    idx = torch.arange(t + 1, device=dev).expand(qh, t + 1).contiguous()
+    ref = _attn_static(q, pk, pv, ck, cv, idx, t, h2k)
+    torch.cuda.synchronize()
+    assert torch.equal(out, ref)
+    # Materialised check of the dense attention itself.
+    kk = torch.cat([pk[:, :t], ck[:, None]], 1).float()[h2k]
+    vv = torch.cat([pv[:, :t], cv[:, None]], 1).float()[h2k]
+    p = torch.softmax((kk @ q.float()[:, :, None])[..., 0] / math.sqrt(128), -1)
+    dense = (p[:, :, None] * vv).sum(1)
+    assert torch.allclose(out.float(), dense, atol=2e-2, rtol=2e-2)
+    # Sparse: selected rows from a top-k-like index list (k_max larger than t for small t).
+    k_max = 511
+    k = min(k_max, t)
+    sel = torch.stack([torch.randperm(t, generator=gen)[:k].sort().values for _ in range(qh)]).to(dev)
+    idx = torch.cat([sel, torch.full((qh, 1), t, device=dev)], 1)
+    padded = torch.full((qh, k_max + 1), 10**9, device=dev, dtype=torch.int64)
+    padded[:, :k + 1] = idx
+    sp = torch.empty((qh, math.ceil((k_max + 1) / 256), 130), device=dev, dtype=torch.float32)
+    out2 = torch.empty_like(out)
+    check(lib.popkv_attn_dyn(ptr(q), _lib.BF16, 1, qh, ptr(pk), ptr(pv), _lib.BF16, kvh, max_tokens, 0,
+                             pk.stride(0), pk.stride(1), 0, pv.stride(0), pv.stride(1), ptr(ck), ptr(cv), ptr(pos),
+                             ptr(padded), k_max + 1, k_max, ptr(h2k), 256, ptr(sp), ptr(out2), _lib.BF16,
+                             _stream(dev)))
+    ref2 = _attn_static(q, pk, pv, ck, cv, idx.contiguous(), t, h2k)
+    torch.cuda.synchronize()
+    assert torch.equal(out2, ref2)
+
+
+@pytest.mark.parametrize("g,tg", [(16, 128), (64, 64)])
+def test_append_kv_dyn_matches_static(cuda_device, g, tg):
+    dev = cuda_device
+    gen = torch.Generator().manual_seed(tg)
+    kvh, cap = 3, 4 * tg
+    keys = torch.randn(kvh, cap, 128, generator=gen).to(torch.bfloat16).to(dev)
+    vals = torch.randn(kvh, cap, 128, generator=gen).to(torch.bfloat16).to(dev)
+    lib, check, ptr = _lib.lib(), _lib.check, _lib.ptr
+    for pos in (0, tg - 1, tg, 2 * tg + 5, cap - 1):
+        base = _planes(dev, kvh, cap, g, keys[:, :max(pos, 1)].contiguous(), tg)
+        newk = torch.randn(kvh, 128, generator=gen).to(torch.bfloat16).to(dev)
+        newv = torch.randn(kvh, 128, generator=gen).to(torch.bfloat16).to(dev)
+        # Static append.
+        k1, v1 = keys.clone(), vals.clone()
+        p1 = tuple(x.clone() for x in base)
+        sealed = pos - pos % tg
+        check(lib.popkv_append_kv(ptr(newk), ptr(newv), _lib.BF16, kvh, 128, ptr(k1), ptr(v1), k1.stride(0),
+                                  k1.stride(1), v1.stride(0), v1.stride(1), pos, *(ptr(x) for x in p1), cap,
+                                  sealed, tg, g, _stream(dev)))
+        # Device-position append, new rows passed in.
+        k2, v2 = keys.clone(), vals.clone()
+        p2 = tuple(x.clone() for x in base)
+        d = torch.tensor([pos], device=dev, dtype=torch.int64)
+        check(lib.popkv_append_kv_dyn(ptr(newk), ptr(newv), _lib.BF16, kvh, 128, ptr(k2), ptr(v2), k2.stride(0),
+                                      k2.stride(1), v2.stride(0), v2.stride(1), ptr(d), cap, *(ptr(x) for x in p2),
+                                      cap, tg, g, _stream(dev)))
+        # Device-position append, row already in the cache.
+        k3, v3 = keys.clone(), vals.clone()
+        k3[:, pos], v3[:, pos] = newk, newv
+        p3 = tuple(x.clone() for x in base)
+        check(lib.popkv_append_kv_dyn(None, None, _lib.BF16, kvh, 128, ptr(k3), ptr(v3), k3.stride(0),
+                                      k3.stride(1), v3.stride(0), v3.stride(1), ptr(d), cap, *(ptr(x) for x in p3),
+                                      cap, tg, g, _stream(dev)))
+        torch.cuda.synchronize()
+        assert torch.equal(k1, k2) and torch.equal(v1, v2) and torch.equal(k1, k3) and torch.equal(v1, v3)
+        for a, b, c in zip(p1, p2, p3):
+            assert torch.equal(a, b) and torch.equal(a, c)
+
+
+def test_glue_kernels_follow_eager_ops(cuda_device):
+    dev = cuda_device
+    gen = torch.Generator().manual_seed(5)
+    lib, check, ptr = _lib.lib(), _lib.check, _lib.ptr
+    B, H = 3, 4096
+    hidden = torch.randn(B, H, generator=gen).to(torch.bfloat16).to(dev)
+    delta = torch.randn(B, H, generator=gen).to(torch.bfloat16).to(dev)
+    w = (1 + 0.1 * torch.randn(H, generator=gen)).to(torch.bfloat16).to(dev)
+    ref_h = hidden + delta
+    ref = rms_norm(ref_h, w, 1e-5)
+    out = torch.empty_like(hidden)
+    h = hidden.clone()
+    check(lib.popkv_rms_norm(ptr(delta), ptr(h), ptr(w), B, H, 1e-5, ptr(out), _stream(dev)))
+    torch.cuda.synchronize()
+    assert torch.equal(h, ref_h)
+    diff = (out.float() - ref.float()).abs()
+    assert diff.max() <= 2 ** -6 * ref.float().abs().max()  # one bf16 ulp at most (sum order)
+    assert (diff == 0).float().mean() > 0.98
+    # RoPE + append: bit-exact against the eager rounding.
+    cfg = LlamaConfig()
+    cos, sin = rope_tables(cfg, 64, dev)
+    QH, KVH, cap = 32, 8, 64
+    qkv = torch.randn(B, (QH + 2 * KVH) * 128, generator=gen).to(torch.bfloat16).to(dev)
+    kc = torch.zeros(B, KVH, cap, 128, device=dev, dtype=torch.bfloat16)
+    vc = torch.zeros_like(kc)
+    q = torch.empty(B, QH, 128, device=dev, dtype=torch.bfloat16)
+    kcur = torch.empty(B, KVH, 128, device=dev, dtype=torch.bfloat16)
+    vcur = torch.empty_like(kcur)
+    pos = 37
+    d = torch.tensor([pos], device=dev, dtype=torch.int64)
+    check(lib.popkv_rope_append(ptr(qkv), B, QH, KVH, 128, ptr(cos), ptr(sin), ptr(d), cap - 1, ptr(q), ptr(kcur),
+                                ptr(vcur), ptr(kc), ptr(vc), kc.stride(0), kc.stride(1), kc.stride(2), vc.stride(0),
+                                vc.stride(1), vc.stride(2), _stream(dev)))
+    torch.cuda.synchronize()
+    x = qkv.view(B, QH + 2 * KVH, 128)
+    rq = apply_rope(x[:, :QH], cos[pos:pos + 1], sin[pos:pos + 1])
+    rk = apply_rope(x[:, QH:QH + KVH], cos[pos:pos + 1], sin[pos:pos + 1])
+    assert torch.equal(q, rq) and torch.equal(kcur, rk) and torch.equal(vcur, x[:, QH + KVH:])
+    assert torch.equal(kc[:, :, pos], rk) and torch.equal(vc[:, :, pos], x[:, QH + KVH:])
+    assert torch.count_nonzero(kc[:, :, :pos]) == 0 and torch.count_nonzero(kc[:, :, pos + 1:]) == 0
+    # SiLU * up.
+    I = 14336
+    gu = torch.randn(B, 2 * I, generator=gen).to(torch.bfloat16).to(dev) * 3
+    act = torch.empty(B, I, device=dev, dtype=torch.bfloat16)
+    check(lib.popkv_silu_mul(ptr(gu), B, I, ptr(act), _stream(dev)))
+    torch.cuda.synchronize()
+    ref = F.silu(gu[:, :I]) * gu[:, I:]
+    diff = (act.float() - ref.float()).abs()
+    assert (diff == 0).float().mean() > 0.999
+    assert torch.allclose(act.float(), ref.float(), rtol=2 ** -7, atol=0)
+
+
+class _StaticLengthDecoder(LlamaSparseDecoder):
+    """The same loop run eagerly with the static-length kernels and a Python-integer
+    cache length per call, as the reference decoder launches its stages
+    (popkv.py:1076-1115, append afterwards as popkv.py:884-972)."""
+
+    def _attention(self, layer, s):
+        lib, check, ptr = _lib.lib(), _lib.check, _lib.ptr
+        t = int(self.position.item())
+        B, rows = self.batch, self.batch * self.qh
+        kc, vc = self.k_cache[layer], self.v_cache[layer]
+        dev = self.device
+        if layer in self.packed:
+            sign, mag, low, delta = self.packed[layer]
+            k = min(self.k_max, t)
+            idx = torch.empty((rows, k + 1), device=dev, dtype=torch.int64)
+            if t > 0:
+                scores = torch.empty((rows, t), device=dev, dtype=torch.float16)
+                check(lib.popkv_score(ptr(self.q), _lib.BF16, 1, rows, 128, ptr(sign), ptr(mag), ptr(low),
+                                      ptr(delta), B * self.kvh, self.meta_capacity, ptr(self.head_to_kv), t,
+                                      self.g, ptr(scores), _lib.F16, s))
+                check(lib.popkv_topk(ptr(scores), _lib.F16, rows, t, t, k, t, ptr(idx), k + 1, s))
+            else:
+                idx.fill_(0)
+        else:
+            idx = torch.arange(t + 1, device=dev).expand(rows, t + 1).contiguous()
+        sel = idx.shape[1]
+        partials = torch.empty((rows, math.ceil(sel / self.split_tokens), 130), device=dev, dtype=torch.float32)
+        check(lib.popkv_attn_partial(ptr(self.q), _lib.BF16, 1, rows, 128, ptr(kc), ptr(vc), _lib.BF16,
+                                     B * self.kvh, t, 0, kc.stride(1), kc.stride(2), 0, vc.stride(1), vc.stride(2),
+                                     ptr(self.k_cur), ptr(self.v_cur), ptr(idx), sel, None, ptr(self.head_to_kv),
+                                     self.split_tokens, ptr(partials), s))
+        check(lib.popkv_attn_merge(ptr(partials), rows, partials.shape[1], 128, ptr(self.attn), _lib.BF16, s))
+        if layer in self.packed:
+            sign, mag, low, delta = self.packed[layer]
+            check(lib.popkv_append_kv(ptr(self.k_cur), ptr(self.v_cur), _lib.BF16, B * self.kvh, 128, ptr(kc),
+                                      ptr(vc), kc.stride(1), kc.stride(2), vc.stride(1), vc.stride(2), t,
+                                      ptr(sign), ptr(mag), ptr(low), ptr(delta), self.meta_capacity,
+                                      t - t % self.tg, self.tg, self.g, s))
+
+
+def _prefix(cfg, batch, T, seed=3):
+    gen = torch.Generator().manual_seed(seed)
+    return torch.randint(0, cfg.vocab_size, (batch, T), generator=gen)
+
+
+@pytest.mark.parametrize("method,batch,T,steps", [("popkv-s", 1, 250, 24), ("popkv-q", 2, 200, 12),
+                                                  ("full", 1, 100, 6)])
+def test_graph_decoder_matches_static_length_loop(cuda_device, method, batch, T, steps):
+    weights = LlamaWeights.random(TINY, device=cuda_device, seed=1, std=0.05)
+    tg = {"popkv-s": 64, "popkv-q": 128, "full": 32}[method]
+    g = {"popkv-s": 64, "popkv-q": 16, "full": 32}[method]
+    retrieval = RetrievalConfig(budget=64, group_size=tg, dim_group_size=g)
+    ids = _prefix(TINY, batch, T)
+    graph = LlamaSparseDecoder(weights, method=method, retrieval=retrieval, batch=batch, max_context=T + steps + 1)
+    static = _StaticLengthDecoder(weights, method=method, retrieval=retrieval, batch=batch,
+                                  max_context=T + steps + 1, use_graph=False)
+    first_a = graph.prefill(ids)
+    first_b = static.prefill(ids)
+    assert torch.equal(first_a, first_b)
+    for l in graph.packed:
+        for a, b in zip(graph.packed[l], static.packed[l]):
+            assert torch.equal(a, b)
+    for step in range(steps):
+        la = graph.decode().clone()
+        lb = static.decode().clone()
+        assert torch.equal(la, lb), f"step {step}: logits differ"
+        assert torch.equal(graph.token, static.token)
+    assert int(graph.position.item()) == T + steps
+    for l in range(TINY.num_hidden_layers):
+        assert torch.equal(graph.k_cache[l], static.k_cache[l])
+        assert torch.equal(graph.v_cache[l], static.v_cache[l])
+    for l in graph.packed:
+        for a, b in zip(graph.packed[l], static.packed[l]):
+            assert torch.equal(a, b)
+    graph.close()
+
+
+def test_generate_replays_without_host_round_trips(cuda_device):
+    weights = LlamaWeights.random(TINY, device=cuda_device, seed=2, std=0.05)
+    ids = _prefix(TINY, 1, 150, seed=9)
+    a = LlamaSparseDecoder(weights, method="popkv-s", retrieval=RetrievalConfig(budget=64, group_size=64,
+                                                                                dim_group_size=64),
+                           max_context=200)
+    b = LlamaSparseDecoder(weights, method="popkv-s", retrieval=RetrievalConfig(budget=64, group_size=64,
+                                                                                dim_group_size=64),
+                           max_context=200, use_graph=False)
+    a.prefill(ids)
+    b.prefill(ids)
+    out = a.generate(20)
+    ref = torch.stack([b.decode().argmax(-1).cpu() for _ in range(20)], 1)
+    assert torch.equal(out, ref)
+    with pytest.raises(RuntimeError, match="capacity"):
+        a.generate(100)
+
+
+def test_dense_decode_matches_transformers_llama(cuda_device):
+    """method="full" against transformers' LlamaForCausalLM on the same weights.
+
+    Both run in bf16 with different rounding paths, so the yardstick is an fp32
+    run of the transformers model: our logits must be no further from it than
+    twice the bf16 transformers run is.
+    """
+    import copy
+    transformers = pytest.importorskip("transformers")
+    cfg = transformers.LlamaConfig(hidden_size=1024, intermediate_size=2048, num_attention_heads=8,
+                                   num_key_value_heads=2, head_dim=128, num_hidden_layers=3, vocab_size=2000,
+                                   rope_theta=500000.0, rms_norm_eps=1e-5, max_position_embeddings=4096,
+                                   tie_word_embeddings=False)
+    torch.manual_seed(0)
+    model = transformers.LlamaForCausalLM(cfg).eval()
+    for p in model.parameters():
+        if p.ndim == 2:
+            torch.nn.init.normal_(p, 0.0, 0.02)
+    model = model.to(device=cuda_device, dtype=torch.bfloat16)
+    model32 = copy.deepcopy(model).float()
+    inv_freq = 1.0 / (500000.0 ** (torch.arange(0, 128, 2, device=cuda_device).float() / 128))
+    # Keep the rotary inverse frequencies in fp32, as a bf16 checkpoint load does.
+    model.model.rotary_emb.inv_freq = inv_freq
+    model32.model.rotary_emb.inv_freq = inv_freq
+    weights = LlamaWeights.from_module(model)
+    T, steps = 120, 4
+    ids = _prefix(weights.config, 1, T, seed=4)
+    dec = LlamaSparseDecoder(weights, method="full", max_context=T + steps + 1)
+    dec.prefill(ids)
+    seq = ids[0].tolist()
+    for _ in range(steps):
+        seq.append(int(dec.token.item()))
+        logits = dec.decode()[0].clone()
+        with torch.no_grad():
+            x = torch.tensor([seq], device=cuda_device)
+            ref32 = model32(input_ids=x).logits[0, -1].float()
+            hf16 = model(input_ids=x).logits[0, -1].float()
+        err = (logits - ref32).norm() / ref32.norm()
+        hf_err = (hf16 - ref32).norm() / ref32.norm()
+        assert err <= max(2 * hf_err, 5e-3), (err, hf_err)
+        assert (logits.argmax() == ref32.argmax()) or (ref32.max() - ref32[logits.argmax()] < 0.05)
+    dec.close()
