@@ -828,10 +828,12 @@ def run_model(args, world, rank, local):
     time.sleep(0.25)
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     t0 = time.time()
+    torch.cuda.nvtx.range_push("decode_steps")  # the launch-list capture filters on this range
     start.record(stream)
     for _ in range(K):
         dec.step()
     end.record(stream)
+    torch.cuda.nvtx.range_pop()
     torch.cuda.synchronize(device)
     t1 = time.time()
     sampler.stop()

@@ -490,6 +490,57 @@ POPKV_API int popkv_rope_append(const void* qkv, int64_t batch, int64_t q_heads,
                                 void* stream);
 POPKV_API int popkv_silu_mul(const void* gate_up, int64_t rows, int64_t inter, void* act, void* stream);
 
+/*
+ * Weight-streaming products of the decode step, bf16, batch 1..4 (the rows of
+ * x), weights W [rows, k] row-major (k a multiple of 8, 16-byte aligned), fp32
+ * accumulation, bf16 results; each fuses the element-wise work around it.  The
+ * reference runs these as nn.Linear modules of the HF model plus separate
+ * eager ops (popkv.py:1009-1016, :1103-1112; decode_runtime.py:37-40).
+ *
+ * popkv_linear: out[b, r] = sum_j W[r, j] x[b, j] (o_proj, down_proj).
+ *
+ * The popkv_norm_* products first form h = hidden[b] (or embed[token[b]] when
+ * embed is non-NULL: the first layer) plus delta[b] when non-NULL (the
+ * residual add, rounded to bf16), store h to hidden_out when non-NULL, and use
+ * x = RMSNorm(h) * norm_w (LlamaRMSNorm rounding points, eps) as the vector:
+ *
+ * popkv_norm_qkv_rope: W = [q | k | v] rows of q_heads + 2 kv_heads heads of
+ *   128; rotary embedding at p = *position_dev (clamped to max_position) from
+ *   bf16 cos/sin tables [max_position + 1, 64]; rotated q to q_out [b, q_heads,
+ *   128], rotated k and v to k_cur / v_cur [b, kv_heads, 128] and to row p of
+ *   the caches (element (b, h, t, d) at base + b*batch_stride + h*head_stride +
+ *   t*token_stride + d).  Replaces q/k/v_proj + _apply_rope + append_kv
+ *   (popkv.py:1011-1016, :745-749, :965-972).
+ * popkv_norm_gate_up_swiglu: W = [gate | up] ([2 inter, k]); act [b, inter] =
+ *   silu(gate x) * (up x) (LlamaMLP without down_proj).
+ * popkv_norm_lm_head_argmax: logits [b, vocab] = W x, and the greedy token
+ *   (largest logit, lowest index among equals) to token_next[b]; argmax_state
+ *   holds batch + 1 zeroed uint64 and is left zeroed; when position_dev is
+ *   non-NULL the launch's last CTA adds 1 to it.  Replaces the final norm +
+ *   lm_head (popkv.py:1109-1110) and the greedy argmax of the caller.
+ */
+/* Count of weight-streaming product warps whose bounded wait for a weight
+ * copy gave up since the library was loaded (0 in a healthy run; their
+ * outputs are incomplete).  Synchronises with the device. */
+POPKV_API int popkv_gemv_timeouts(uint32_t* count);
+POPKV_API int popkv_linear(const void* w, int64_t rows, int64_t k, const void* x, int64_t batch, void* out,
+                           int64_t out_stride, void* stream);
+POPKV_API int popkv_norm_qkv_rope(const void* w, int64_t q_heads, int64_t kv_heads, int64_t k, int64_t batch,
+                                  const void* hidden, const void* delta, const void* embed, const int64_t* token,
+                                  const void* norm_w, float eps, void* hidden_out, const void* cos_table,
+                                  const void* sin_table, const int64_t* position_dev, int64_t max_position,
+                                  void* q_out, void* k_cur, void* v_cur, void* k_cache, void* v_cache,
+                                  int64_t k_batch_stride, int64_t k_head_stride, int64_t k_token_stride,
+                                  int64_t v_batch_stride, int64_t v_head_stride, int64_t v_token_stride,
+                                  void* stream);
+POPKV_API int popkv_norm_gate_up_swiglu(const void* w, int64_t inter, int64_t k, int64_t batch,
+                                        const void* hidden, const void* delta, const void* norm_w, float eps,
+                                        void* hidden_out, void* act, void* stream);
+POPKV_API int popkv_norm_lm_head_argmax(const void* w, int64_t vocab, int64_t k, int64_t batch,
+                                        const void* hidden, const void* delta, const void* norm_w, float eps,
+                                        void* hidden_out, void* logits, unsigned long long* argmax_state,
+                                        int64_t* token_next, int64_t* position_dev, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

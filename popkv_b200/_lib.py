@@ -59,6 +59,12 @@ _SIGNATURES = {
     "popkv_rope_append": ([_P, _L, _L, _L, _L, _P, _P, _P, _L, _P, _P, _P, _P, _P, _L, _L, _L,
                            _L, _L, _L, _P], _I),
     "popkv_silu_mul": ([_P, _L, _L, _P, _P], _I),
+    "popkv_gemv_timeouts": ([ctypes.POINTER(ctypes.c_uint32)], _I),
+    "popkv_linear": ([_P, _L, _L, _P, _L, _P, _L, _P], _I),
+    "popkv_norm_qkv_rope": ([_P, _L, _L, _L, _L, _P, _P, _P, _P, _P, ctypes.c_float, _P, _P, _P, _P, _L,
+                             _P, _P, _P, _P, _P, _L, _L, _L, _L, _L, _L, _P], _I),
+    "popkv_norm_gate_up_swiglu": ([_P, _L, _L, _L, _P, _P, _P, ctypes.c_float, _P, _P, _P], _I),
+    "popkv_norm_lm_head_argmax": ([_P, _L, _L, _L, _P, _P, _P, ctypes.c_float, _P, _P, _P, _P, _P, _P], _I),
 }
 
 _lock = threading.Lock()

@@ -20,7 +20,7 @@ INCLUDE = ROOT / "include"
 LIB_DIR = PACKAGE / "lib"
 LIB_PATH = LIB_DIR / "libpopkv_b200.so"
 SOURCES = ("abi.cu", "pack.cu", "score.cu", "score_mma.cu", "topk.cu", "attention.cu", "attention_static.cu",
-           "peer.cu", "retrieve.cu", "decoder.cu")
+           "peer.cu", "retrieve.cu", "decoder.cu", "gemv.cu")
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",

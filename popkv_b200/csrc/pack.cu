@@ -266,8 +266,11 @@ __global__ void __launch_bounds__(kRowThreads) pack_rows_kernel(
 
     if (dyn_position) {
         // Append at a device-resident position (one CTA column, the graph-replayed
-        // decode loop): `tokens` bounds the position; the open group runs from
-        // the last group boundary to it.
+        // decode loop, launched with programmatic dependent launch): `tokens`
+        // bounds the position; the open group runs from the last group boundary
+        // to it.
+        pdl_wait();
+        pdl_launch_dependents();
         int64_t pos = *dyn_position;
         pos = pos < 0 ? 0 : (pos < tokens ? pos : tokens - 1);
         const int64_t sealed = pos - pos % token_group;
@@ -622,11 +625,13 @@ extern "C" int popkv_append_kv_dyn(const void* new_keys, const void* new_values,
                             static_cast<size_t>(token_group_size) * (128 * sizeof(T) + 16);
         const int st = allow_dynamic_smem(pack_rows_kernel<T, G>, static_cast<int>(smem));
         if (st != POPKV_OK) return st;
-        pack_rows_kernel<T, G><<<grid, kRowThreads, smem, s>>>(
-            static_cast<const T*>(cache_keys), k_head_stride, k_token_stride, max_tokens, token_group_size,
-            k_sign, k_mag, k_low, k_delta, capacity, 0, static_cast<const T*>(new_keys),
-            static_cast<const T*>(new_values), static_cast<T*>(cache_values), v_head_stride,
-            v_token_stride, position_dev);
+        const cudaError_t err = launch_pdl(
+            pack_rows_kernel<T, G>, grid, dim3(kRowThreads), smem, s, 1, static_cast<const T*>(cache_keys),
+            k_head_stride, k_token_stride, max_tokens, static_cast<int64_t>(token_group_size), k_sign, k_mag,
+            k_low, k_delta, capacity, static_cast<int64_t>(0), static_cast<const T*>(new_keys),
+            static_cast<const T*>(new_values), static_cast<T*>(cache_values), v_head_stride, v_token_stride,
+            position_dev);
+        if (err != cudaSuccess) return fail(POPKV_ERR_CUDA, "popkv_append_kv_dyn: %s", cudaGetErrorString(err));
         return check_launch("popkv_append_kv_dyn");
     };
     auto by_g = [&](auto tag) -> int {

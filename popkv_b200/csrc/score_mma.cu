@@ -21,6 +21,7 @@
 #include <cstdint>
 
 #include "common.cuh"
+#include "mbarrier.cuh"
 #include "score_impl.cuh"
 #include "score_mma.cuh"
 
@@ -67,14 +68,10 @@ constexpr int kKBlocks = 8;       // 128 dims x {uk, uk*km} bytes / 32 bytes per
 constexpr int kABlockBytes = kMmaTile * 32;  // one k-block of A: 4 KB
 constexpr int kBBlockBytes = kMmaN * 32;     // one k-block of B: 512 B
 constexpr int kABytes = kKBlocks * kABlockBytes;
-constexpr int kMaxWaitPolls = 1 << 20;
 
 // ---------------------------------------------------------------------------
 // PTX wrappers.
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ uint32_t smem_addr(const void* p) {
-    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
 
 // Shared-memory matrix descriptor, no swizzle, K-major: core matrices of 8 rows
 // x 16 bytes stored as 128 contiguous bytes; the next 16 bytes along K sit 128
@@ -108,10 +105,6 @@ __device__ __forceinline__ void tc_fence_after() {
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 }
 
-// Generic-proxy shared-memory writes become visible to the tensor cores.
-__device__ __forceinline__ void fence_async_smem() {
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-}
 
 __device__ __forceinline__ void mma_i8(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
                                        uint32_t accumulate) {
@@ -133,27 +126,6 @@ __device__ __forceinline__ void mma_commit(uint64_t* mbar) {
                  :: "r"(smem_addr(mbar)) : "memory");
 }
 
-__device__ __forceinline__ void mbar_init(uint64_t* mbar, uint32_t count) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" :: "r"(smem_addr(mbar)), "r"(count) : "memory");
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-}
-
-// Bounded wait for the phase with the given parity; false if it gave up.
-__device__ __forceinline__ bool mbar_wait(uint64_t* mbar, uint32_t parity) {
-    const uint32_t addr = smem_addr(mbar);
-    for (int i = 0; i < kMaxWaitPolls; ++i) {
-        uint32_t done;
-        asm volatile(
-            "{\n\t"
-            ".reg .pred p;\n\t"
-            "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-            "selp.u32 %0, 1, 0, p;\n\t"
-            "}\n"
-            : "=r"(done) : "r"(addr), "r"(parity) : "memory");
-        if (done) return true;
-    }
-    return false;
-}
 
 // Byte offset of (row, 16-byte chunk c16 of a 32-byte k-block row) inside a
 // k-block laid out as described at kmajor_desc.
@@ -210,13 +182,6 @@ __device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t (&c)[8]) {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
-__device__ __forceinline__ void mbar_arrive(uint64_t* mbar) {
-    asm volatile(
-        "{\n\t"
-        ".reg .b64 st;\n\t"
-        "mbarrier.arrive.shared::cta.b64 st, [%0];\n\t"
-        "}\n" :: "r"(smem_addr(mbar)) : "memory");
-}
 
 template <int G, typename QT>
 __global__ void __launch_bounds__(kWsThreads, 2) score128_ws_kernel(

@@ -22,10 +22,13 @@ token, replayed for every decode step:
   then append);
 * greedy selection (argmax) feeds the next step's token id on the device, so a
   run of ``generate`` steps needs no host round trip;
-* the projections and the MLP are cuBLAS GEMMs (fused q|k|v and gate|up
-  weights); RMSNorm with the residual add, RoPE + KV append and SiLU * up are
-  small kernels of the C ABI; the dense layers use the split-attention kernel
-  over every cached token.
+* for batch <= 4 the projections are the library's weight-streaming
+  products (fused q|k|v and gate|up weights) with the element-wise work in
+  their prologues and epilogues: residual add + RMSNorm (and the embedding
+  lookup of layer 0), RoPE + KV append, SwiGLU, and the LM head's greedy
+  argmax + position advance -- four launches per layer besides attention;
+  larger batches use cuBLAS GEMMs and separate RMSNorm / RoPE / SwiGLU kernels;
+* the dense layers use the split-attention kernel over every cached token.
 
 The prefill (``prefill``) is plain PyTorch (causal SDPA); it is not on the
 decode path.  Weights are random (``LlamaWeights.random``) or taken from a
@@ -253,7 +256,11 @@ class LlamaSparseDecoder:
         # Activations.
         bf = torch.bfloat16
         self.hidden = torch.zeros((B, H), device=dev, dtype=bf)
+        self.hidden_b = torch.zeros((B, H), device=dev, dtype=bf)  # ping-pong partner (fused path)
         self.x = torch.zeros((B, H), device=dev, dtype=bf)
+        # Fused weight-streaming products (batch <= 4); cuBLAS + separate kernels otherwise.
+        self.fused = B <= 4
+        self.argmax_state = torch.zeros(B + 1, device=dev, dtype=torch.int64)
         self.qkv = torch.zeros((B, (self.qh + 2 * self.kvh) * D), device=dev, dtype=bf)
         self.q = torch.zeros((B, self.qh, D), device=dev, dtype=bf)
         self.k_cur = torch.zeros((B, self.kvh, D), device=dev, dtype=bf)
@@ -325,6 +332,13 @@ class LlamaSparseDecoder:
                 ptr(self.q), _lib.BF16, 1, B * self.qh, ptr(sign), ptr(mag), ptr(low), ptr(delta),
                 B * self.kvh, self.meta_capacity, ptr(self.head_to_kv), ptr(self.position),
                 self.max_tokens, self.g, ptr(self.scores), self.score_stride, s))
+            # The token's key is in the cache already (the q/k/v product wrote it):
+            # re-encode its open group now that the score has read the old planes
+            # (the reference's order: decode, then append_retrieval_caches).
+            check(lib.popkv_append_kv_dyn(
+                None, None, _lib.BF16, B * self.kvh, 128, ptr(kc), ptr(vc), ks, kc.stride(2), vs,
+                vc.stride(2), ptr(self.position), self.max_context, ptr(sign), ptr(mag), ptr(low),
+                ptr(delta), self.meta_capacity, self.tg, self.g, s))
             check(lib.popkv_topk_dyn(
                 ptr(self.scores), B * self.qh, ptr(self.position), self.max_tokens, self.score_stride,
                 self.k_max, ptr(self.indices), self.k_max + 1, s))
@@ -336,14 +350,6 @@ class LlamaSparseDecoder:
             self.max_tokens, 0, ks, kc.stride(2), 0, vs, vc.stride(2), ptr(self.k_cur),
             ptr(self.v_cur), ptr(self.position), indices, index_stride, self.k_max,
             ptr(self.head_to_kv), self.split_tokens, ptr(self.partials), ptr(out), _lib.BF16, s))
-        if layer in self.packed:
-            # The token's key is in the cache already (popkv_rope_append); re-encode
-            # its open group now that this layer's score has read the old planes.
-            sign, mag, low, delta = self.packed[layer]
-            check(lib.popkv_append_kv_dyn(
-                None, None, _lib.BF16, B * self.kvh, 128, ptr(kc), ptr(vc), ks, kc.stride(2), vs,
-                vc.stride(2), ptr(self.position), self.max_context, ptr(sign), ptr(mag), ptr(low),
-                ptr(delta), self.meta_capacity, self.tg, self.g, s))
         if self.world > 1:
             selected = self.k_max + 1 if layer in self.packed else self.max_tokens + 1
             self._gather(s, math.ceil(selected / self.split_tokens))
@@ -361,6 +367,43 @@ class LlamaSparseDecoder:
 
     def _launch(self, stream: torch.cuda.Stream) -> None:
         """Enqueue one decode step on ``stream``."""
+        if self.fused:
+            self._launch_fused(stream)
+        else:
+            self._launch_cublas(stream)
+
+    def _launch_fused(self, stream: torch.cuda.Stream) -> None:
+        """The step as 4 weight-streaming products per layer plus the attention chain.
+
+        The residual stream ping-pongs between ``hidden`` (before a layer) and
+        ``hidden_b`` (after its attention): each norm prologue adds the pending
+        delta (the previous product's output), stores the sum and normalises it.
+        """
+        lib, check, ptr = _lib.lib(), _lib.check, _lib.ptr
+        s = ctypes_stream(stream)
+        cfg, B = self.cfg, self.batch
+        H, I, eps = cfg.hidden_size, cfg.intermediate_size, cfg.rms_norm_eps
+        QH, D = cfg.num_attention_heads, cfg.head_dim
+        for l, lw in enumerate(self.w.layers):
+            kc, vc = self.k_cache[l], self.v_cache[l]
+            first = l == 0
+            check(lib.popkv_norm_qkv_rope(
+                ptr(self.qkv_weights[l]), self.qh, self.kvh, H, B, None if first else ptr(self.hidden),
+                None if first else ptr(self.down), ptr(self.w.embed) if first else None, ptr(self.token),
+                ptr(lw.input_norm), eps, ptr(self.hidden_b), ptr(self.cos), ptr(self.sin), ptr(self.position),
+                self.max_context - 1, ptr(self.q), ptr(self.k_cur), ptr(self.v_cur), ptr(kc), ptr(vc),
+                kc.stride(0), kc.stride(1), kc.stride(2), vc.stride(0), vc.stride(1), vc.stride(2), s))
+            with torch.cuda.stream(stream):
+                self._attention(l, s)
+            check(lib.popkv_linear(ptr(lw.o), H, QH * D, ptr(self.attn_full), B, ptr(self.o), H, s))
+            check(lib.popkv_norm_gate_up_swiglu(ptr(lw.gate_up), I, H, B, ptr(self.hidden_b), ptr(self.o),
+                                                ptr(lw.post_norm), eps, ptr(self.hidden), ptr(self.act), s))
+            check(lib.popkv_linear(ptr(lw.down), H, I, ptr(self.act), B, ptr(self.down), H, s))
+        check(lib.popkv_norm_lm_head_argmax(
+            ptr(self.w.lm_head), cfg.vocab_size, H, B, ptr(self.hidden), ptr(self.down), ptr(self.w.norm), eps,
+            None, ptr(self.logits), ptr(self.argmax_state), ptr(self.token), ptr(self.position), s))
+
+    def _launch_cublas(self, stream: torch.cuda.Stream) -> None:
         lib, check, ptr = _lib.lib(), _lib.check, _lib.ptr
         s = ctypes_stream(stream)
         cfg, B = self.cfg, self.batch
@@ -389,8 +432,7 @@ class LlamaSparseDecoder:
             check(lib.popkv_rms_norm(ptr(delta), ptr(self.hidden), ptr(self.w.norm), B, H, eps,
                                      ptr(self.x), s))
             torch.mm(self.x, self.w.lm_head.t(), out=self.logits)
-            self.logits_f32.copy_(self.logits)
-            torch.argmax(self.logits_f32, dim=-1, out=self.next_token)
+            torch.argmax(self.logits, dim=-1, out=self.next_token)
             self.token.copy_(self.next_token)
             self.position.add_(1)
 
@@ -513,6 +555,7 @@ class LlamaSparseDecoder:
                 raise ValueError(f"token ids must be in [0, {self.cfg.vocab_size})")
             self.token.copy_(ids)
         self.step()
+        self.logits_f32.copy_(self.logits)
         return self.logits_f32
 
     def generate(self, steps: int) -> torch.Tensor:
