@@ -490,6 +490,7 @@ POPKV_API int popkv_rope_append(const void* qkv, int64_t batch, int64_t q_heads,
                                 void* stream);
 POPKV_API int popkv_silu_mul(const void* gate_up, int64_t rows, int64_t inter, void* act, void* stream);
 
+
 /*
  * Weight-streaming products of the decode step, bf16, batch 1..4 (the rows of
  * x), weights W [rows, k] row-major (k a multiple of 8, 16-byte aligned), fp32

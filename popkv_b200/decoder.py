@@ -301,6 +301,7 @@ class LlamaSparseDecoder:
         self.partials = torch.zeros((B * self.qh, splits, D + 2), device=dev, dtype=torch.float32)
         self.head_to_kv = (torch.arange(B * self.qh, device=dev, dtype=torch.int64) // self.group_heads)
         self.cos, self.sin = rope_tables(cfg, cap, dev)
+        self._side = torch.cuda.Stream(dev) if dev.type == "cuda" else None
         self.graph = None
         self.use_graph = use_graph
         self.prefix_length = 0
@@ -319,7 +320,21 @@ class LlamaSparseDecoder:
         return torch.cat([q, k, v], 0).contiguous()
 
     # -- the decode step ---------------------------------------------------------
-    def _attention(self, layer: int, s) -> None:
+    def _append(self, layer: int, s) -> None:
+        """Re-encode the open token group of a sparse layer (the token's key is in
+        the cache already: the q/k/v product wrote it)."""
+        lib, check, ptr = _lib.lib(), _lib.check, _lib.ptr
+        kc, vc = self.k_cache[layer], self.v_cache[layer]
+        sign, mag, low, delta = self.packed[layer]
+        check(lib.popkv_append_kv_dyn(
+            None, None, _lib.BF16, self.batch * self.kvh, 128, ptr(kc), ptr(vc), kc.stride(1), kc.stride(2),
+            vc.stride(1), vc.stride(2), ptr(self.position), self.max_context, ptr(sign), ptr(mag), ptr(low),
+            ptr(delta), self.meta_capacity, self.tg, self.g, s))
+
+    def _attention(self, layer: int, s, after_score=None) -> None:
+        """Score, top-k and attention of one layer; ``after_score(layer)`` forks the
+        append re-encode (it must follow the score, nothing else waits for it).
+        Without ``after_score`` the append runs inline after the score."""
         lib, check, ptr = _lib.lib(), _lib.check, _lib.ptr
         B = self.batch
         kc, vc = self.k_cache[layer], self.v_cache[layer]
@@ -332,13 +347,12 @@ class LlamaSparseDecoder:
                 ptr(self.q), _lib.BF16, 1, B * self.qh, ptr(sign), ptr(mag), ptr(low), ptr(delta),
                 B * self.kvh, self.meta_capacity, ptr(self.head_to_kv), ptr(self.position),
                 self.max_tokens, self.g, ptr(self.scores), self.score_stride, s))
-            # The token's key is in the cache already (the q/k/v product wrote it):
-            # re-encode its open group now that the score has read the old planes
+            # The open group is re-encoded once the score has read the old planes
             # (the reference's order: decode, then append_retrieval_caches).
-            check(lib.popkv_append_kv_dyn(
-                None, None, _lib.BF16, B * self.kvh, 128, ptr(kc), ptr(vc), ks, kc.stride(2), vs,
-                vc.stride(2), ptr(self.position), self.max_context, ptr(sign), ptr(mag), ptr(low),
-                ptr(delta), self.meta_capacity, self.tg, self.g, s))
+            if after_score is not None:
+                after_score(layer)
+            else:
+                self._append(layer, s)
             check(lib.popkv_topk_dyn(
                 ptr(self.scores), B * self.qh, ptr(self.position), self.max_tokens, self.score_stride,
                 self.k_max, ptr(self.indices), self.k_max + 1, s))
@@ -384,6 +398,14 @@ class LlamaSparseDecoder:
         cfg, B = self.cfg, self.batch
         H, I, eps = cfg.hidden_size, cfg.intermediate_size, cfg.rms_norm_eps
         QH, D = cfg.num_attention_heads, cfg.head_dim
+        side = self._side
+
+        def fork(fn):
+            ev = torch.cuda.Event()
+            ev.record(stream)
+            side.wait_event(ev)
+            fn(ctypes_stream(side))
+
         for l, lw in enumerate(self.w.layers):
             kc, vc = self.k_cache[l], self.v_cache[l]
             first = l == 0
@@ -394,11 +416,13 @@ class LlamaSparseDecoder:
                 self.max_context - 1, ptr(self.q), ptr(self.k_cur), ptr(self.v_cur), ptr(kc), ptr(vc),
                 kc.stride(0), kc.stride(1), kc.stride(2), vc.stride(0), vc.stride(1), vc.stride(2), s))
             with torch.cuda.stream(stream):
-                self._attention(l, s)
+                self._attention(l, s, after_score=lambda layer: fork(lambda ss: self._append(layer, ss)))
             check(lib.popkv_linear(ptr(lw.o), H, QH * D, ptr(self.attn_full), B, ptr(self.o), H, s))
             check(lib.popkv_norm_gate_up_swiglu(ptr(lw.gate_up), I, H, B, ptr(self.hidden_b), ptr(self.o),
                                                 ptr(lw.post_norm), eps, ptr(self.hidden), ptr(self.act), s))
             check(lib.popkv_linear(ptr(lw.down), H, I, ptr(self.act), B, ptr(self.down), H, s))
+        # The side branch (the appends) rejoins before the position advances.
+        stream.wait_stream(side)
         check(lib.popkv_norm_lm_head_argmax(
             ptr(self.w.lm_head), cfg.vocab_size, H, B, ptr(self.hidden), ptr(self.down), ptr(self.w.norm), eps,
             None, ptr(self.logits), ptr(self.argmax_state), ptr(self.token), ptr(self.position), s))

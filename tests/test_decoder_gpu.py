@@ -234,7 +234,7 @@ class _StaticLengthDecoder(LlamaSparseDecoder):
     cache length per call, as the reference decoder launches its stages
     (popkv.py:1076-1115, append afterwards as popkv.py:884-972)."""
 
-    def _attention(self, layer, s):
+    def _attention(self, layer, s, after_score=None):
         lib, check, ptr = _lib.lib(), _lib.check, _lib.ptr
         t = int(self.position.item())
         B, rows = self.batch, self.batch * self.qh
