@@ -85,6 +85,13 @@ def parse_args(argv=None):
                    help="full 32-layer Llama-3.1-8B-shaped greedy decode (config 2) instead of one layer")
     p.add_argument("--model-method", choices=("popkv-s", "popkv-q", "popkv-normal", "full"), default="popkv-s")
     p.add_argument("--gen-steps", type=int, default=256, help="timed greedy decode steps (--model)")
+    p.add_argument("--prefill", choices=("model", "synthetic"), default="model",
+                   help="--model: run the prefix through the model, or fill the caches with the synthetic "
+                        "key/value distributions (config 4 sizes)")
+    p.add_argument("--products", action="store_true",
+                   help="time the decode step's weight-streaming products against cuBLAS at the model's shapes")
+    p.add_argument("--product-shape", default=None,
+                   help="ROWSxK: one product shape only, 3 launches each (for an ncu capture)")
     return p.parse_args(argv)
 
 
@@ -815,7 +822,10 @@ def run_model(args, world, rank, local):
     ids = torch.randint(0, cfg.vocab_size, (args.batch, T), generator=gen)
     torch.cuda.synchronize(device)
     t_prefill = time.time()
-    dec.prefill(ids)
+    if args.prefill == "model":
+        dec.prefill(ids)
+    else:
+        dec.prefill_synthetic(T, seed=rank)
     prefill_s = time.time() - t_prefill
     stream = torch.cuda.current_stream(device)
     for _ in range(W):
@@ -873,18 +883,24 @@ def run_model(args, world, rank, local):
         # Our kernels per step: dense layer 6 (2 norms, RoPE/append, partial, merge,
         # SiLU), sparse layer 9 (+ score, top-k, append re-encode), final norm 1.
         ours_per_step = dense * 6 + len(dec.sparse_layers) * 9 + 1
+        workload = ("config 2: 32-layer Llama-3.1-8B-shaped decoder" if args.batch == 1 and T <= 65536
+                    else "config 4 shape: 32-layer Llama-3.1-8B-shaped decoder")
         result = {
             "metric": MODEL_METRIC, "value": round(ms, 4), "unit": "ms", "n_gpus": world,
             "steps": K, "warmup": W, "ms_per_step": round(ms, 4), "higher_is_better": False,
             "scaling": "strong",
             "vs_baseline": (round(ms / PUBLISHED_MODEL_MS[method], 4) if method in PUBLISHED_MODEL_MS
                             and args.context == 32768 and args.batch == 1 else None),
-            "dtype": "bf16", "data": "synthetic (random-init weights N(0, 0.02), uniform random prefix ids)",
+            "dtype": "bf16",
+            "data": ("synthetic (random-init weights N(0, 0.02), uniform random prefix ids)" if args.prefill == "model"
+                     else "synthetic (random-init weights N(0, 0.02); prefix K/V drawn from the seeded key/value "
+                          "distributions, no model prefill)"),
             "config": {
-                "workload": f"config 2: 32-layer Llama-3.1-8B-shaped decoder, {method} "
+                "workload": f"{workload}, {method} "
                             f"(layers 0-1 dense), batch {args.batch}, prefix {T}, budget {args.budget}, "
                             f"{K} greedy steps after {W} warm-up steps",
                 "method": method, "batch": args.batch, "prefix": T, "budget": args.budget,
+                "prefill": args.prefill,
                 "context_at_timed_steps": [position0, position0 + K - 1],
                 "parallelism": f"kv-head shard x{world}" + ("" if world == 1 else
                                                             " + NCCL all-gather per layer, replicated MLP"),
@@ -911,6 +927,85 @@ def run_model(args, world, rank, local):
         dist.destroy_process_group()
 
 
+# ---------------------------------------------------------------------------
+# weight-streaming products vs cuBLAS (the model step's dominant kernels)
+# ---------------------------------------------------------------------------
+
+MODEL_PRODUCTS = {"qkv": (6144, 4096), "o_proj": (4096, 4096), "gate_up": (28672, 4096),
+                  "down": (4096, 14336), "lm_head": (128256, 4096)}
+
+
+def run_products(args):
+    """popkv_linear against torch.mm (cuBLAS) at batch 1, each timed as a CUDA graph
+    of back-to-back launches cycling over weight copies larger than L2."""
+    import torch
+    from popkv_b200 import _lib
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    lib, check, ptr = _lib.lib(), _lib.check, _lib.ptr
+    peaks = measured_peaks()
+    shapes = MODEL_PRODUCTS
+    reps = 20
+    if args.product_shape:
+        n, k = (int(v) for v in args.product_shape.lower().split("x"))
+        shapes, reps = {args.product_shape: (n, k)}, 3
+    results = {}
+    for name, (n, k) in shapes.items():
+        copies = max(2, int(3 * L2_BYTES // (n * k * 2)) + 1)
+        gen = torch.Generator(device=device)
+        gen.manual_seed(0)
+        ws = [torch.empty(n, k, device=device, dtype=torch.bfloat16).normal_(generator=gen) for _ in range(copies)]
+        x = torch.empty(1, k, device=device, dtype=torch.bfloat16).normal_(generator=gen)
+        out = torch.empty(1, n, device=device, dtype=torch.bfloat16)
+
+        def ours(i):
+            check(lib.popkv_linear(ptr(ws[i % copies]), n, k, ptr(x), 1, ptr(out), n, _lib.stream_of(device)))
+
+        def cublas(i):
+            torch.mm(x, ws[i % copies].t(), out=out)
+
+        entry = {}
+        for label, fn in (("ours", ours), ("cublas", cublas)):
+            if args.product_shape:  # plain launches, for a profiler
+                for i in range(reps):
+                    fn(i)
+                torch.cuda.synchronize(device)
+                continue
+            us = time_graph(fn, reps, device)
+            gbs = n * k * 2 / (us * 1e-6) / 1e9
+            entry[label] = {"us": round(us, 2), "gbs": round(gbs, 1), "frac_of_hbm": round(gbs / peaks["hbm_gbs"], 4)}
+        results[name] = {"rows": n, "k": k, **entry}
+        del ws
+    if not args.product_shape:
+        print(json.dumps({"metric": "weight-streaming product time, batch 1 (graph-timed, weights > L2)",
+                          "unit": "us", "peak_gbs": peaks["hbm_gbs"], "peak_source": peaks["source"],
+                          "products": results}), flush=True)
+
+
+def time_graph(fn, reps, device) -> float:
+    """Mean device time of fn(i) over `reps` launches captured back to back in one CUDA graph."""
+    import torch
+    side = torch.cuda.Stream(device)
+    side.wait_stream(torch.cuda.current_stream(device))
+    with torch.cuda.stream(side):
+        fn(0)
+        fn(1)
+    torch.cuda.synchronize(device)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=side):
+        for i in range(reps):
+            fn(i)
+    graph.replay()
+    torch.cuda.synchronize(device)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(3):
+        graph.replay()
+    end.record()
+    torch.cuda.synchronize(device)
+    return start.elapsed_time(end) * 1000.0 / (3 * reps)
+
+
 def main(argv=None):
     args = parse_args(argv)
     world, rank, local = dist_env()
@@ -919,6 +1014,9 @@ def main(argv=None):
         return
     if args.model:
         run_model(args, world, rank, local)
+        return
+    if args.products:
+        run_products(args)
         return
     run_ours(args, world, rank, local)
 

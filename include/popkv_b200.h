@@ -409,7 +409,7 @@ POPKV_API int popkv_score_dyn(const void* queries, int queries_dtype, int64_t ba
 /*
  * popkv_topk over fp16 rows of t = *tokens_dev scores with k = min(k_max, t)
  * and the current slot t at out[r*out_stride + k] (out_stride >= k_max + 1).
- * max_tokens <= 131072.  Replaces torch.topk + _append_current
+ * max_tokens <= 262144.  Replaces torch.topk + _append_current
  * (popkv.py:1090-1099, :287-291).
  */
 POPKV_API int popkv_topk_dyn(const uint16_t* scores, int64_t rows, const int64_t* tokens_dev,

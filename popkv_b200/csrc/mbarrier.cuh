@@ -59,7 +59,7 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* mbar, uint32_t b
 }
 
 // Bulk copy of `bytes` (a multiple of 16; both addresses 16-byte aligned) from
-// global to this CTA's shared memory, completing on `mbar`.  No multicast.
+// global to this CTA's shared memory, completing on `mbar`; the destination is this CTA only.
 __device__ __forceinline__ void bulk_copy_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* mbar) {
     asm volatile(
         "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"

@@ -17,7 +17,7 @@
 // because finishing a step needs every peer's rows of that step.
 //
 // The memory is a plain cudaMalloc allocation exported with cudaIpcGetMemHandle:
-// no multicast object, no TMA.
+// no NVLS object, no TMA.
 #include <cstdint>
 #include <cstring>
 

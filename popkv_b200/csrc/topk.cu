@@ -825,7 +825,7 @@ __global__ void __launch_bounds__(kClusterThreads) topk16_cluster_kernel(
     const uint16_t* __restrict__ scores, int64_t tokens, int64_t row_stride, int64_t k,
     int64_t current_index, int64_t* __restrict__ out, int64_t out_stride, bool vec_ok,
     const int64_t* __restrict__ dyn_tokens) {
-    static_assert(PER % 8 == 0 && PER <= 32, "PER keys per thread, whole uint4 loads");
+    static_assert(PER % 8 == 0 && PER <= 64, "PER keys per thread, whole uint4 loads");
     constexpr int64_t kSlice = static_cast<int64_t>(kClusterThreads) * PER;
     __shared__ __align__(16) uint32_t hist[kHistBins];
     __shared__ uint32_t hist2[32];
@@ -1004,7 +1004,8 @@ int launch_cluster16(const void* scores, int64_t rows, int64_t tokens, int64_t r
     return check_launch("popkv_topk");
 }
 
-// fp16 rows of up to 8 * 512 * 32 keys with 0 < k <= tokens < 2^16 per CTA
+// fp16 rows of up to 8 * 512 * 64 keys (64 keys per thread only with 8 CTAs
+// per row) with 0 < k <= tokens and fewer than 2^16 keys per CTA
 // slice: about one wave of CTAs (rows * CPR near 148), the fewest keys per
 // thread that cover the row.  Returns -1 when the shape does not apply.
 int try_launch_cluster16(const void* scores, int64_t rows, int64_t tokens, int64_t row_stride,
@@ -1018,7 +1019,7 @@ int try_launch_cluster16(const void* scores, int64_t rows, int64_t tokens, int64
     while (cpr < 4 && rows * cpr * 2 <= 160) cpr *= 2;
     while (cpr < 8 && tokens > static_cast<int64_t>(cpr) * kClusterThreads * 32) cpr *= 2;
     int per = 8;
-    while (per < 32 && tokens > static_cast<int64_t>(cpr) * kClusterThreads * per) per *= 2;
+    while (per < (cpr == 8 ? 64 : 32) && tokens > static_cast<int64_t>(cpr) * kClusterThreads * per) per *= 2;
     if (tokens > static_cast<int64_t>(cpr) * kClusterThreads * per) return -1;
 #define POPKV_C16(CPR_, PER_)                                                                      \
     if (cpr == CPR_ && per == PER_)                                                                \
@@ -1029,6 +1030,7 @@ int try_launch_cluster16(const void* scores, int64_t rows, int64_t tokens, int64
     POPKV_C16_CPR(2)
     POPKV_C16_CPR(4)
     POPKV_C16_CPR(8)
+    POPKV_C16(8, 64)
 #undef POPKV_C16_CPR
 #undef POPKV_C16
     return -1;
@@ -1147,6 +1149,6 @@ extern "C" int popkv_topk_dyn(const uint16_t* scores, int64_t rows, const int64_
                                         out_stride, vec_ok, static_cast<cudaStream_t>(stream), tokens_dev);
     if (st < 0)
         return fail(POPKV_ERR_UNSUPPORTED, "popkv_topk_dyn: at most %d tokens and %d rows per launch",
-                    8 * kClusterThreads * 32, 0x7FFFFFF);
+                    8 * kClusterThreads * 64, 0x7FFFFFF);
     return st;
 }

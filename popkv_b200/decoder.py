@@ -399,12 +399,14 @@ class LlamaSparseDecoder:
         H, I, eps = cfg.hidden_size, cfg.intermediate_size, cfg.rms_norm_eps
         QH, D = cfg.num_attention_heads, cfg.head_dim
         side = self._side
+        forked = []
 
         def fork(fn):
             ev = torch.cuda.Event()
             ev.record(stream)
             side.wait_event(ev)
             fn(ctypes_stream(side))
+            forked.append(True)
 
         for l, lw in enumerate(self.w.layers):
             kc, vc = self.k_cache[l], self.v_cache[l]
@@ -422,7 +424,8 @@ class LlamaSparseDecoder:
                                                 ptr(lw.post_norm), eps, ptr(self.hidden), ptr(self.act), s))
             check(lib.popkv_linear(ptr(lw.down), H, I, ptr(self.act), B, ptr(self.down), H, s))
         # The side branch (the appends) rejoins before the position advances.
-        stream.wait_stream(side)
+        if forked:
+            stream.wait_stream(side)
         check(lib.popkv_norm_lm_head_argmax(
             ptr(self.w.lm_head), cfg.vocab_size, H, B, ptr(self.hidden), ptr(self.down), ptr(self.w.norm), eps,
             None, ptr(self.logits), ptr(self.argmax_state), ptr(self.token), ptr(self.position), s))
@@ -542,6 +545,40 @@ class LlamaSparseDecoder:
         self._pack_prefix(T)
         self.prefix_length = T
         self.position.fill_(T)
+        self.token.copy_(first)
+        torch.cuda.synchronize(dev)
+        return first
+
+    @torch.inference_mode()
+    def prefill_synthetic(self, T: int, *, seed: int = 0, chunk: int = 16384) -> torch.Tensor:
+        """Fill KV-cache rows [0, T) with the synthetic key/value distributions instead
+        of running the model over a prefix (for contexts where a model prefill would
+        take minutes, e.g. batch 16 x 131072 tokens).
+
+        Keys: N(0, 1) per element times a per-(sequence, KV head, channel) factor
+        exp(N(0, 0.5)) (outlier channels), then RoPE at the token's position;
+        values N(0, 1) -- the benchmark configuration's stand-in distributions
+        (popkv_b200.workloads), drawn on the device.  Packs the sparse layers'
+        planes, sets the position to T and the next input token to a seeded id.
+        """
+        if not 0 < T <= self.max_tokens:
+            raise ValueError(f"prefix length must be in [1, {self.max_tokens}]")
+        dev, D = self.device, self.cfg.head_dim
+        gen = torch.Generator(device=dev)
+        gen.manual_seed(seed)
+        for l in range(self.cfg.num_hidden_layers):
+            kc, vc = self.k_cache[l], self.v_cache[l]
+            for b in range(self.batch):
+                factors = torch.empty((self.kvh, 1, D), device=dev).normal_(0.0, 0.5, generator=gen).exp_()
+                for c0 in range(0, T, chunk):
+                    c1 = min(T, c0 + chunk)
+                    k = torch.empty((self.kvh, c1 - c0, D), device=dev).normal_(generator=gen).mul_(factors)
+                    kc[b, :, c0:c1] = apply_rope(k.to(torch.bfloat16), self.cos[c0:c1], self.sin[c0:c1])
+                    vc[b, :, c0:c1] = torch.empty((self.kvh, c1 - c0, D), device=dev).normal_(generator=gen)
+        self._pack_prefix(T)
+        self.prefix_length = T
+        self.position.fill_(T)
+        first = torch.randint(0, self.cfg.vocab_size, (self.batch,), device=dev, generator=gen)
         self.token.copy_(first)
         torch.cuda.synchronize(dev)
         return first

@@ -493,3 +493,31 @@ def test_weight_streaming_products_match_fp32_matmul(cuda_device, batch):
         close = (got.float() - want.float()).abs() <= 2 ** -6 * want.float().abs() + 1e-3
         assert float(close.float().mean()) > 0.98
     assert torch.count_nonzero(kc[:, :, :33]) == 0 and torch.count_nonzero(kc[:, :, 34:]) == 0
+
+
+def test_topk_dyn_beyond_128k_tokens(cuda_device):
+    """Rows longer than 131072 keys (config 4's 128K context plus decoded tokens)."""
+    dev = cuda_device
+    lib, check, ptr = _lib.lib(), _lib.check, _lib.ptr
+    gen = torch.Generator().manual_seed(3)
+    rows, max_tokens, k_max = 6, 131072 + 700, 4095
+    stride = (max_tokens + 7) // 8 * 8
+    scores = (torch.randn(rows, stride, generator=gen) * 4).to(torch.float16).to(dev)
+    scores[:, 5000:5100] = 7.5  # a block of ties
+    for t in (max_tokens, 131072 + 3, 90000):
+        pos = torch.tensor([t], device=dev, dtype=torch.int64)
+        out = torch.empty(rows, k_max + 1, device=dev, dtype=torch.int64)
+        check(lib.popkv_topk_dyn(ptr(scores), rows, ptr(pos), max_tokens, stride, k_max, ptr(out), k_max + 1,
+                                 _stream(dev)))
+        ref = torch.empty_like(out)
+        check(lib.popkv_topk(ptr(scores), _lib.F16, rows, t, stride, k_max, t, ptr(ref), k_max + 1, _stream(dev)))
+        torch.cuda.synchronize()
+        assert torch.equal(out, ref)
+        # Selection semantics: every chosen score >= every unchosen one.
+        sel = out[:, :k_max]
+        chosen = torch.gather(scores[:, :t].float(), 1, sel)
+        mask = torch.ones(rows, t, dtype=torch.bool, device=dev)
+        mask.scatter_(1, sel, False)
+        rest = scores[:, :t].float().masked_fill(~mask, float("-inf"))
+        assert torch.all(chosen.min(1).values >= rest.max(1).values)
+        assert torch.all(out[:, k_max] == t)
