@@ -537,6 +537,35 @@ POPKV_API int popkv_norm_qkv_rope(const void* w, int64_t q_heads, int64_t kv_hea
 POPKV_API int popkv_norm_gate_up_swiglu(const void* w, int64_t inter, int64_t k, int64_t batch,
                                         const void* hidden, const void* delta, const void* norm_w, float eps,
                                         void* hidden_out, void* act, void* stream);
+/*
+ * A layer's tail at batch 1 in one persistent launch (one CTA per SM):
+ * o_out = o_w attn; act = SwiGLU(gate_up_w RMSNorm(hidden_mid + o_out)) with
+ * hidden = hidden_mid + o_out stored; down_out = down_w act; then either the
+ * next layer's popkv_norm_qkv_rope (next_qkv_w non-NULL: hidden + down_out,
+ * stored to hidden_mid_out, normalised with next_input_norm, RoPE at
+ * *position_dev into q_out / k_cur / v_cur and the caches) or, with next_qkv_w
+ * NULL, popkv_norm_lm_head_argmax (final_norm, logits, argmax_state [2],
+ * token_next, and *position_dev advanced by one).  Weight copies stream
+ * across the phase boundaries; the phases meet at a bounded grid barrier on
+ * `barrier` (2 uint32, zero at setup, left reusable).  Same results as the
+ * separate products.  Replaces o_proj + MLP + the next layer's projections
+ * (popkv.py:1103-1112, :1009-1016).
+ */
+POPKV_API int popkv_layer_tail(int64_t hidden_size, int64_t inter, int64_t attn_width, const void* o_w,
+                               const void* attn, void* o_out, const void* gate_up_w, const void* post_norm,
+                               const void* hidden_mid, void* hidden, void* act, float eps, const void* down_w,
+                               void* down_out, const void* next_qkv_w, int64_t q_heads, int64_t kv_heads,
+                               const void* next_input_norm, void* hidden_mid_out, const void* cos_table,
+                               const void* sin_table, const int64_t* position_dev, int64_t max_position,
+                               void* q_out, void* k_cur, void* v_cur, void* k_cache, void* v_cache,
+                               int64_t k_batch_stride, int64_t k_head_stride, int64_t k_token_stride,
+                               int64_t v_batch_stride, int64_t v_head_stride, int64_t v_token_stride,
+                               const void* lm_head_w, int64_t vocab, const void* final_norm, void* logits,
+                               unsigned long long* argmax_state, int64_t* token_next, unsigned int* barrier,
+                               void* stream);
+/* Count of layer-tail waits (a weight copy or the grid barrier) that gave up
+ * since the library was loaded; 0 in a healthy run.  Synchronises. */
+POPKV_API int popkv_layer_tail_timeouts(uint32_t* count);
 POPKV_API int popkv_norm_lm_head_argmax(const void* w, int64_t vocab, int64_t k, int64_t batch,
                                         const void* hidden, const void* delta, const void* norm_w, float eps,
                                         void* hidden_out, void* logits, unsigned long long* argmax_state,

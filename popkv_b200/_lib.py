@@ -60,6 +60,10 @@ _SIGNATURES = {
                            _L, _L, _L, _P], _I),
     "popkv_silu_mul": ([_P, _L, _L, _P, _P], _I),
     "popkv_gemv_timeouts": ([ctypes.POINTER(ctypes.c_uint32)], _I),
+    "popkv_layer_tail": ([_L, _L, _L, _P, _P, _P, _P, _P, _P, _P, _P, ctypes.c_float, _P, _P, _P, _L, _L,
+                          _P, _P, _P, _P, _P, _L, _P, _P, _P, _P, _P, _L, _L, _L, _L, _L, _L, _P, _L, _P,
+                          _P, _P, _P, _P, _P], _I),
+    "popkv_layer_tail_timeouts": ([ctypes.POINTER(ctypes.c_uint32)], _I),
     "popkv_linear": ([_P, _L, _L, _P, _L, _P, _L, _P], _I),
     "popkv_norm_qkv_rope": ([_P, _L, _L, _L, _L, _P, _P, _P, _P, _P, ctypes.c_float, _P, _P, _P, _P, _L,
                              _P, _P, _P, _P, _P, _L, _L, _L, _L, _L, _L, _P], _I),

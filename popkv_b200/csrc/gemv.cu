@@ -270,6 +270,30 @@ __device__ __forceinline__ void unit_epilogue(const GemvArgs& a, int64_t u, int6
     }
 }
 
+// The greedy choice over all CTAs: each CTA folds its best key into the global
+// one; the last CTA to arrive writes the token ids, clears the state and
+// advances the position.
+__device__ __forceinline__ void argmax_finish(const GemvArgs& a, unsigned long long* cta_key, unsigned int& s_last) {
+    const int tid = threadIdx.x;
+    __syncthreads();
+    if (tid < a.batch && cta_key[tid]) atomicMax(a.argmax_key + tid, cta_key[tid]);
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) s_last = atomicAdd(a.done, 1u) == gridDim.x - 1;
+    __syncthreads();
+    if (s_last) {
+        __threadfence();
+        if (tid < a.batch) {
+            const unsigned long long key = atomicExch(a.argmax_key + tid, 0ull);
+            a.token_next[tid] = static_cast<int64_t>(0xFFFFFFFFu - static_cast<uint32_t>(key & 0xFFFFFFFFull));
+        }
+        if (tid == 0) {
+            *a.done = 0u;
+            if (a.advance) *a.advance += 1;
+        }
+    }
+}
+
 // Weights move in pieces of up to kPieceElems elements of one row; each warp
 // streams its own pieces through a private ring of S shared-memory slots with
 // bulk asynchronous copies (lane 0 issues, every lane waits on the slot's
@@ -407,25 +431,204 @@ __global__ void __launch_bounds__(kTmaThreads, 1) gemv_kernel(const GemvArgs a) 
         }
         __syncwarp();
     }
-    if constexpr (EPI == kArgmax) {
-        __syncthreads();
-        if (tid < a.batch && cta_key[tid]) atomicMax(a.argmax_key + tid, cta_key[tid]);
+    if constexpr (EPI == kArgmax) argmax_finish(a, cta_key, s_last);
+}
+
+// ---------------------------------------------------------------------------
+// Layer tail (batch 1): o_proj -> gate/up + SwiGLU -> down -> the next layer's
+// q/k/v + RoPE, or the LM head + greedy argmax after the last layer, in one
+// persistent launch of one CTA per SM.  Each warp's ring streams its pieces of
+// all four phases back to back, so HBM stays busy across the phase boundaries;
+// only the compute of phase p + 1 waits for every CTA to finish phase p (its
+// input is phase p's output): a bounded grid barrier, then the CTA rebuilds x
+// in shared memory.  One CTA per SM (220 KB of shared memory) and a grid of at
+// most one CTA per SM make every CTA co-resident once earlier kernels drain.
+// ---------------------------------------------------------------------------
+constexpr int kTailPhases = 4;
+constexpr int kTailSlots = 3;
+constexpr int kGridPolls = 1 << 22;
+
+struct TailArgs {
+    GemvArgs ph[kTailPhases];
+    unsigned int* barrier;  // [2]: arrivals, generation; zero at setup, self-resetting
+};
+
+__device__ unsigned int g_tail_timeouts = 0;
+
+// Grid-wide barrier of co-resident CTAs; false if the bounded wait gave up.
+__device__ __forceinline__ bool grid_barrier(unsigned int* bar) {
+    __shared__ int s_ok;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        volatile unsigned int* vb = bar;
+        const unsigned int gen = vb[1];
         __threadfence();
-        __syncthreads();
-        if (tid == 0) s_last = atomicAdd(a.done, 1u) == gridDim.x - 1;
-        __syncthreads();
-        if (s_last) {
+        int ok = 1;
+        if (atomicAdd(bar, 1u) == gridDim.x - 1) {
+            atomicExch(bar, 0u);
             __threadfence();
-            if (tid < a.batch) {
-                const unsigned long long key = atomicExch(a.argmax_key + tid, 0ull);
-                a.token_next[tid] = static_cast<int64_t>(0xFFFFFFFFu - static_cast<uint32_t>(key & 0xFFFFFFFFull));
+            atomicAdd(bar + 1, 1u);
+        } else {
+            ok = 0;
+            for (int i = 0; i < kGridPolls; ++i) {
+                if (vb[1] != gen) {
+                    ok = 1;
+                    break;
+                }
+                __nanosleep(64);
             }
-            if (tid == 0) {
-                *a.done = 0u;
-                if (a.advance) *a.advance += 1;
+        }
+        __threadfence();
+        s_ok = ok;
+    }
+    __syncthreads();
+    return s_ok != 0;
+}
+
+template <int LAST>
+__device__ __forceinline__ int tail_rows_per_unit(int p) {
+    return (p == 1 || (p == 3 && LAST == kRope)) ? 2 : 1;
+}
+
+template <int LAST>
+__device__ __forceinline__ void tail_rows(int p, const GemvArgs& a, int64_t u, int64_t& r0, int64_t& r1) {
+    if (p == 1) unit_rows<kSwiglu>(a, u, r0, r1);
+    else if (p == 3 && LAST == kRope) unit_rows<kRope>(a, u, r0, r1);
+    else unit_rows<kStore>(a, u, r0, r1);
+}
+
+template <int LAST>
+__global__ void __launch_bounds__(kTmaThreads, 1) layer_tail_kernel(const TailArgs t) {
+    constexpr int S = kTailSlots;
+    extern __shared__ __align__(128) uint4 smem[];
+    uint4* ring = smem;
+    uint4* xs = smem + kTmaWarps * S * (kPieceBytes / 16);
+    __shared__ __align__(8) uint64_t bars[kTmaWarps][S];
+    __shared__ float red[kMaxBatch * kTmaWarps];
+    __shared__ unsigned long long cta_key[kMaxBatch];
+    __shared__ unsigned int s_last;
+
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int64_t gw = static_cast<int64_t>(blockIdx.x) * kTmaWarps + warp;
+    uint4* my_ring = ring + static_cast<int64_t>(warp) * S * (kPieceBytes / 16);
+
+    // This warp's pieces, phase by phase.
+    int64_t cum[kTailPhases + 1];
+    int npieces[kTailPhases], ppu[kTailPhases];
+    cum[0] = 0;
+#pragma unroll
+    for (int p = 0; p < kTailPhases; ++p) {
+        const GemvArgs& a = t.ph[p];
+        npieces[p] = (a.k + kPieceElems - 1) / kPieceElems;
+        ppu[p] = tail_rows_per_unit<LAST>(p) * npieces[p];
+        const int64_t mine = (gw < a.active_warps && gw < a.units) ? (a.units - 1 - gw) / a.active_warps + 1 : 0;
+        cum[p + 1] = cum[p] + mine * ppu[p];
+    }
+    const int64_t total = cum[kTailPhases];
+
+    auto issue = [&](int64_t j) {
+        int p = 0;
+        while (p < kTailPhases - 1 && j >= cum[p + 1]) ++p;
+        const GemvArgs& a = t.ph[p];
+        const int64_t local = j - cum[p];
+        const int rem = static_cast<int>(local % ppu[p]);
+        const int r = rem / npieces[p], pc = rem % npieces[p];
+        int64_t r0, r1;
+        tail_rows<LAST>(p, a, gw + (local / ppu[p]) * a.active_warps, r0, r1);
+        const int64_t k = a.k;
+        const int64_t row = r == 0 ? r0 : r1;
+        const int64_t off = static_cast<int64_t>(pc) * kPieceElems;
+        const int64_t elems = k - off < kPieceElems ? k - off : kPieceElems;
+        const int st = static_cast<int>(j % S);
+        mbar_arrive_expect_tx(&bars[warp][st], static_cast<uint32_t>(elems * 2));
+        bulk_copy_g2s(my_ring + st * (kPieceBytes / 16), a.w + row * k + off, static_cast<uint32_t>(elems * 2),
+                      &bars[warp][st]);
+    };
+
+    if (lane == 0) {
+#pragma unroll
+        for (int st = 0; st < S; ++st) mbar_init(&bars[warp][st], 1);
+        fence_async_smem();
+        for (int64_t j = 0; j < S && j < total; ++j) issue(j);
+    }
+    if (tid < kMaxBatch) cta_key[tid] = 0ull;
+    __syncwarp();
+    pdl_wait();
+    pdl_launch_dependents();
+
+    bool failed = false;
+    int64_t j = 0, j_fail = 0;
+    for (int p = 0; p < kTailPhases; ++p) {
+        const GemvArgs& a = t.ph[p];
+        if (p > 0 && !grid_barrier(t.barrier) && tid == 0) atomicAdd(&g_tail_timeouts, 1u);
+        if (p == 1 || p == 3) load_x_norm<1, kTmaThreads, kTmaWarps>(a, xs, red);
+        else load_x_plain<1, kTmaThreads>(a, xs);
+        int64_t pos = 0;
+        if (p == 3 && LAST == kRope) {
+            pos = *a.position;
+            pos = pos < 0 ? 0 : (pos > a.max_position ? a.max_position : pos);
+        }
+        float acc0[2] = {0.0f, 0.0f}, acc1[2] = {0.0f, 0.0f};
+        for (; j < cum[p + 1]; ++j) {
+            if (failed) continue;
+            const int st = static_cast<int>(j % S);
+            if (!__all_sync(0xFFFFFFFFu, mbar_wait(&bars[warp][st], static_cast<uint32_t>((j / S) & 1)))) {
+                failed = true;
+                j_fail = j;
+                if (lane == 0) atomicAdd(&g_tail_timeouts, 1u);
+                continue;
+            }
+            const int64_t local = j - cum[p];
+            const int rem = static_cast<int>(local % ppu[p]);
+            const int r = rem / npieces[p], pc = rem % npieces[p];
+            const int pch = (a.k - pc * kPieceElems < kPieceElems ? a.k - pc * kPieceElems : kPieceElems) / 8;
+            const uint4* wp = my_ring + st * (kPieceBytes / 16);
+            const uint4* xp = xs + pc * (kPieceElems / 8);
+            if (r == 0) {
+#pragma unroll 4
+                for (int c = lane; c < pch; c += 32) dot8(wp[c], xp[c], acc0[0], acc1[0]);
+            } else {
+#pragma unroll 4
+                for (int c = lane; c < pch; c += 32) dot8(wp[c], xp[c], acc0[1], acc1[1]);
+            }
+            __syncwarp();
+            if (lane == 0 && j + S < total) {
+                fence_async_smem();
+                issue(j + S);
+            }
+            if (rem == ppu[p] - 1) {
+                const int64_t u = gw + (local / ppu[p]) * a.active_warps;
+                int64_t r0, r1;
+                tail_rows<LAST>(p, a, u, r0, r1);
+                float y[2][1];
+                y[0][0] = round_bf(warp_sum(acc0[0] + acc1[0]));
+                y[1][0] = round_bf(warp_sum(acc0[1] + acc1[1]));
+                acc0[0] = acc0[1] = acc1[0] = acc1[1] = 0.0f;
+                if (lane == 0) {
+                    if (p == 1) {
+                        const float (&yy)[2][1] = y;
+                        unit_epilogue<1, kSwiglu, 2>(a, u, r0, yy, pos, cta_key);
+                    } else if (p == 3) {
+                        if constexpr (LAST == kRope) {
+                            unit_epilogue<1, kRope, 2>(a, u, r0, y, pos, cta_key);
+                        } else {
+                            const float y1[1][1] = {{y[0][0]}};
+                            unit_epilogue<1, kArgmax, 1>(a, u, r0, y1, pos, cta_key);
+                        }
+                    } else {
+                        const float y1[1][1] = {{y[0][0]}};
+                        unit_epilogue<1, kStore, 1>(a, u, r0, y1, pos, cta_key);
+                    }
+                }
             }
         }
     }
+    if (failed && lane == 0) {  // the copies still in flight land before the CTA exits
+        for (int64_t jj = j_fail; jj < total && jj < j_fail + S; ++jj)
+            mbar_wait(&bars[warp][jj % S], static_cast<uint32_t>((jj / S) & 1));
+    }
+    __syncwarp();
+    if constexpr (LAST == kArgmax) argmax_finish(t.ph[kTailPhases - 1], cta_key, s_last);
 }
 
 int g_sm_count[64] = {0};
@@ -618,5 +821,131 @@ extern "C" int popkv_gemv_timeouts(uint32_t* count) {
     if (!count) return fail(POPKV_ERR_INVALID, "popkv_gemv_timeouts: null pointer");
     const cudaError_t err = cudaMemcpyFromSymbol(count, g_gemv_timeouts, sizeof(uint32_t));
     if (err != cudaSuccess) return fail(POPKV_ERR_CUDA, "popkv_gemv_timeouts: %s", cudaGetErrorString(err));
+    return POPKV_OK;
+}
+
+namespace popkv {
+namespace {
+
+template <int LAST>
+int launch_tail(TailArgs t, cudaStream_t stream) {
+    const int sms = sm_count();
+    const int64_t warps = static_cast<int64_t>(sms) * kTmaWarps;
+    for (int p = 0; p < kTailPhases; ++p) {
+        const int64_t rounds = (t.ph[p].units + warps - 1) / warps;
+        t.ph[p].active_warps = static_cast<int>(rounds > 0 ? (t.ph[p].units + rounds - 1) / rounds : 1);
+    }
+    int64_t kmax = 0;
+    for (int p = 0; p < kTailPhases; ++p) kmax = t.ph[p].k > kmax ? t.ph[p].k : kmax;
+    const size_t smem = static_cast<size_t>(kTmaWarps) * kTailSlots * kPieceBytes + static_cast<size_t>(kmax) * 2;
+    if (smem + 4096 > static_cast<size_t>(kSmemBudget))
+        return fail(POPKV_ERR_UNSUPPORTED, "popkv_layer_tail: k too large for shared memory");
+    const int st = allow_dynamic_smem(layer_tail_kernel<LAST>, static_cast<int>(smem));
+    if (st != POPKV_OK) return st;
+    const cudaError_t err = launch_pdl(layer_tail_kernel<LAST>, dim3(static_cast<unsigned>(sms)), dim3(kTmaThreads),
+                                       smem, stream, 1, t);
+    if (err != cudaSuccess) return fail(POPKV_ERR_CUDA, "popkv_layer_tail: %s", cudaGetErrorString(err));
+    return check_launch("popkv_layer_tail");
+}
+
+}  // namespace
+}  // namespace popkv
+
+extern "C" int popkv_layer_tail(int64_t hidden_size, int64_t inter, int64_t attn_width, const void* o_w,
+                                const void* attn, void* o_out, const void* gate_up_w, const void* post_norm,
+                                const void* hidden_mid, void* hidden, void* act, float eps, const void* down_w,
+                                void* down_out, const void* next_qkv_w, int64_t q_heads, int64_t kv_heads,
+                                const void* next_input_norm, void* hidden_mid_out, const void* cos_table,
+                                const void* sin_table, const int64_t* position_dev, int64_t max_position,
+                                void* q_out, void* k_cur, void* v_cur, void* k_cache, void* v_cache,
+                                int64_t k_batch_stride, int64_t k_head_stride, int64_t k_token_stride,
+                                int64_t v_batch_stride, int64_t v_head_stride, int64_t v_token_stride,
+                                const void* lm_head_w, int64_t vocab, const void* final_norm, void* logits,
+                                unsigned long long* argmax_state, int64_t* token_next, unsigned int* barrier,
+                                void* stream) {
+    using namespace popkv;
+    const char* name = "popkv_layer_tail";
+    const int64_t H = hidden_size;
+    int st = check_common(o_w, H, attn_width, 1, name);
+    if (st == POPKV_OK) st = check_common(gate_up_w, 2 * inter, H, 1, name);
+    if (st == POPKV_OK) st = check_common(down_w, H, inter, 1, name);
+    if (st != POPKV_OK) return st;
+    if (!attn || !o_out || !act || !down_out || !barrier || !aligned(attn, 16) || !aligned(o_out, 16) ||
+        !aligned(act, 16) || !aligned(down_out, 16))
+        return fail(POPKV_ERR_INVALID, "%s: null or unaligned buffer", name);
+    st = check_norm(hidden_mid, o_out, nullptr, nullptr, post_norm, hidden, name);
+    if (st != POPKV_OK) return st;
+    TailArgs t{};
+    t.barrier = barrier;
+    GemvArgs& o = t.ph[0];
+    o.w = static_cast<const __nv_bfloat16*>(o_w);
+    o.units = H;
+    o.k = static_cast<int>(attn_width);
+    o.batch = 1;
+    o.x = static_cast<const __nv_bfloat16*>(attn);
+    o.out = static_cast<__nv_bfloat16*>(o_out);
+    o.out_stride = H;
+    t.ph[1] = norm_args(gate_up_w, inter, H, 1, hidden_mid, o_out, nullptr, nullptr, post_norm, eps, hidden);
+    t.ph[1].out = static_cast<__nv_bfloat16*>(act);
+    t.ph[1].out_stride = inter;
+    t.ph[1].pair_offset = inter;
+    GemvArgs& d = t.ph[2];
+    d.w = static_cast<const __nv_bfloat16*>(down_w);
+    d.units = H;
+    d.k = static_cast<int>(inter);
+    d.batch = 1;
+    d.x = static_cast<const __nv_bfloat16*>(act);
+    d.out = static_cast<__nv_bfloat16*>(down_out);
+    d.out_stride = H;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (next_qkv_w) {
+        if (q_heads <= 0 || kv_heads <= 0 || !cos_table || !sin_table || !position_dev || !q_out || !k_cur ||
+            !v_cur || !k_cache || !v_cache || max_position < 0)
+            return fail(POPKV_ERR_INVALID, "%s: null pointer or invalid heads for the q/k/v phase", name);
+        st = check_common(next_qkv_w, (q_heads + 2 * kv_heads) * 128, H, 1, name);
+        if (st == POPKV_OK) st = check_norm(hidden, down_out, nullptr, nullptr, next_input_norm, hidden_mid_out, name);
+        if (st != POPKV_OK) return st;
+        GemvArgs& q = t.ph[3];
+        q = norm_args(next_qkv_w, (q_heads + 2 * kv_heads) * 64, H, 1, hidden, down_out, nullptr, nullptr,
+                      next_input_norm, eps, hidden_mid_out);
+        q.q_heads = static_cast<int>(q_heads);
+        q.kv_heads = static_cast<int>(kv_heads);
+        q.cos_tab = static_cast<const __nv_bfloat16*>(cos_table);
+        q.sin_tab = static_cast<const __nv_bfloat16*>(sin_table);
+        q.position = position_dev;
+        q.max_position = max_position;
+        q.q_out = static_cast<__nv_bfloat16*>(q_out);
+        q.k_cur = static_cast<__nv_bfloat16*>(k_cur);
+        q.v_cur = static_cast<__nv_bfloat16*>(v_cur);
+        q.k_cache = static_cast<__nv_bfloat16*>(k_cache);
+        q.v_cache = static_cast<__nv_bfloat16*>(v_cache);
+        q.kbs = k_batch_stride;
+        q.khs = k_head_stride;
+        q.kts = k_token_stride;
+        q.vbs = v_batch_stride;
+        q.vhs = v_head_stride;
+        q.vts = v_token_stride;
+        return launch_tail<kRope>(t, s);
+    }
+    if (!lm_head_w || !final_norm || !logits || !argmax_state || !token_next)
+        return fail(POPKV_ERR_INVALID, "%s: null pointer for the LM-head phase", name);
+    st = check_common(lm_head_w, vocab, H, 1, name);
+    if (st != POPKV_OK) return st;
+    GemvArgs& l = t.ph[3];
+    l = norm_args(lm_head_w, vocab, H, 1, hidden, down_out, nullptr, nullptr, final_norm, eps, nullptr);
+    l.out = static_cast<__nv_bfloat16*>(logits);
+    l.out_stride = vocab;
+    l.argmax_key = argmax_state;
+    l.done = reinterpret_cast<unsigned int*>(argmax_state + 1);
+    l.token_next = token_next;
+    l.advance = const_cast<int64_t*>(position_dev);
+    return launch_tail<kArgmax>(t, s);
+}
+
+extern "C" int popkv_layer_tail_timeouts(uint32_t* count) {
+    using namespace popkv;
+    if (!count) return fail(POPKV_ERR_INVALID, "popkv_layer_tail_timeouts: null pointer");
+    const cudaError_t err = cudaMemcpyFromSymbol(count, g_tail_timeouts, sizeof(uint32_t));
+    if (err != cudaSuccess) return fail(POPKV_ERR_CUDA, "popkv_layer_tail_timeouts: %s", cudaGetErrorString(err));
     return POPKV_OK;
 }

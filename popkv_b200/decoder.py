@@ -260,6 +260,10 @@ class LlamaSparseDecoder:
         self.x = torch.zeros((B, H), device=dev, dtype=bf)
         # Fused weight-streaming products (batch <= 4); cuBLAS + separate kernels otherwise.
         self.fused = B <= 4
+        # Batch 1, opt-in: each layer's o_proj .. next q/k/v as one persistent
+        # launch (bit-identical results; see layer_tail).
+        self.tail = False
+        self.tail_barrier = torch.zeros(2, device=dev, dtype=torch.int32)
         self.argmax_state = torch.zeros(B + 1, device=dev, dtype=torch.int64)
         self.qkv = torch.zeros((B, (self.qh + 2 * self.kvh) * D), device=dev, dtype=bf)
         self.q = torch.zeros((B, self.qh, D), device=dev, dtype=bf)
@@ -408,21 +412,44 @@ class LlamaSparseDecoder:
             fn(ctypes_stream(side))
             forked.append(True)
 
+        L = len(self.w.layers)
         for l, lw in enumerate(self.w.layers):
             kc, vc = self.k_cache[l], self.v_cache[l]
             first = l == 0
-            check(lib.popkv_norm_qkv_rope(
-                ptr(self.qkv_weights[l]), self.qh, self.kvh, H, B, None if first else ptr(self.hidden),
-                None if first else ptr(self.down), ptr(self.w.embed) if first else None, ptr(self.token),
-                ptr(lw.input_norm), eps, ptr(self.hidden_b), ptr(self.cos), ptr(self.sin), ptr(self.position),
-                self.max_context - 1, ptr(self.q), ptr(self.k_cur), ptr(self.v_cur), ptr(kc), ptr(vc),
-                kc.stride(0), kc.stride(1), kc.stride(2), vc.stride(0), vc.stride(1), vc.stride(2), s))
+            if first or not self.tail:
+                check(lib.popkv_norm_qkv_rope(
+                    ptr(self.qkv_weights[l]), self.qh, self.kvh, H, B, None if first else ptr(self.hidden),
+                    None if first else ptr(self.down), ptr(self.w.embed) if first else None, ptr(self.token),
+                    ptr(lw.input_norm), eps, ptr(self.hidden_b), ptr(self.cos), ptr(self.sin), ptr(self.position),
+                    self.max_context - 1, ptr(self.q), ptr(self.k_cur), ptr(self.v_cur), ptr(kc), ptr(vc),
+                    kc.stride(0), kc.stride(1), kc.stride(2), vc.stride(0), vc.stride(1), vc.stride(2), s))
             with torch.cuda.stream(stream):
                 self._attention(l, s, after_score=lambda layer: fork(lambda ss: self._append(layer, ss)))
+            if self.tail:
+                # o_proj, gate/up + SwiGLU, down and the next layer's q/k/v (or the LM
+                # head) in one persistent launch.  The side branch (the appends)
+                # rejoins before the LM head advances the position.
+                last = l == L - 1
+                if last and forked:
+                    stream.wait_stream(side)
+                nk, nv = (kc, vc) if last else (self.k_cache[l + 1], self.v_cache[l + 1])
+                check(lib.popkv_layer_tail(
+                    H, I, QH * D, ptr(lw.o), ptr(self.attn_full), ptr(self.o), ptr(lw.gate_up), ptr(lw.post_norm),
+                    ptr(self.hidden_b), ptr(self.hidden), ptr(self.act), eps, ptr(lw.down), ptr(self.down),
+                    None if last else ptr(self.qkv_weights[l + 1]), self.qh, self.kvh,
+                    None if last else ptr(self.w.layers[l + 1].input_norm), ptr(self.hidden_b), ptr(self.cos),
+                    ptr(self.sin), ptr(self.position), self.max_context - 1, ptr(self.q), ptr(self.k_cur),
+                    ptr(self.v_cur), ptr(nk), ptr(nv), nk.stride(0), nk.stride(1), nk.stride(2), nv.stride(0),
+                    nv.stride(1), nv.stride(2), ptr(self.w.lm_head) if last else None, cfg.vocab_size,
+                    ptr(self.w.norm), ptr(self.logits), ptr(self.argmax_state), ptr(self.token),
+                    ptr(self.tail_barrier), s))
+                continue
             check(lib.popkv_linear(ptr(lw.o), H, QH * D, ptr(self.attn_full), B, ptr(self.o), H, s))
             check(lib.popkv_norm_gate_up_swiglu(ptr(lw.gate_up), I, H, B, ptr(self.hidden_b), ptr(self.o),
                                                 ptr(lw.post_norm), eps, ptr(self.hidden), ptr(self.act), s))
             check(lib.popkv_linear(ptr(lw.down), H, I, ptr(self.act), B, ptr(self.down), H, s))
+        if self.tail:
+            return
         # The side branch (the appends) rejoins before the position advances.
         if forked:
             stream.wait_stream(side)

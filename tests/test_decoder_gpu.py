@@ -521,3 +521,30 @@ def test_topk_dyn_beyond_128k_tokens(cuda_device):
         rest = scores[:, :t].float().masked_fill(~mask, float("-inf"))
         assert torch.all(chosen.min(1).values >= rest.max(1).values)
         assert torch.all(out[:, k_max] == t)
+
+
+@pytest.mark.parametrize("method", ["popkv-s", "full"])
+def test_layer_tail_matches_separate_products(cuda_device, method):
+    """The persistent layer tail (batch 1) reproduces the separate products bit for bit."""
+    import ctypes
+    weights = LlamaWeights.random(TINY, device=cuda_device, seed=5, std=0.05)
+    retrieval = RetrievalConfig(budget=64, group_size=64, dim_group_size=64)
+    ids = _prefix(TINY, 1, 150, seed=2)
+    a = LlamaSparseDecoder(weights, method=method, retrieval=retrieval, max_context=180)
+    b = LlamaSparseDecoder(weights, method=method, retrieval=retrieval, max_context=180)
+    a.tail = True
+    a.capture()
+    assert not b.tail
+    a.prefill(ids)
+    b.prefill(ids)
+    for _ in range(12):
+        la, lb = a.decode().clone(), b.decode().clone()
+        assert torch.equal(la, lb)
+        assert torch.equal(a.token, b.token)
+    assert int(a.position.item()) == int(b.position.item()) == 162
+    for l in range(TINY.num_hidden_layers):
+        assert torch.equal(a.k_cache[l], b.k_cache[l]) and torch.equal(a.v_cache[l], b.v_cache[l])
+    for name in ("popkv_layer_tail_timeouts", "popkv_gemv_timeouts"):
+        count = ctypes.c_uint32(99)
+        _lib.check(getattr(_lib.lib(), name)(ctypes.byref(count)))
+        assert count.value == 0, name
