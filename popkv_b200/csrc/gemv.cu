@@ -306,6 +306,21 @@ constexpr int kPieceBytes = kPieceElems * 2;
 // flight (~190 KB) is what keeps the stream near peak, so one CTA per SM.
 constexpr int kSmemBudget = 227 * 1024;
 
+// Walks a warp's pieces in order without divisions: the warp's unit t, row r
+// of the unit, piece p of the row.
+struct PieceCursor {
+    int t = 0, r = 0, p = 0;
+    __device__ __forceinline__ void next(int rows, int npieces) {
+        if (++p == npieces) {
+            p = 0;
+            if (++r == rows) {
+                r = 0;
+                ++t;
+            }
+        }
+    }
+};
+
 template <int MB, int PRO, int EPI, int S>
 __global__ void __launch_bounds__(kTmaThreads, 1) gemv_kernel(const GemvArgs a) {
     constexpr int R = (EPI == kSwiglu || EPI == kRope) ? 2 : 1;  // rows per unit
@@ -323,26 +338,25 @@ __global__ void __launch_bounds__(kTmaThreads, 1) gemv_kernel(const GemvArgs a) 
     const int64_t k = a.k;
     const int npieces = (a.k + kPieceElems - 1) / kPieceElems;
     const int ppu = R * npieces;
-    const int64_t my_units =
-        (gw < a.active_warps && gw < a.units) ? (a.units - 1 - gw) / a.active_warps + 1 : 0;
-    const int64_t total = my_units * ppu;
+    const int my_units =
+        (gw < a.active_warps && gw < a.units) ? static_cast<int>((a.units - 1 - gw) / a.active_warps + 1) : 0;
+    const int total = my_units * ppu;
     uint4* my_ring = ring + static_cast<int64_t>(warp) * S * (kPieceBytes / 16);
 
-    // Piece j of this warp: unit gw + (j / ppu) * active_warps, row (j % ppu) / npieces,
-    // elements [p * kPieceElems, ...) of that row.
-    auto issue = [&](int64_t j) {
-        const int64_t t = j / ppu;
-        const int rem = static_cast<int>(j % ppu);
-        const int r = rem / npieces, p = rem % npieces;
+    // Piece j of this warp (issued in order, lane 0): unit gw + t * active_warps,
+    // row r of the unit, elements [p * kPieceElems, ...) of that row.
+    PieceCursor produced;
+    auto issue = [&](int j) {
         int64_t r0, r1;
-        unit_rows<EPI>(a, gw + t * a.active_warps, r0, r1);
-        const int64_t row = r == 0 ? r0 : r1;
-        const int64_t off = static_cast<int64_t>(p) * kPieceElems;
+        unit_rows<EPI>(a, gw + static_cast<int64_t>(produced.t) * a.active_warps, r0, r1);
+        const int64_t row = produced.r == 0 ? r0 : r1;
+        const int64_t off = static_cast<int64_t>(produced.p) * kPieceElems;
         const int64_t elems = k - off < kPieceElems ? k - off : kPieceElems;
-        const int st = static_cast<int>(j % S);
+        const int st = j % S;
         mbar_arrive_expect_tx(&bars[warp][st], static_cast<uint32_t>(elems * 2));
         bulk_copy_g2s(my_ring + st * (kPieceBytes / 16), a.w + row * k + off, static_cast<uint32_t>(elems * 2),
                       &bars[warp][st]);
+        produced.next(R, npieces);
     };
 
     // The weights do not depend on the previous kernel: fill the ring first.
@@ -350,7 +364,7 @@ __global__ void __launch_bounds__(kTmaThreads, 1) gemv_kernel(const GemvArgs a) 
 #pragma unroll
         for (int st = 0; st < S; ++st) mbar_init(&bars[warp][st], 1);
         fence_async_smem();
-        for (int64_t j = 0; j < S && j < total; ++j) issue(j);
+        for (int j = 0; j < S && j < total; ++j) issue(j);
     }
     if constexpr (EPI == kArgmax) {
         if (tid < kMaxBatch) cta_key[tid] = 0ull;
@@ -374,16 +388,19 @@ __global__ void __launch_bounds__(kTmaThreads, 1) gemv_kernel(const GemvArgs a) 
 #pragma unroll
         for (int m = 0; m < MB; ++m) acc0[r][m] = acc1[r][m] = 0.0f;
     bool failed = false;
-    int64_t j = 0;
+    int j = 0;
+    PieceCursor cur;
     for (; j < total; ++j) {
-        const int st = static_cast<int>(j % S);
+        const int st = j % S;
         const bool ok = __all_sync(0xFFFFFFFFu, mbar_wait(&bars[warp][st], static_cast<uint32_t>((j / S) & 1)));
         if (!ok) {
             failed = true;
             break;
         }
-        const int rem = static_cast<int>(j % ppu);
-        const int r = rem / npieces, p = rem % npieces;
+        const int r = cur.r, p = cur.p;
+        const bool unit_end = r == R - 1 && p == npieces - 1;
+        const int64_t u = gw + static_cast<int64_t>(cur.t) * a.active_warps;
+        cur.next(R, npieces);
         const int pch = (a.k - p * kPieceElems < kPieceElems ? a.k - p * kPieceElems : kPieceElems) / 8;
         const uint4* wp = my_ring + st * (kPieceBytes / 16);
         const uint4* xp = xs + p * (kPieceElems / 8);
@@ -407,8 +424,7 @@ __global__ void __launch_bounds__(kTmaThreads, 1) gemv_kernel(const GemvArgs a) 
             fence_async_smem();  // this slot's reads come before the copy that overwrites it
             issue(j + S);
         }
-        if (rem == ppu - 1) {
-            const int64_t u = gw + (j / ppu) * a.active_warps;
+        if (unit_end) {
             int64_t r0, r1;
             unit_rows<EPI>(a, u, r0, r1);
             float y[R][MB];
@@ -426,7 +442,7 @@ __global__ void __launch_bounds__(kTmaThreads, 1) gemv_kernel(const GemvArgs a) 
         // Record the stall and wait (bounded) for this warp's copies still in flight.
         if (lane == 0) {
             atomicAdd(&g_gemv_timeouts, 1u);
-            for (int64_t jj = j; jj < total && jj < j + S; ++jj)
+            for (int jj = j; jj < total && jj < j + S; ++jj)
                 mbar_wait(&bars[warp][jj % S], static_cast<uint32_t>((jj / S) & 1));
         }
         __syncwarp();
@@ -450,32 +466,47 @@ constexpr int kGridPolls = 1 << 22;
 
 struct TailArgs {
     GemvArgs ph[kTailPhases];
-    unsigned int* barrier;  // [2]: arrivals, generation; zero at setup, self-resetting
+    unsigned long long* barrier;  // ticket counter, zero at setup
 };
 
 __device__ unsigned int g_tail_timeouts = 0;
 
-// Grid-wide barrier of co-resident CTAs; false if the bounded wait gave up.
-__device__ __forceinline__ bool grid_barrier(unsigned int* bar) {
+#ifdef POPKV_TAIL_TIMING
+// Phase timestamps (globaltimer ns) of thread 0 of each CTA: start, after the
+// dependency wait, then per phase: compute start, CTA done, barrier released.
+constexpr int kTailStamps = 14;
+__device__ unsigned long long g_tail_stamp_ns[160 * kTailStamps];
+#define POPKV_TAIL_STAMP(i)                                                           \
+    do {                                                                              \
+        if (threadIdx.x == 0 && blockIdx.x < 160) {                                  \
+            unsigned long long t_;                                                   \
+            asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_));                   \
+            g_tail_stamp_ns[blockIdx.x * kTailStamps + (i)] = t_;                    \
+        }                                                                             \
+    } while (0)
+#else
+#define POPKV_TAIL_STAMP(i) \
+    do {                    \
+    } while (0)
+#endif
+
+// Grid-wide barrier of co-resident CTAs on a monotonic ticket counter (never
+// reset, so consecutive launches of the same grid size share it): arrival n
+// waits until the count reaches the next multiple of the grid size.  False if
+// the bounded wait gave up.
+__device__ __forceinline__ bool grid_barrier(unsigned long long* count) {
     __shared__ int s_ok;
     __syncthreads();
     if (threadIdx.x == 0) {
-        volatile unsigned int* vb = bar;
-        const unsigned int gen = vb[1];
         __threadfence();
-        int ok = 1;
-        if (atomicAdd(bar, 1u) == gridDim.x - 1) {
-            atomicExch(bar, 0u);
-            __threadfence();
-            atomicAdd(bar + 1, 1u);
-        } else {
-            ok = 0;
-            for (int i = 0; i < kGridPolls; ++i) {
-                if (vb[1] != gen) {
-                    ok = 1;
-                    break;
-                }
-                __nanosleep(64);
+        const unsigned long long ticket = atomicAdd(count, 1ull);
+        const unsigned long long target = (ticket / gridDim.x + 1) * gridDim.x;
+        volatile unsigned long long* vc = count;
+        int ok = 0;
+        for (int i = 0; i < kGridPolls; ++i) {
+            if (*vc >= target) {
+                ok = 1;
+                break;
             }
         }
         __threadfence();
@@ -512,75 +543,88 @@ __global__ void __launch_bounds__(kTmaThreads, 1) layer_tail_kernel(const TailAr
     const int64_t gw = static_cast<int64_t>(blockIdx.x) * kTmaWarps + warp;
     uint4* my_ring = ring + static_cast<int64_t>(warp) * S * (kPieceBytes / 16);
 
-    // This warp's pieces, phase by phase.
-    int64_t cum[kTailPhases + 1];
-    int npieces[kTailPhases], ppu[kTailPhases];
-    cum[0] = 0;
+    // This warp's units per phase; pieces walk the phases in order.
+    int units[kTailPhases], rows[kTailPhases], npieces[kTailPhases];
+    int total = 0;
 #pragma unroll
     for (int p = 0; p < kTailPhases; ++p) {
         const GemvArgs& a = t.ph[p];
         npieces[p] = (a.k + kPieceElems - 1) / kPieceElems;
-        ppu[p] = tail_rows_per_unit<LAST>(p) * npieces[p];
-        const int64_t mine = (gw < a.active_warps && gw < a.units) ? (a.units - 1 - gw) / a.active_warps + 1 : 0;
-        cum[p + 1] = cum[p] + mine * ppu[p];
+        rows[p] = tail_rows_per_unit<LAST>(p);
+        units[p] = (gw < a.active_warps && gw < a.units) ? static_cast<int>((a.units - 1 - gw) / a.active_warps + 1) : 0;
+        total += units[p] * rows[p] * npieces[p];
     }
-    const int64_t total = cum[kTailPhases];
 
-    auto issue = [&](int64_t j) {
-        int p = 0;
-        while (p < kTailPhases - 1 && j >= cum[p + 1]) ++p;
+    int prod_phase = 0;
+    PieceCursor produced;
+    auto issue = [&](int j) {
+        while (produced.t == units[prod_phase]) {  // next phase with work for this warp
+            ++prod_phase;
+            produced = PieceCursor{};
+        }
+        const int p = prod_phase;
         const GemvArgs& a = t.ph[p];
-        const int64_t local = j - cum[p];
-        const int rem = static_cast<int>(local % ppu[p]);
-        const int r = rem / npieces[p], pc = rem % npieces[p];
         int64_t r0, r1;
-        tail_rows<LAST>(p, a, gw + (local / ppu[p]) * a.active_warps, r0, r1);
+        tail_rows<LAST>(p, a, gw + static_cast<int64_t>(produced.t) * a.active_warps, r0, r1);
         const int64_t k = a.k;
-        const int64_t row = r == 0 ? r0 : r1;
-        const int64_t off = static_cast<int64_t>(pc) * kPieceElems;
+        const int64_t row = produced.r == 0 ? r0 : r1;
+        const int64_t off = static_cast<int64_t>(produced.p) * kPieceElems;
         const int64_t elems = k - off < kPieceElems ? k - off : kPieceElems;
-        const int st = static_cast<int>(j % S);
+        const int st = j % S;
         mbar_arrive_expect_tx(&bars[warp][st], static_cast<uint32_t>(elems * 2));
         bulk_copy_g2s(my_ring + st * (kPieceBytes / 16), a.w + row * k + off, static_cast<uint32_t>(elems * 2),
                       &bars[warp][st]);
+        produced.next(rows[p], npieces[p]);
     };
 
     if (lane == 0) {
 #pragma unroll
         for (int st = 0; st < S; ++st) mbar_init(&bars[warp][st], 1);
         fence_async_smem();
-        for (int64_t j = 0; j < S && j < total; ++j) issue(j);
+        for (int jj = 0; jj < S && jj < total; ++jj) issue(jj);
     }
     if (tid < kMaxBatch) cta_key[tid] = 0ull;
+    POPKV_TAIL_STAMP(0);
     __syncwarp();
     pdl_wait();
     pdl_launch_dependents();
+    POPKV_TAIL_STAMP(1);
 
     bool failed = false;
-    int64_t j = 0, j_fail = 0;
+    int j = 0, j_fail = 0;
     for (int p = 0; p < kTailPhases; ++p) {
         const GemvArgs& a = t.ph[p];
-        if (p > 0 && !grid_barrier(t.barrier) && tid == 0) atomicAdd(&g_tail_timeouts, 1u);
+        if (p > 0) {
+            __syncthreads();
+            POPKV_TAIL_STAMP(3 * p);  // every warp of the CTA is done with phase p - 1
+            if (!grid_barrier(t.barrier) && tid == 0) atomicAdd(&g_tail_timeouts, 1u);
+            POPKV_TAIL_STAMP(3 * p + 1);
+        }
         if (p == 1 || p == 3) load_x_norm<1, kTmaThreads, kTmaWarps>(a, xs, red);
         else load_x_plain<1, kTmaThreads>(a, xs);
+        POPKV_TAIL_STAMP(3 * p + 2);
         int64_t pos = 0;
         if (p == 3 && LAST == kRope) {
             pos = *a.position;
             pos = pos < 0 ? 0 : (pos > a.max_position ? a.max_position : pos);
         }
+        const int R = rows[p], np = npieces[p];
+        const int count = units[p] * R * np;
         float acc0[2] = {0.0f, 0.0f}, acc1[2] = {0.0f, 0.0f};
-        for (; j < cum[p + 1]; ++j) {
+        PieceCursor cur;
+        for (int q = 0; q < count; ++q, ++j) {
             if (failed) continue;
-            const int st = static_cast<int>(j % S);
+            const int st = j % S;
             if (!__all_sync(0xFFFFFFFFu, mbar_wait(&bars[warp][st], static_cast<uint32_t>((j / S) & 1)))) {
                 failed = true;
                 j_fail = j;
                 if (lane == 0) atomicAdd(&g_tail_timeouts, 1u);
                 continue;
             }
-            const int64_t local = j - cum[p];
-            const int rem = static_cast<int>(local % ppu[p]);
-            const int r = rem / npieces[p], pc = rem % npieces[p];
+            const int r = cur.r, pc = cur.p;
+            const bool unit_end = r == R - 1 && pc == np - 1;
+            const int64_t u = gw + static_cast<int64_t>(cur.t) * a.active_warps;
+            cur.next(R, np);
             const int pch = (a.k - pc * kPieceElems < kPieceElems ? a.k - pc * kPieceElems : kPieceElems) / 8;
             const uint4* wp = my_ring + st * (kPieceBytes / 16);
             const uint4* xp = xs + pc * (kPieceElems / 8);
@@ -596,8 +640,7 @@ __global__ void __launch_bounds__(kTmaThreads, 1) layer_tail_kernel(const TailAr
                 fence_async_smem();
                 issue(j + S);
             }
-            if (rem == ppu[p] - 1) {
-                const int64_t u = gw + (local / ppu[p]) * a.active_warps;
+            if (unit_end) {
                 int64_t r0, r1;
                 tail_rows<LAST>(p, a, u, r0, r1);
                 float y[2][1];
@@ -606,8 +649,7 @@ __global__ void __launch_bounds__(kTmaThreads, 1) layer_tail_kernel(const TailAr
                 acc0[0] = acc0[1] = acc1[0] = acc1[1] = 0.0f;
                 if (lane == 0) {
                     if (p == 1) {
-                        const float (&yy)[2][1] = y;
-                        unit_epilogue<1, kSwiglu, 2>(a, u, r0, yy, pos, cta_key);
+                        unit_epilogue<1, kSwiglu, 2>(a, u, r0, y, pos, cta_key);
                     } else if (p == 3) {
                         if constexpr (LAST == kRope) {
                             unit_epilogue<1, kRope, 2>(a, u, r0, y, pos, cta_key);
@@ -623,8 +665,10 @@ __global__ void __launch_bounds__(kTmaThreads, 1) layer_tail_kernel(const TailAr
             }
         }
     }
+    __syncthreads();
+    POPKV_TAIL_STAMP(12);
     if (failed && lane == 0) {  // the copies still in flight land before the CTA exits
-        for (int64_t jj = j_fail; jj < total && jj < j_fail + S; ++jj)
+        for (int jj = j_fail; jj < total && jj < j_fail + S; ++jj)
             mbar_wait(&bars[warp][jj % S], static_cast<uint32_t>((jj / S) & 1));
     }
     __syncwarp();
@@ -875,8 +919,9 @@ extern "C" int popkv_layer_tail(int64_t hidden_size, int64_t inter, int64_t attn
         return fail(POPKV_ERR_INVALID, "%s: null or unaligned buffer", name);
     st = check_norm(hidden_mid, o_out, nullptr, nullptr, post_norm, hidden, name);
     if (st != POPKV_OK) return st;
+    if (!aligned(barrier, 8)) return fail(POPKV_ERR_INVALID, "%s: barrier must be 8-byte aligned", name);
     TailArgs t{};
-    t.barrier = barrier;
+    t.barrier = reinterpret_cast<unsigned long long*>(barrier);
     GemvArgs& o = t.ph[0];
     o.w = static_cast<const __nv_bfloat16*>(o_w);
     o.units = H;
@@ -949,3 +994,10 @@ extern "C" int popkv_layer_tail_timeouts(uint32_t* count) {
     if (err != cudaSuccess) return fail(POPKV_ERR_CUDA, "popkv_layer_tail_timeouts: %s", cudaGetErrorString(err));
     return POPKV_OK;
 }
+
+#ifdef POPKV_TAIL_TIMING
+extern "C" __attribute__((visibility("default"))) int popkv_tail_stamps(unsigned long long* host, int ctas) {
+    return static_cast<int>(cudaMemcpyFromSymbol(host, popkv::g_tail_stamp_ns,
+                                                  sizeof(unsigned long long) * popkv::kTailStamps * ctas));
+}
+#endif
