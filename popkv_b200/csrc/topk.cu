@@ -1021,6 +1021,13 @@ int try_launch_cluster16(const void* scores, int64_t rows, int64_t tokens, int64
     int per = 8;
     while (per < (cpr == 8 ? 64 : 32) && tokens > static_cast<int64_t>(cpr) * kClusterThreads * per) per *= 2;
     if (tokens > static_cast<int64_t>(cpr) * kClusterThreads * per) return -1;
+    // A row just past 4 x 512 x 16 keys (e.g. 33K tokens) would take 32 keys per
+    // thread in 4 CTAs and leave the last CTA of each cluster idle: 6 CTAs at 16
+    // keys per thread halve the per-thread work instead.
+    if (cpr == 4 && per == 32 && tokens <= static_cast<int64_t>(6) * kClusterThreads * 16) {
+        cpr = 6;
+        per = 16;
+    }
 #define POPKV_C16(CPR_, PER_)                                                                      \
     if (cpr == CPR_ && per == PER_)                                                                \
         return launch_cluster16<CPR_, PER_>(scores, rows, tokens, row_stride, k, current_index, out, \
@@ -1029,6 +1036,7 @@ int try_launch_cluster16(const void* scores, int64_t rows, int64_t tokens, int64
     POPKV_C16_CPR(1)
     POPKV_C16_CPR(2)
     POPKV_C16_CPR(4)
+    POPKV_C16(6, 16)
     POPKV_C16_CPR(8)
     POPKV_C16(8, 64)
 #undef POPKV_C16_CPR

@@ -240,7 +240,7 @@ def _tie_heavy_scores(gen, rows, tokens, levels=None):
     return x
 
 
-@pytest.mark.parametrize("tokens", (1, 2, 100, 1000, 4096, 32768, 49152, 65536, 131072))
+@pytest.mark.parametrize("tokens", (1, 2, 100, 1000, 4096, 32768, 33024, 49152, 65536, 131072))
 @pytest.mark.parametrize("dtype", (torch.float16, torch.float32))
 def test_topk_matches_oracle(cuda_device, tokens, dtype):
     gen = torch.Generator().manual_seed(tokens)
@@ -255,7 +255,8 @@ def test_topk_matches_oracle(cuda_device, tokens, dtype):
         assert torch.all(got[:, k] == tokens)
 
 
-@pytest.mark.parametrize("rows,tokens", [(1, 131072), (3, 65536), (32, 32768), (64, 8191), (200, 777)])
+@pytest.mark.parametrize("rows,tokens", [(1, 131072), (3, 65536), (32, 32768), (32, 33024), (64, 8191),
+                                         (200, 777)])
 def test_topk_all_equal_and_row_counts(cuda_device, rows, tokens):
     """Every key equal (all winners are ties, taken in index order) and many cluster shapes."""
     gen = torch.Generator().manual_seed(rows)
