@@ -81,6 +81,8 @@ def parse_args(argv=None):
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU baseline sample budget")
     p.add_argument("--stage-reps", type=int, default=50)
+    p.add_argument("--no-model", action="store_true",
+                   help="skip the full-model decode measurement that a 1-GPU default run adds")
     p.add_argument("--model", action="store_true",
                    help="full 32-layer Llama-3.1-8B-shaped greedy decode (config 2) instead of one layer")
     p.add_argument("--model-method", choices=("popkv-s", "popkv-q", "popkv-normal", "full"), default="popkv-s")
@@ -441,6 +443,14 @@ def run_ours(args, world, rank, local):
         }
         if not args.no_cpu_baseline and world == 1:
             result["cpu_baseline"] = cpu_baseline(args, layer, max_seconds=args.cpu_seconds)
+    if world == 1 and not args.no_model:
+        # The metric's second half: full-model decode ms/token (config 2), one GPU.
+        model_args = argparse.Namespace(**{**vars(args), "context": 32768, "budget": 4096, "batch": 1,
+                                           "prefill": "model"})
+        model = measure_model(model_args, 1, 0, device, None, warmup=3)
+        result["full_model"] = {k: model[k] for k in ("metric", "value", "unit", "vs_baseline", "data", "config",
+                                                     "roofline", "e2e", "gpu_launches", "clocks")}
+    if rank == 0:
         print(json.dumps(result), flush=True)
     for st in steps:
         st.graph = None
@@ -805,6 +815,17 @@ def run_model(args, world, rank, local):
     import torch
     dist = init_dist(world, local)
     device = torch.device("cuda", local)
+    result = measure_model(args, world, rank, device, dist)
+    if rank == 0:
+        print(json.dumps(result), flush=True)
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def measure_model(args, world, rank, device, dist, warmup=None):
+    """Time the full-model greedy decode (config 2 by default); the JSON object on rank 0, None elsewhere."""
+    import torch
     from popkv_b200 import _lib
     from popkv_b200.decoder import LLAMA31_8B, LlamaSparseDecoder, LlamaWeights
     from popkv_b200.popkv import POPKV_PRESETS, RetrievalConfig
@@ -814,7 +835,7 @@ def run_model(args, world, rank, local):
     tg, g = POPKV_PRESETS.get(method, (32, 32))
     retrieval = RetrievalConfig(budget=args.budget, group_size=tg, dim_group_size=g)
     weights = LlamaWeights.random(cfg, device=device, seed=0)
-    T, W, K = args.context, args.warmup, args.gen_steps
+    T, W, K = args.context, (args.warmup if warmup is None else warmup), args.gen_steps
     dec = LlamaSparseDecoder(weights, method=method, retrieval=retrieval, batch=args.batch,
                              max_context=T + W + 2 * K + 2, rank=rank, world=world,
                              group=None)
@@ -834,7 +855,7 @@ def run_model(args, world, rank, local):
         dist.barrier()
     torch.cuda.synchronize(device)
     position0 = int(dec.position.item())
-    sampler = ClockSampler(physical_gpu_index(local)).start()
+    sampler = ClockSampler(physical_gpu_index(device.index or 0)).start()
     time.sleep(0.25)
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     t0 = time.time()
@@ -920,11 +941,12 @@ def run_model(args, world, rank, local):
             "gpu_launches": ours_per_step * K,
             "clocks": sampler.summary(t0, t1),
         }
-        print(json.dumps(result), flush=True)
+    else:
+        result = None
     dec.close()
-    if dist is not None:
-        dist.barrier()
-        dist.destroy_process_group()
+    del dec, weights
+    torch.cuda.empty_cache()
+    return result
 
 
 # ---------------------------------------------------------------------------
