@@ -80,3 +80,24 @@ def test_weights_from_module_fuse_projections():
     # Bytes a batch-1 decode step streams: every matrix but the embedding.
     per_layer = (512 * 256 + 256 * 256 + 2 * 512 * 256 + 256 * 512 + 2 * 256) * 2
     assert w.bytes_per_token() == per_layer + (64 * 256 + 256) * 2
+
+
+def test_kv_head_shard_takes_its_heads_qkv_rows():
+    """A world-N decoder keeps rank r's query heads and KV heads of the fused q|k|v projection."""
+    from popkv_b200.decoder import LlamaSparseDecoder
+    cfg = LlamaConfig(hidden_size=1024, num_attention_heads=8, num_key_value_heads=4, intermediate_size=512,
+                      vocab_size=64, num_hidden_layers=1)
+    w = LlamaWeights.random(cfg, device="cpu", seed=3)
+    full = w.layers[0].qkv.view(8 + 2 * 4, 128, 1024)
+    world = 2
+    for rank in range(world):
+        dec = LlamaSparseDecoder(w, method="full", max_context=16, rank=rank, world=world, use_graph=False)
+        assert dec.qh == 4 and dec.kvh == 2
+        local = dec.qkv_weights[0].view(4 + 2 * 2, 128, 1024)
+        q_heads = range(4 * rank, 4 * rank + 4)
+        kv_heads = range(2 * rank, 2 * rank + 2)
+        want = torch.cat([full[list(q_heads)], full[[8 + h for h in kv_heads]], full[[12 + h for h in kv_heads]]])
+        assert torch.equal(local, want)
+        assert tuple(dec.k_cache[0].shape) == (1, 2, 16, 128)
+    with pytest.raises(ValueError, match="divide"):
+        LlamaSparseDecoder(w, method="full", max_context=16, rank=0, world=3, use_graph=False)
