@@ -81,6 +81,9 @@ def parse_args(argv=None):
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU baseline sample budget")
     p.add_argument("--stage-reps", type=int, default=50)
+    p.add_argument("--mlp-parallel", choices=("replicated", "tensor"), default="replicated",
+                   help="--model on several GPUs: replicated o_proj/MLP (one all-gather per layer) or "
+                        "tensor-parallel (two all-reduces per layer)")
     p.add_argument("--no-model", action="store_true",
                    help="skip the full-model decode measurement that a 1-GPU default run adds")
     p.add_argument("--model", action="store_true",
@@ -799,10 +802,7 @@ def model_bytes_per_step(dec, weights, position: int) -> dict:
     B, kvh, qh = dec.batch, dec.kvh, dec.qh
     L = dec.cfg.num_hidden_layers
     dense = L - len(dec.sparse_layers)
-    w = weights.bytes_per_token()
-    if dec.world > 1:  # this rank streams only its heads' q/k/v rows
-        per_layer_qkv = weights.layers[0].qkv.numel() * 2
-        w -= L * (per_layer_qkv - dec.qkv_weights[0].numel() * 2)
+    w = dec.weight_bytes_per_step()  # this rank's q/k/v rows (and MLP slice in tensor mode)
     kv_dense = dense * B * kvh * (position + 1) * 128 * 2 * 2
     reps = 128 // dec.g
     meta = len(dec.sparse_layers) * B * kvh * position * (32 + 4 * reps)
@@ -838,7 +838,7 @@ def measure_model(args, world, rank, device, dist, warmup=None):
     T, W, K = args.context, (args.warmup if warmup is None else warmup), args.gen_steps
     dec = LlamaSparseDecoder(weights, method=method, retrieval=retrieval, batch=args.batch,
                              max_context=T + W + 2 * K + 2, rank=rank, world=world,
-                             group=None)
+                             group=None, mlp_parallel=args.mlp_parallel)
     gen = torch.Generator().manual_seed(0)
     ids = torch.randint(0, cfg.vocab_size, (args.batch, T), generator=gen)
     torch.cuda.synchronize(device)
@@ -923,8 +923,10 @@ def measure_model(args, world, rank, device, dist, warmup=None):
                 "method": method, "batch": args.batch, "prefix": T, "budget": args.budget,
                 "prefill": args.prefill,
                 "context_at_timed_steps": [position0, position0 + K - 1],
-                "parallelism": f"kv-head shard x{world}" + ("" if world == 1 else
-                                                            " + NCCL all-gather per layer, replicated MLP"),
+                "parallelism": f"kv-head shard x{world}" + (
+                    "" if world == 1 else " + NCCL all-gather per layer, replicated MLP"
+                    if args.mlp_parallel == "replicated" else
+                    " + tensor-parallel o_proj/MLP, two NCCL all-reduces per layer"),
                 "l2": "each step streams ~16 GB of weights > L2",
                 "launch": "one CUDA graph per token (device-resident position), replayed",
             },

@@ -210,12 +210,19 @@ class LlamaSparseDecoder:
             GPU): this rank owns KV heads [rank*KVH/world, (rank+1)*KVH/world) and
             their query heads; the attention outputs are all-gathered (NCCL) per
             layer into the replicated output projection and MLP.
+        mlp_parallel: "replicated" (the plan above: every rank streams the whole
+            output projection and MLP) or "tensor" (batch <= 4, several ranks):
+            o_proj and down_proj keep this rank's input columns (its heads, its
+            1/world of the intermediate dims), gate/up its intermediate rows;
+            the two partial outputs are summed with an NCCL all-reduce each
+            layer instead of all-gathering the attention rows.  Each rank then
+            streams 1/world of those weights.  The LM head stays replicated.
     """
 
     def __init__(self, weights: LlamaWeights, *, method: str = "popkv-s",
                  retrieval: RetrievalConfig | None = None, batch: int = 1, max_context: int,
                  split_tokens: int = 256, rank: int = 0, world: int = 1, group=None,
-                 use_graph: bool = True) -> None:
+                 use_graph: bool = True, mlp_parallel: str = "replicated") -> None:
         if method not in DECODE_METHODS:
             raise ValueError(f"method must be one of {DECODE_METHODS}")
         cfg = weights.config
@@ -228,6 +235,11 @@ class LlamaSparseDecoder:
             raise ValueError("the in-graph append re-encodes token groups of at most 128")
         if cfg.num_key_value_heads % world:
             raise ValueError("KV heads must divide evenly over the ranks")
+        if mlp_parallel not in ("replicated", "tensor"):
+            raise ValueError("mlp_parallel must be 'replicated' or 'tensor'")
+        self.tensor_mlp = mlp_parallel == "tensor" and world > 1
+        if self.tensor_mlp and (batch > 4 or cfg.intermediate_size % (8 * world)):
+            raise ValueError("mlp_parallel='tensor' needs batch <= 4 and intermediate dims divisible by 8 * world")
         self.w, self.cfg, self.method, self.retrieval = weights, cfg, method, retrieval
         self.device = weights.embed.device
         self.batch, self.max_context = int(batch), int(max_context)
@@ -274,12 +286,26 @@ class LlamaSparseDecoder:
         self._gathered = None if world == 1 else torch.zeros((world, B, self.qh, D), device=dev, dtype=bf)
         self.o = torch.zeros((B, H), device=dev, dtype=bf)
         self.gate_up = torch.zeros((B, 2 * I), device=dev, dtype=bf)
-        self.act = torch.zeros((B, I), device=dev, dtype=bf)
+        self.inter_local = I // world if self.tensor_mlp else I
+        self.act = torch.zeros((B, self.inter_local), device=dev, dtype=bf)
         self.down = torch.zeros((B, H), device=dev, dtype=bf)
         self.logits = torch.zeros((B, cfg.vocab_size), device=dev, dtype=bf)
         self.logits_f32 = torch.zeros((B, cfg.vocab_size), device=dev, dtype=torch.float32)
         # This rank's q | k | v rows of every layer's fused projection.
         self.qkv_weights = [self._local_qkv(lw.qkv) for lw in weights.layers]
+        # This rank's output-projection columns and MLP slice (tensor mode), else the whole matrices.
+        self.o_weights, self.gate_up_weights, self.down_weights = [], [], []
+        for lw in weights.layers:
+            if self.tensor_mlp:
+                r, il = rank, self.inter_local
+                self.o_weights.append(lw.o[:, r * self.qh * D:(r + 1) * self.qh * D].contiguous())
+                self.gate_up_weights.append(torch.cat([lw.gate_up[r * il:(r + 1) * il],
+                                                       lw.gate_up[I + r * il:I + (r + 1) * il]]).contiguous())
+                self.down_weights.append(lw.down[:, r * il:(r + 1) * il].contiguous())
+            else:
+                self.o_weights.append(lw.o)
+                self.gate_up_weights.append(lw.gate_up)
+                self.down_weights.append(lw.down)
         # KV caches [B, KVH_local, cap, D] and the sparse layers' packed planes
         # [B * KVH_local, meta_capacity, ...] (batch entries flattened into heads).
         self.k_cache = [torch.zeros((B, self.kvh, cap, D), device=dev, dtype=bf) for _ in range(L)]
@@ -344,7 +370,7 @@ class LlamaSparseDecoder:
         kc, vc = self.k_cache[layer], self.v_cache[layer]
         # Batch entries are flattened into heads: one sequence = KVH_local heads.
         ks, vs = kc.stride(1), vc.stride(1)
-        out = self.attn if self.world == 1 else None
+        out = self.attn if (self.world == 1 or self.tensor_mlp) else None
         if layer in self.packed:
             sign, mag, low, delta = self.packed[layer]
             check(lib.popkv_score_dyn(
@@ -368,9 +394,24 @@ class LlamaSparseDecoder:
             self.max_tokens, 0, ks, kc.stride(2), 0, vs, vc.stride(2), ptr(self.k_cur),
             ptr(self.v_cur), ptr(self.position), indices, index_stride, self.k_max,
             ptr(self.head_to_kv), self.split_tokens, ptr(self.partials), ptr(out), _lib.BF16, s))
-        if self.world > 1:
+        if self.world > 1 and not self.tensor_mlp:
             selected = self.k_max + 1 if layer in self.packed else self.max_tokens + 1
             self._gather(s, math.ceil(selected / self.split_tokens))
+
+    def _sum_partials(self, t: torch.Tensor, stream) -> None:
+        """Tensor mode: sum the ranks' partial products (NCCL all-reduce, inside the graph)."""
+        if self.tensor_mlp:
+            import torch.distributed as dist
+            with torch.cuda.stream(stream):
+                dist.all_reduce(t, group=self.group)
+
+    def weight_bytes_per_step(self) -> int:
+        """Weight bytes this rank streams per decode step (batch <= 4; norms included)."""
+        total = self.w.lm_head.numel() * 2 + self.w.norm.numel() * 2
+        for l, lw in enumerate(self.w.layers):
+            total += (self.qkv_weights[l].numel() + self.o_weights[l].numel() + self.gate_up_weights[l].numel()
+                      + self.down_weights[l].numel() + lw.input_norm.numel() + lw.post_norm.numel()) * 2
+        return int(total)
 
     def _gather(self, s, splits: int) -> None:
         """Merge, then all-gather the shards' attention rows [B, QH/N, D] into [B, QH, D]."""
@@ -425,7 +466,7 @@ class LlamaSparseDecoder:
                     kc.stride(0), kc.stride(1), kc.stride(2), vc.stride(0), vc.stride(1), vc.stride(2), s))
             with torch.cuda.stream(stream):
                 self._attention(l, s, after_score=lambda layer: fork(lambda ss: self._append(layer, ss)))
-            if self.tail:
+            if self.tail and not self.tensor_mlp:
                 # o_proj, gate/up + SwiGLU, down and the next layer's q/k/v (or the LM
                 # head) in one persistent launch.  The side branch (the appends)
                 # rejoins before the LM head advances the position.
@@ -444,11 +485,16 @@ class LlamaSparseDecoder:
                     ptr(self.w.norm), ptr(self.logits), ptr(self.argmax_state), ptr(self.token),
                     ptr(self.tail_barrier), s))
                 continue
-            check(lib.popkv_linear(ptr(lw.o), H, QH * D, ptr(self.attn_full), B, ptr(self.o), H, s))
-            check(lib.popkv_norm_gate_up_swiglu(ptr(lw.gate_up), I, H, B, ptr(self.hidden_b), ptr(self.o),
-                                                ptr(lw.post_norm), eps, ptr(self.hidden), ptr(self.act), s))
-            check(lib.popkv_linear(ptr(lw.down), H, I, ptr(self.act), B, ptr(self.down), H, s))
-        if self.tail:
+            o_in, o_k, il = ((self.attn, self.qh * D, self.inter_local) if self.tensor_mlp
+                             else (self.attn_full, QH * D, I))
+            check(lib.popkv_linear(ptr(self.o_weights[l]), H, o_k, ptr(o_in), B, ptr(self.o), H, s))
+            self._sum_partials(self.o, stream)
+            check(lib.popkv_norm_gate_up_swiglu(ptr(self.gate_up_weights[l]), il, H, B, ptr(self.hidden_b),
+                                                ptr(self.o), ptr(lw.post_norm), eps, ptr(self.hidden),
+                                                ptr(self.act), s))
+            check(lib.popkv_linear(ptr(self.down_weights[l]), H, il, ptr(self.act), B, ptr(self.down), H, s))
+            self._sum_partials(self.down, stream)
+        if self.tail and not self.tensor_mlp:
             return
         # The side branch (the appends) rejoins before the position advances.
         if forked:
