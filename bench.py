@@ -41,8 +41,10 @@ if str(ROOT) not in sys.path:
 
 METRIC = "decode ms/token (score+top-k+sparse attn), one layer"
 UNIT = "ms"
-# PopKV-Q at 32K, budget 4096, per token over 30 sparse layers:
-# score 1.365 + top-k 1.814 + partial 3.600 + merge 0.143 = 6.922 ms -> per layer.
+# The reference's published PG19 decode breakdown (PopKV-Q at 32K, budget
+# 4096, per token over its 30 sparse layers; score_comparison.csv and
+# report.md of its five-methods run): score 1.365 + top-k 1.814 + partial
+# 3.600 + merge 0.143 = 6.922 ms -> per layer.
 PUBLISHED_MS_PER_LAYER = (1.365 + 1.814 + 3.600 + 0.143) / 30.0
 
 # DRAM traffic per launch (dram__bytes_read.sum + dram__bytes_write.sum) of the
@@ -787,8 +789,8 @@ def run_reference(args, world, rank):
 # ---------------------------------------------------------------------------
 
 MODEL_METRIC = "full-model decode ms/token (32-layer Llama-3.1-8B shape, greedy)"
-# full-model generation ms/token (decode + selection + update) at
-# 32K, batch 1, budget 4096 (README.md:60-61 of the reference).
+# The reference's published full-model generation ms/token (decode + selection
+# + update) at 32K, batch 1, budget 4096 (README.md:60-61 of the reference).
 PUBLISHED_MODEL_MS = {"popkv-s": 43.011, "popkv-q": 43.888}
 
 

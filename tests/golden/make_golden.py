@@ -41,7 +41,9 @@ def f16_bits(t):
 
 def main() -> None:
     parser = argparse.ArgumentParser()
-    parser.add_argument("--reference", default=os.environ.get("POPKV_REFERENCE", "/root/reference"))
+    parser.add_argument("--reference", default=os.environ.get("POPKV_REFERENCE"),
+                        required="POPKV_REFERENCE" not in os.environ,
+                        help="checkout of the reference (kw78999/PopKV) to import; or set POPKV_REFERENCE")
     parser.add_argument("--out", default=str(HERE / "popkv_golden.npz"))
     args = parser.parse_args()
     os.environ["TRITON_INTERPRET"] = "1"
