@@ -9,8 +9,10 @@ top-k + current slot, split partials, merge) into one CUDA graph.
 ``fused=True`` uses the single popkv_retrieve launch instead (one thread-block
 cluster per KV head).  Replaying the graph costs one launch.
 
-The graph is specific to the cache length it was captured at.  Call
-``recapture()`` after appending tokens (or use ``run_eager``).
+The graph is specific to the cache length it was captured at: call
+``recapture()`` after appending tokens (or use ``run_eager``).  With
+``max_tokens`` the cache length is read from device memory instead
+(``set_length``), so one captured graph serves every length up to the bound.
 """
 from __future__ import annotations
 
@@ -48,6 +50,13 @@ class SparseAttentionStep:
         chunks: split the step into this many KV-head chunks on forked streams
             so that one chunk's top-k and attention overlap the next chunk's
             score (batch 1 with the consecutive GQA mapping only).
+        max_tokens: keep the cache length in device memory (``length``, set
+            with ``set_length``) so that the captured graph serves every length
+            up to ``max_tokens`` (the *_dyn kernels): ``prefix_keys`` /
+            ``prefix_values`` are then the static caches with at least
+            ``max_tokens`` token rows, and the packed planes hold at least
+            ``max_tokens`` tokens.  Head dim 128, bf16/fp16, the unfused
+            radix path without chunks.
     """
 
     def __init__(self, cache: PopKVCache, prefix_keys: torch.Tensor, prefix_values: torch.Tensor,
@@ -55,7 +64,7 @@ class SparseAttentionStep:
                  q_dtype: torch.dtype = torch.bfloat16, split_tokens: int = 256,
                  batch: int = 1, use_graph: bool = True, fused: bool = False,
                  select: str = "auto", chunks: int = 1, host_io: bool = False,
-                 gather=None) -> None:
+                 gather=None, max_tokens: int | None = None) -> None:
         if prefix_keys.ndim == 3:
             prefix_keys, prefix_values = prefix_keys[None], prefix_values[None]
         if prefix_keys.stride(-1) != 1 or prefix_values.stride(-1) != 1:
@@ -70,7 +79,16 @@ class SparseAttentionStep:
             raise ValueError("SparseAttentionStep needs head_dim 128 (the fp16 score path)")
         if int(prefix_keys.shape[0]) != self.batch:
             raise ValueError("prefix keys batch does not match")
-        if cache.token_count != self.prefix_tokens:
+        self.dynamic = max_tokens is not None
+        if self.dynamic:
+            if not 0 < int(max_tokens) <= self.prefix_tokens or int(max_tokens) > int(cache.packed[0].shape[1]):
+                raise ValueError("max_tokens must fit the K/V caches and the packed planes")
+            if fused or chunks != 1 or select == "hist":
+                raise ValueError("max_tokens needs the unfused radix path without chunks")
+            if cache.token_count > int(max_tokens):
+                raise ValueError("cache token count exceeds max_tokens")
+            self.prefix_tokens = int(max_tokens)
+        elif cache.token_count != self.prefix_tokens:
             raise ValueError("cache token count must equal the prefix length")
         self.head_to_kv = head_to_kv.to(device=self.device, dtype=torch.int64).contiguous()
         self.q_heads = int(self.head_to_kv.numel()) if q_heads is None else int(q_heads)
@@ -108,7 +126,11 @@ class SparseAttentionStep:
         self.q_mag = torch.zeros_like(self.q_sign)
         self.q_low = torch.zeros((B, QH, reps), device=dev, dtype=torch.float32)
         self.q_delta = torch.zeros_like(self.q_low)
-        self.scores = torch.zeros((B, QH, self.prefix_tokens), device=dev, dtype=torch.float16)
+        # Dynamic mode: score rows padded to 16 bytes (the top-k's vector loads).
+        self.score_stride = (self.prefix_tokens + 7) // 8 * 8 if self.dynamic else self.prefix_tokens
+        self.scores = torch.zeros((B, QH, self.score_stride), device=dev, dtype=torch.float16)
+        self.length = (torch.tensor([cache.token_count], device=dev, dtype=torch.int64) if self.dynamic
+                       else None)
         self.indices = torch.zeros((B, QH, self.selected), device=dev, dtype=torch.int64)
         self.partials = torch.zeros((B, QH, self.splits, D + 2), device=dev, dtype=torch.float32)
         self.counters = torch.zeros((B * QH,), device=dev, dtype=torch.int32)  # self-resetting
@@ -227,6 +249,9 @@ class SparseAttentionStep:
             # (device-addressable under unified addressing).
             output = self.host_output[:, q0:q1]
         mapping = self.head_to_kv if (h0, h1) == (0, self.kv_heads) else self._chunk_map
+        if self.dynamic:
+            self._launch_dynamic(s, queries, packed, capacity, pk, pv, ck, cv, indices, partials, output, mapping)
+            return
         # Query encoding runs in the score kernel's prologue.
         if self.select == "hist":
             hist = self.hist[q0:q1]
@@ -257,6 +282,35 @@ class SparseAttentionStep:
         else:
             check(lib.popkv_attn_merge(ptr(partials), B * QH, self.splits, 128, ptr(output),
                                        _lib.dtype_code(output), s))
+
+    def _launch_dynamic(self, s, queries, packed, capacity, pk, pv, ck, cv, indices, partials, output,
+                        mapping) -> None:
+        """Score, top-k, partials and merge with the cache length read from ``self.length``."""
+        lib, check, ptr = _lib.lib(), _lib.check, _lib.ptr
+        B, QH, KVH = self.batch, self.q_heads, self.kv_heads
+        check(lib.popkv_score_dyn(ptr(queries), _lib.dtype_code(queries), B, QH, *(ptr(t) for t in packed), KVH,
+                                  capacity, ptr(mapping), ptr(self.length), self.prefix_tokens, self.g,
+                                  ptr(self.scores), self.score_stride, s))
+        check(lib.popkv_topk_dyn(ptr(self.scores), B * QH, ptr(self.length), self.prefix_tokens,
+                                 self.score_stride, self.k, ptr(indices), self.selected, s))
+        out = None if self.gather is not None else output
+        check(lib.popkv_attn_dyn(
+            ptr(queries), _lib.dtype_code(queries), B, QH, ptr(pk), ptr(pv), _lib.dtype_code(pk), KVH,
+            self.prefix_tokens, pk.stride(0), pk.stride(1), pk.stride(2), pv.stride(0), pv.stride(1),
+            pv.stride(2), ptr(ck), ptr(cv), ptr(self.length), ptr(indices), self.selected, self.k, ptr(mapping),
+            self.split_tokens, ptr(partials), ptr(out), _lib.dtype_code(output), s))
+        if self.gather is not None:
+            self.gather.launch(partials, self.splits, s)
+
+    def set_length(self, tokens: int | None = None) -> None:
+        """Dynamic mode: the number of cached prefix tokens the next replays use
+        (default ``cache.token_count``); the current token is slot ``tokens``."""
+        if not self.dynamic:
+            raise RuntimeError("set_length needs a step built with max_tokens")
+        t = self.cache.token_count if tokens is None else int(tokens)
+        if not 0 <= t <= self.prefix_tokens:
+            raise ValueError(f"length must be in [0, {self.prefix_tokens}]")
+        self.length.fill_(t)
 
     def recapture(self) -> None:
         """(Re)build the CUDA graph of the step's launches for the current buffers."""

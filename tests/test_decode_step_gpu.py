@@ -166,3 +166,40 @@ def test_host_io_step_moves_inputs_and_output_in_the_graph(cuda_device):
     # Device inputs bypass the staging buffers and return the device output.
     dev_out = step(to(x.queries).to(dev), to(x.current_keys[0]).to(dev), to(x.current_values[0]).to(dev))
     assert dev_out.is_cuda and torch.equal(dev_out, want)
+
+
+@pytest.mark.parametrize("preset,budget,host_io", [("popkv-q", 512, False), ("popkv-s", 300, True)])
+def test_device_length_step_serves_every_length(cuda_device, preset, budget, host_io):
+    """One captured step with the cache length on the device, replayed across appended
+    tokens, equals a fresh step captured at each length (bit for bit)."""
+    dev = cuda_device
+    tg, g = P.POPKV_PRESETS[preset]
+    gen = torch.Generator().manual_seed(budget)
+    kvh, qh, t0, cap = 8, 32, 1000 - tg // 2, 1200
+    keys = torch.randn(kvh, cap, 128, generator=gen).to(torch.bfloat16).to(dev)
+    values = torch.randn(kvh, cap, 128, generator=gen).to(torch.bfloat16).to(dev)
+    cache = P.build_popkv_cache(keys[:, :t0].contiguous(), group_size=tg, dim_group_size=g,
+                                reserve_tokens=cap - t0)
+    mapping = torch.from_numpy(head_to_kv(qh, kvh)).to(dev)
+    dyn = SparseAttentionStep(cache, keys, values, mapping, budget=budget, max_tokens=cap - 1, host_io=host_io)
+    for _ in range(tg + 3):  # crosses a token-group boundary
+        t = cache.token_count
+        q = torch.randn(1, qh, 128, generator=gen).to(torch.bfloat16).to(dev)
+        ck = torch.randn(kvh, 128, generator=gen).to(torch.bfloat16).to(dev)
+        cv = torch.randn(kvh, 128, generator=gen).to(torch.bfloat16).to(dev)
+        static = SparseAttentionStep(cache, keys[:, :t], values[:, :t], mapping, budget=budget)
+        want = static(q, ck, cv).clone()
+        dyn.set_length()
+        if host_io:
+            dyn.host_queries.copy_(q.cpu().view_as(dyn.host_queries))
+            dyn.host_current_keys.copy_(ck.cpu().view_as(dyn.host_current_keys))
+            dyn.host_current_values.copy_(cv.cpu().view_as(dyn.host_current_values))
+            got = dyn(dyn.host_queries, dyn.host_current_keys, dyn.host_current_values)
+            torch.cuda.current_stream().synchronize()
+            got = got.to(dev)
+        else:
+            got = dyn(q, ck, cv).clone()
+        assert torch.equal(got.view_as(want), want), f"length {t}"
+        P.append_popkv_kv(cache, keys, values, ck, cv)
+    with pytest.raises(ValueError, match="max_tokens"):
+        SparseAttentionStep(cache, keys, values, mapping, budget=budget, max_tokens=cap + 1)
