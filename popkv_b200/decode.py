@@ -56,7 +56,7 @@ class SparseAttentionStep:
             ``prefix_values`` are then the static caches with at least
             ``max_tokens`` token rows, and the packed planes hold at least
             ``max_tokens`` tokens.  Head dim 128, bf16/fp16, the unfused
-            radix path without chunks.
+            radix path without chunks, one GPU.
     """
 
     def __init__(self, cache: PopKVCache, prefix_keys: torch.Tensor, prefix_values: torch.Tensor,
@@ -83,8 +83,8 @@ class SparseAttentionStep:
         if self.dynamic:
             if not 0 < int(max_tokens) <= self.prefix_tokens or int(max_tokens) > int(cache.packed[0].shape[1]):
                 raise ValueError("max_tokens must fit the K/V caches and the packed planes")
-            if fused or chunks != 1 or select == "hist":
-                raise ValueError("max_tokens needs the unfused radix path without chunks")
+            if fused or chunks != 1 or select == "hist" or gather is not None:
+                raise ValueError("max_tokens needs the unfused radix path without chunks or a peer gather")
             if cache.token_count > int(max_tokens):
                 raise ValueError("cache token count exceeds max_tokens")
             self.prefix_tokens = int(max_tokens)
