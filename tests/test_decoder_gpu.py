@@ -275,7 +275,7 @@ def _prefix(cfg, batch, T, seed=3):
 
 
 @pytest.mark.parametrize("method,batch,T,steps", [("popkv-s", 1, 250, 24), ("popkv-q", 2, 200, 12),
-                                                  ("full", 1, 100, 6)])
+                                                  ("full", 1, 100, 6), ("popkv-s", 5, 120, 4)])
 def test_graph_decoder_matches_static_length_loop(cuda_device, method, batch, T, steps):
     weights = LlamaWeights.random(TINY, device=cuda_device, seed=1, std=0.05)
     tg = {"popkv-s": 64, "popkv-q": 128, "full": 32}[method]
@@ -548,3 +548,28 @@ def test_layer_tail_matches_separate_products(cuda_device, method):
         count = ctypes.c_uint32(99)
         _lib.check(getattr(_lib.lib(), name)(ctypes.byref(count)))
         assert count.value == 0, name
+
+
+def test_synthetic_prefill_fills_caches_and_planes(cuda_device):
+    """prefill_synthetic writes K/V rows [0, T) of every layer, packs the sparse layers'
+    planes exactly as popkv_pack does from those rows, and leaves a valid next token."""
+    weights = LlamaWeights.random(TINY, device=cuda_device, seed=4, std=0.02)
+    retrieval = RetrievalConfig(budget=64, group_size=64, dim_group_size=64)
+    dec = LlamaSparseDecoder(weights, method="popkv-s", retrieval=retrieval, batch=2, max_context=300)
+    T = 250
+    first = dec.prefill_synthetic(T, seed=3)
+    assert int(dec.position.item()) == T
+    assert torch.all((first >= 0) & (first < TINY.vocab_size))
+    for l in range(TINY.num_hidden_layers):
+        kc, vc = dec.k_cache[l], dec.v_cache[l]
+        assert torch.count_nonzero(kc[:, :, T:]) == 0 and torch.count_nonzero(vc[:, :, T:]) == 0
+        assert bool((kc[:, :, :T].abs().sum(-1) > 0).all()) and bool((vc[:, :, :T].abs().sum(-1) > 0).all())
+    for l, planes in dec.packed.items():
+        keys = dec.k_cache[l].reshape(-1, dec.max_context, 128)[:, :T].contiguous()
+        want = popkv_cuda.pack_keys(keys, token_capacity=dec.meta_capacity, token_group_size=64, dim_group_size=64)
+        for a, b in zip(planes, want):
+            assert torch.equal(a[:, :T], b[:, :T])
+    for _ in range(3):  # decodes from there
+        logits = dec.decode()
+        assert torch.isfinite(logits).all()
+    dec.close()
