@@ -228,6 +228,26 @@ def make_layer(args, world, rank, device):
     return layer
 
 
+def fold_batch(layer, batch: int):
+    """Independent sequences as extra heads: [B, KVH, ...] -> [1, B*KVH, ...].
+
+    Each sequence has its own cache and metadata (config 3's batch); the step
+    then runs as batch 1 over B times the heads, with the consecutive GQA
+    mapping of every sequence's query heads onto its own KV heads.
+    """
+    import torch
+    out = dict(layer)
+    kvl, ql = layer["kv_local"], layer["q_local"]
+    out["keys"] = layer["keys"].reshape(1, batch * kvl, *layer["keys"].shape[2:])
+    out["values"] = layer["values"].reshape(1, batch * kvl, *layer["values"].shape[2:])
+    out["queries"] = layer["queries"].reshape(1, batch * ql, 128)
+    out["cur_k"] = layer["cur_k"].reshape(1, batch * kvl, 128)
+    out["cur_v"] = layer["cur_v"].reshape(1, batch * kvl, 128)
+    out["mapping"] = torch.arange(batch * ql, device=layer["mapping"].device, dtype=torch.int64) // (ql // kvl)
+    out["q_local"], out["kv_local"] = batch * ql, batch * kvl
+    return out
+
+
 def build_steps(args, layer, copies: int, gather=None):
     """`copies` independent layer instances (own cache + metadata), each a captured step."""
     import torch
@@ -238,13 +258,11 @@ def build_steps(args, layer, copies: int, gather=None):
         keys = layer["keys"].clone()
         values = layer["values"].clone()
         B = args.batch
-        # Metadata packed from the (batch-0) keys of this shard; batch > 1 shares layout per row.
+        # One cache per step: a batch of independent sequences arrives folded into heads.
         caches = []
         for b in range(B):
             caches.append(P.build_popkv_cache(keys[b], group_size=layer["tg"], dim_group_size=layer["g"],
                                               reserve_tokens=0))
-        if B > 1:
-            raise SystemExit("batch > 1 benchmarking is not wired yet")
         step = SparseAttentionStep(caches[0], keys, values, layer["mapping"], budget=args.budget,
                                    q_dtype=torch.bfloat16, batch=B, use_graph=not args.no_graph,
                                    select=args.select, chunks=args.chunks, gather=gather,
@@ -329,6 +347,12 @@ def run_ours(args, world, rank, local):
     from popkv_b200 import _lib
     _lib.lib()
     layer = make_layer(args, world, rank, device)
+    batch = args.batch
+    if batch > 1:  # independent sequences, folded into heads; everything below runs as batch 1
+        if world > 1:
+            raise SystemExit("batch > 1 runs on one GPU")
+        layer = fold_batch(layer, batch)
+        args = argparse.Namespace(**{**vars(args), "batch": 1, "no_cpu_baseline": True})
     copies = max(2, math.ceil(3 * L2_BYTES / max(1, layer_bytes(args, layer))))
     copies = min(copies, 16)
     q_local = layer["q_local"]
@@ -389,6 +413,8 @@ def run_ours(args, world, rank, local):
         for j, k in enumerate(sorted(stages)):
             stages[k]["us"] = float(vec[j].item())
         e2e["value"] = float(vec[-1].item())
+    # The published per-layer figure and the ncu traffic are for config 1 itself.
+    default_workload = all({**vars(args), "batch": batch}.get(k) == v for k, v in DEFAULT_WORKLOAD.items())
     if rank == 0:
         rows = union_rows(steps[0])
         abytes = algorithmic_bytes(args, layer, rows)
@@ -412,13 +438,14 @@ def run_ours(args, world, rank, local):
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(ms_per_step, 5), "higher_is_better": False,
             "scaling": "strong",
-            "vs_baseline": round(ms_per_step / PUBLISHED_MS_PER_LAYER, 4),
+            "vs_baseline": round(ms_per_step / PUBLISHED_MS_PER_LAYER, 4) if default_workload else None,
             "dtype": "bf16", "data": "synthetic (seeded N(0,1) keys x lognormal channel factors + RoPE)",
             "config": {
-                "workload": f"config 1: single-layer decode step, {args.preset}, batch {args.batch}, "
-                            f"32 q / 8 kv heads, head_dim 128, context {args.context}, budget {args.budget}",
+                "workload": (f"config {1 if batch == 1 else 3}: single-layer decode step, {args.preset}, "
+                             f"batch {batch}, 32 q / 8 kv heads, head_dim 128, context {args.context}, "
+                             f"budget {args.budget}"),
                 "preset": args.preset, "token_group": layer["tg"], "dim_group": layer["g"],
-                "batch": args.batch, "context": args.context, "budget": args.budget,
+                "batch": batch, "context": args.context, "budget": args.budget,
                 "parallelism": f"kv-head shard x{world}" + ("" if world == 1 else (
                     " + merge fused with the all-gather over NVLink peer memory" if peer is not None
                     else " + NCCL all-gather")),
@@ -429,8 +456,7 @@ def run_ours(args, world, rank, local):
                 "bound": "hbm", "kernel": dominant,
                 "achieved": dom.get("achieved_gbs"), "peak": peaks["hbm_gbs"], "unit": "GB/s",
                 "frac": dom.get("frac_of_hbm"),
-                "traffic": (NCU_TRAFFIC_CONFIG1.get(dominant) if world == 1 and all(
-                    getattr(args, k) == v for k, v in DEFAULT_WORKLOAD.items()) else None),
+                "traffic": (NCU_TRAFFIC_CONFIG1.get(dominant) if world == 1 and default_workload else None),
                 "algorithmic_bytes": dom.get("algorithmic_bytes"),
                 "peak_source": peaks["source"],
             },
@@ -552,7 +578,8 @@ def stage_breakdown(args, layer, steps, device):
         check(lib.popkv_topk_hist(
             ptr(st.scores), ptr(st.hist), B * st.q_heads, st.prefix_tokens, st.prefix_tokens, st.k,
             st.prefix_tokens, ptr(st.indices), st.selected, s))
-    run("score_topk_hist", score_topk_hist)
+    if args.context <= 65536:  # the histogram top-k takes rows of at most 65536 scores
+        run("score_topk_hist", score_topk_hist)
 
     def score_topk_radix(st):
         check(lib.popkv_score(
