@@ -1004,8 +1004,9 @@ int launch_cluster16(const void* scores, int64_t rows, int64_t tokens, int64_t r
     return check_launch("popkv_topk");
 }
 
-// fp16 rows of up to 8 * 512 * 64 keys (64 keys per thread only with 8 CTAs
-// per row) with 0 < k <= tokens and fewer than 2^16 keys per CTA
+// fp16 rows of up to 8 * 512 * 64 keys (64 keys per thread with 8 CTAs per row,
+// or with 4 when many rows would overflow a wave) with 0 < k <= tokens and
+// fewer than 2^16 keys per CTA
 // slice: about one wave of CTAs (rows * CPR near 148), the fewest keys per
 // thread that cover the row.  Returns -1 when the shape does not apply.
 int try_launch_cluster16(const void* scores, int64_t rows, int64_t tokens, int64_t row_stride,
@@ -1028,6 +1029,13 @@ int try_launch_cluster16(const void* scores, int64_t rows, int64_t tokens, int64
         cpr = 6;
         per = 16;
     }
+    // Many long rows: 8-CTA clusters would need more than one resident wave
+    // (4 CTAs of 512 threads per SM); 4 CTAs at 64 keys per thread fit in one.
+    constexpr int64_t kWaveCtas = 4 * 148;  // resident 512-thread CTAs on a B200 (4 per SM)
+    if (cpr == 8 && per == 32 && rows * 8 > kWaveCtas && tokens <= static_cast<int64_t>(4) * kClusterThreads * 64) {
+        cpr = 4;
+        per = 64;
+    }
 #define POPKV_C16(CPR_, PER_)                                                                      \
     if (cpr == CPR_ && per == PER_)                                                                \
         return launch_cluster16<CPR_, PER_>(scores, rows, tokens, row_stride, k, current_index, out, \
@@ -1036,6 +1044,7 @@ int try_launch_cluster16(const void* scores, int64_t rows, int64_t tokens, int64
     POPKV_C16_CPR(1)
     POPKV_C16_CPR(2)
     POPKV_C16_CPR(4)
+    POPKV_C16(4, 64)
     POPKV_C16(6, 16)
     POPKV_C16_CPR(8)
     POPKV_C16(8, 64)

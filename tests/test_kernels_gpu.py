@@ -256,7 +256,7 @@ def test_topk_matches_oracle(cuda_device, tokens, dtype):
 
 
 @pytest.mark.parametrize("rows,tokens", [(1, 131072), (3, 65536), (32, 32768), (32, 33024), (64, 8191),
-                                         (200, 777)])
+                                         (200, 777), (160, 70000)])
 def test_topk_all_equal_and_row_counts(cuda_device, rows, tokens):
     """Every key equal (all winners are ties, taken in index order) and many cluster shapes."""
     gen = torch.Generator().manual_seed(rows)
