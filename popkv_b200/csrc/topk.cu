@@ -1036,6 +1036,8 @@ int try_launch_cluster16(const void* scores, int64_t rows, int64_t tokens, int64
         cpr = 4;
         per = 64;
     }
+    // Likewise a row of 64K-96K keys fills 6 CTAs at 32 keys per thread.
+    if (cpr == 8 && per == 32 && tokens <= static_cast<int64_t>(6) * kClusterThreads * 32) cpr = 6;
 #define POPKV_C16(CPR_, PER_)                                                                      \
     if (cpr == CPR_ && per == PER_)                                                                \
         return launch_cluster16<CPR_, PER_>(scores, rows, tokens, row_stride, k, current_index, out, \
@@ -1046,6 +1048,7 @@ int try_launch_cluster16(const void* scores, int64_t rows, int64_t tokens, int64
     POPKV_C16_CPR(4)
     POPKV_C16(4, 64)
     POPKV_C16(6, 16)
+    POPKV_C16(6, 32)
     POPKV_C16_CPR(8)
     POPKV_C16(8, 64)
 #undef POPKV_C16_CPR

@@ -240,7 +240,7 @@ def _tie_heavy_scores(gen, rows, tokens, levels=None):
     return x
 
 
-@pytest.mark.parametrize("tokens", (1, 2, 100, 1000, 4096, 32768, 33024, 49152, 65536, 131072))
+@pytest.mark.parametrize("tokens", (1, 2, 100, 1000, 4096, 32768, 33024, 49152, 65536, 98304, 131072))
 @pytest.mark.parametrize("dtype", (torch.float16, torch.float32))
 def test_topk_matches_oracle(cuda_device, tokens, dtype):
     gen = torch.Generator().manual_seed(tokens)
