@@ -86,6 +86,9 @@ def parse_args(argv=None):
     p.add_argument("--mlp-parallel", choices=("replicated", "tensor"), default="replicated",
                    help="--model on several GPUs: replicated o_proj/MLP (one all-gather per layer) or "
                         "tensor-parallel (two all-reduces per layer)")
+    p.add_argument("--all-reduce", choices=("peer", "nccl"), default="peer",
+                   help="--mlp-parallel tensor: sum the partial products with popkv_peer_sum over NVLink peer "
+                        "memory or with an NCCL all-reduce")
     p.add_argument("--no-model", action="store_true",
                    help="skip the full-model decode measurement that a 1-GPU default run adds")
     p.add_argument("--model", action="store_true",
@@ -867,7 +870,8 @@ def measure_model(args, world, rank, device, dist, warmup=None):
     T, W, K = args.context, (args.warmup if warmup is None else warmup), args.gen_steps
     dec = LlamaSparseDecoder(weights, method=method, retrieval=retrieval, batch=args.batch,
                              max_context=T + W + 2 * K + 2, rank=rank, world=world,
-                             group=None, mlp_parallel=args.mlp_parallel)
+                             group=None, mlp_parallel=args.mlp_parallel,
+                             all_reduce=args.all_reduce)
     gen = torch.Generator().manual_seed(0)
     ids = torch.randint(0, cfg.vocab_size, (args.batch, T), generator=gen)
     torch.cuda.synchronize(device)
@@ -933,6 +937,8 @@ def measure_model(args, world, rank, device, dist, warmup=None):
         # Our kernels per step: dense layer 6 (2 norms, RoPE/append, partial, merge,
         # SiLU), sparse layer 9 (+ score, top-k, append re-encode), final norm 1.
         ours_per_step = dense * 6 + len(dec.sparse_layers) * 9 + 1
+        if dec._peer_sum is not None:
+            ours_per_step += 2 * cfg.num_hidden_layers  # the peer all-reduces
         workload = ("config 2: 32-layer Llama-3.1-8B-shaped decoder" if args.batch == 1 and T <= 65536
                     else "config 4 shape: 32-layer Llama-3.1-8B-shaped decoder")
         result = {
@@ -955,7 +961,9 @@ def measure_model(args, world, rank, device, dist, warmup=None):
                 "parallelism": f"kv-head shard x{world}" + (
                     "" if world == 1 else " + NCCL all-gather per layer, replicated MLP"
                     if args.mlp_parallel == "replicated" else
-                    " + tensor-parallel o_proj/MLP, two NCCL all-reduces per layer"),
+                    " + tensor-parallel o_proj/MLP, two NCCL all-reduces per layer"
+                    if args.all_reduce == "nccl" else
+                    " + tensor-parallel o_proj/MLP, two peer-memory all-reduces (popkv_peer_sum) per layer"),
                 "l2": "each step streams ~16 GB of weights > L2",
                 "launch": "one CUDA graph per token (device-resident position), replayed",
             },

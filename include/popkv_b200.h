@@ -384,6 +384,29 @@ POPKV_API int popkv_attn_merge_gather(const float* partials, int64_t rows, int64
                                       const uint64_t* own_recv, uint32_t* state, void* out, void* stream);
 
 /*
+ * One-shot all-reduce (sum) of `count` values of `dtype` in place across
+ * `world` GPUs over peer memory: the partial products of a tensor-parallel
+ * output projection or MLP down projection.  Each 32-bit word of `data` (two
+ * fp16/bf16 values or one fp32) is stored into every peer's receive area with
+ * the launch epoch; each rank polls its own area, with a bounded wait, and sums
+ * in fp32 in rank order, rounded once, so every rank holds the same bits.
+ *
+ * Arguments:
+ * - data: count values, 4-byte aligned; count * element size a multiple of 4.
+ * - peer_recv / own_recv: as popkv_attn_merge_gather, areas of
+ *   2 x world x (count * element size / 4) uint64, zero at setup.
+ * - state: 3 uint32 in this rank's memory, zero at setup; state[2] becomes 1
+ *   when a wait for a peer gave up.
+ *
+ * Every rank must issue the same sequence of these calls on one set of
+ * buffers.  The reference decodes on one GPU and has no counterpart; this
+ * replaces torch.distributed.all_reduce in the tensor-parallel decode of
+ * popkv_b200/decoder.py.
+ */
+POPKV_API int popkv_peer_sum(void* data, int dtype, int64_t count, int64_t rank, int64_t world,
+                             uint64_t* const* peer_recv, const uint64_t* own_recv, uint32_t* state, void* stream);
+
+/*
  * Device-resident step lengths.  The reference passes the cache length as a
  * Python integer on every decode call (popkv.py:1079-1099), so each token's
  * launches differ.  The *_dyn entry points read it from device memory at run

@@ -47,6 +47,7 @@ _SIGNATURES = {
     "popkv_peer_close": ([_P], _I),
     "popkv_peer_free": ([_P], _I),
     "popkv_attn_merge_gather": ([_P, _L, _L, _L, _I, _L, _L, _P, _P, _P, _P, _P], _I),
+    "popkv_peer_sum": ([_P, _I, _L, _L, _L, _P, _P, _P, _P], _I),
     "popkv_retrieve": ([_P, _I, _L, _L, _L, _P, _P, _P, _P, _L, _L, _L, _L, _L, _P, _P, _P, _I,
                         _L, _L, _L, _L, _L, _L, _P, _P, _L, _P, _P, _P, _P], _I),
     "popkv_score_dyn": ([_P, _I, _L, _L, _P, _P, _P, _P, _L, _L, _P, _P, _L, _L, _P, _L, _P], _I),

@@ -159,6 +159,75 @@ __global__ void __launch_bounds__(kGatherThreads) merge_gather_kernel(
     }
 }
 
+// One-shot all-reduce (sum) of a short vector over peer memory: the partial
+// products of a tensor-parallel layer.  Each thread owns one 32-bit word of the
+// vector (two 16-bit values or one fp32), stores it with the launch epoch into
+// every peer's receive area, then polls its own area for the same word of
+// every peer.  The sum runs in fp32 in rank order 0..world-1 and is rounded
+// once, so every rank computes identical bits.  Receive area:
+// [2 parities][world source ranks][words] 8-byte words; state as above.
+constexpr int kSumThreads = 256;
+
+template <typename T>
+__global__ void __launch_bounds__(kSumThreads) peer_sum_kernel(
+    uint32_t* data, int64_t words, int rank, int world, unsigned long long* const* __restrict__ peer_recv,
+    const unsigned long long* own_recv, unsigned int* state) {
+    constexpr int V = 4 / static_cast<int>(sizeof(T));
+    __shared__ int s_failed;
+    pdl_wait();
+    // The next product may fill its weight ring while the words cross NVLink.
+    pdl_launch_dependents();
+    if (threadIdx.x == 0) s_failed = 0;
+    __syncthreads();
+    const unsigned int epoch = state[0] + 1u;
+    const int64_t par = epoch & 1u;
+    const int64_t i = static_cast<int64_t>(blockIdx.x) * kSumThreads + threadIdx.x;
+    if (i < words) {
+        const uint32_t mine = data[i];
+        const unsigned long long word = (static_cast<unsigned long long>(epoch) << 32) | mine;
+        const int64_t send = (par * world + rank) * words + i;
+        for (int r = 0; r < world; ++r)
+            if (r != rank) store_relaxed_sys(peer_recv[r] + send, word);
+        float acc[V];
+#pragma unroll
+        for (int v = 0; v < V; ++v) acc[v] = 0.0f;
+        bool ok = true;
+        for (int r = 0; r < world; ++r) {
+            uint32_t bits = mine;
+            if (r != rank) {
+                const unsigned long long* src = own_recv + (par * world + r) * words + i;
+                unsigned long long w = load_relaxed_sys(src);
+                long long polls = 0;
+                while (static_cast<unsigned int>(w >> 32) != epoch) {
+                    if (++polls > kPolls) {
+                        ok = false;
+                        break;
+                    }
+                    w = load_relaxed_sys(src);
+                }
+                bits = static_cast<uint32_t>(w);
+            }
+#pragma unroll
+            for (int v = 0; v < V; ++v)
+                acc[v] += to_float(from_bits<T>(V == 1 ? bits : (bits >> (16 * v)) & 0xFFFFu));
+        }
+        uint32_t out = 0;
+#pragma unroll
+        for (int v = 0; v < V; ++v) out |= out_bits<T>(acc[v]) << (16 * v);
+        data[i] = out;
+        if (!ok) s_failed = 1;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        if (s_failed) state[2] = 1u;
+        __threadfence();
+        if (atomicAdd(&state[1], 1u) == gridDim.x - 1) {  // the last CTA advances the epoch
+            state[1] = 0u;
+            state[0] = epoch;
+        }
+    }
+}
+
 }  // namespace
 }  // namespace popkv
 
@@ -248,4 +317,45 @@ extern "C" int popkv_attn_merge_gather(const float* partials, int64_t rows, int6
                          own, state, static_cast<__nv_bfloat16*>(out));
     if (err != cudaSuccess) return fail(POPKV_ERR_CUDA, "popkv_attn_merge_gather: %s", cudaGetErrorString(err));
     return check_launch("popkv_attn_merge_gather");
+}
+
+extern "C" int popkv_peer_sum(void* data, int dtype, int64_t count, int64_t rank, int64_t world,
+                              uint64_t* const* peer_recv, const uint64_t* own_recv, uint32_t* state, void* stream) {
+    using namespace popkv;
+    if (!valid_dtype(dtype)) return fail(POPKV_ERR_INVALID, "popkv_peer_sum: data must be fp32/fp16/bf16");
+    if (world < 1 || world > 64 || rank < 0 || rank >= world)
+        return fail(POPKV_ERR_INVALID, "popkv_peer_sum: invalid rank/world");
+    if (!data || !peer_recv || !own_recv || !state) return fail(POPKV_ERR_INVALID, "popkv_peer_sum: null pointer");
+    const int64_t elem = dtype == POPKV_DTYPE_F32 ? 4 : 2;
+    if (count <= 0 || (count * elem) % 4)
+        return fail(POPKV_ERR_INVALID, "popkv_peer_sum: count must be positive and fill whole 4-byte words");
+    if (!aligned(data, 4) || !aligned(own_recv, 8))
+        return fail(POPKV_ERR_INVALID, "popkv_peer_sum: data must be 4-byte and the receive area 8-byte aligned");
+    const int64_t words = count * elem / 4;
+    const int64_t ctas = (words + kSumThreads - 1) / kSumThreads;
+    // Every CTA waits for the peers' CTAs of the same words: one resident wave.
+    int device = 0, sms = 0, per_sm = 0;
+    cudaError_t qerr = cudaGetDevice(&device);
+    if (qerr == cudaSuccess) qerr = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+    if (qerr == cudaSuccess)
+        qerr = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, peer_sum_kernel<float>, kSumThreads, 0);
+    if (qerr != cudaSuccess) return fail(POPKV_ERR_CUDA, "popkv_peer_sum: %s", cudaGetErrorString(qerr));
+    if (ctas > static_cast<int64_t>(sms) * per_sm)
+        return fail(POPKV_ERR_UNSUPPORTED, "popkv_peer_sum: %lld values exceed one resident wave",
+                    static_cast<long long>(count));
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const dim3 grid(static_cast<unsigned>(ctas)), block(kSumThreads);
+    const int r = static_cast<int>(rank), w = static_cast<int>(world);
+    auto peers = reinterpret_cast<unsigned long long* const*>(peer_recv);
+    auto own = reinterpret_cast<const unsigned long long*>(own_recv);
+    auto d = static_cast<uint32_t*>(data);
+    cudaError_t err;
+    if (dtype == POPKV_DTYPE_F32)
+        err = launch_pdl(peer_sum_kernel<float>, grid, block, 0, s, 1, d, words, r, w, peers, own, state);
+    else if (dtype == POPKV_DTYPE_F16)
+        err = launch_pdl(peer_sum_kernel<__half>, grid, block, 0, s, 1, d, words, r, w, peers, own, state);
+    else
+        err = launch_pdl(peer_sum_kernel<__nv_bfloat16>, grid, block, 0, s, 1, d, words, r, w, peers, own, state);
+    if (err != cudaSuccess) return fail(POPKV_ERR_CUDA, "popkv_peer_sum: %s", cudaGetErrorString(err));
+    return check_launch("popkv_peer_sum");
 }

@@ -214,15 +214,19 @@ class LlamaSparseDecoder:
             output projection and MLP) or "tensor" (batch <= 4, several ranks):
             o_proj and down_proj keep this rank's input columns (its heads, its
             1/world of the intermediate dims), gate/up its intermediate rows;
-            the two partial outputs are summed with an NCCL all-reduce each
-            layer instead of all-gathering the attention rows.  Each rank then
+            the two partial outputs are summed with an all-reduce each layer
+            instead of all-gathering the attention rows.  Each rank then
             streams 1/world of those weights.  The LM head stays replicated.
+        all_reduce: how tensor mode sums the partial outputs: "peer" (one
+            popkv_peer_sum launch over NVLink peer memory, fp32 sum in rank order)
+            or "nccl" (torch.distributed.all_reduce).
     """
 
     def __init__(self, weights: LlamaWeights, *, method: str = "popkv-s",
                  retrieval: RetrievalConfig | None = None, batch: int = 1, max_context: int,
                  split_tokens: int = 256, rank: int = 0, world: int = 1, group=None,
-                 use_graph: bool = True, mlp_parallel: str = "replicated") -> None:
+                 use_graph: bool = True, mlp_parallel: str = "replicated",
+                 all_reduce: str = "peer") -> None:
         if method not in DECODE_METHODS:
             raise ValueError(f"method must be one of {DECODE_METHODS}")
         cfg = weights.config
@@ -238,6 +242,8 @@ class LlamaSparseDecoder:
         if mlp_parallel not in ("replicated", "tensor"):
             raise ValueError("mlp_parallel must be 'replicated' or 'tensor'")
         self.tensor_mlp = mlp_parallel == "tensor" and world > 1
+        if all_reduce not in ("peer", "nccl"):
+            raise ValueError("all_reduce must be 'peer' or 'nccl'")
         if self.tensor_mlp and (batch > 4 or cfg.intermediate_size % (8 * world)):
             raise ValueError("mlp_parallel='tensor' needs batch <= 4 and intermediate dims divisible by 8 * world")
         self.w, self.cfg, self.method, self.retrieval = weights, cfg, method, retrieval
@@ -289,6 +295,11 @@ class LlamaSparseDecoder:
         self.inter_local = I // world if self.tensor_mlp else I
         self.act = torch.zeros((B, self.inter_local), device=dev, dtype=bf)
         self.down = torch.zeros((B, H), device=dev, dtype=bf)
+        # Tensor mode: the partial products' all-reduce over peer memory.
+        self._peer_sum = None
+        if self.tensor_mlp and all_reduce == "peer":
+            from .sharding import PeerSum
+            self._peer_sum = PeerSum(B * H, bf, dev, group)
         self.logits = torch.zeros((B, cfg.vocab_size), device=dev, dtype=bf)
         self.logits_f32 = torch.zeros((B, cfg.vocab_size), device=dev, dtype=torch.float32)
         # This rank's q | k | v rows of every layer's fused projection.
@@ -400,7 +411,9 @@ class LlamaSparseDecoder:
 
     def _sum_partials(self, t: torch.Tensor, stream) -> None:
         """Tensor mode: sum the ranks' partial products (NCCL all-reduce, inside the graph)."""
-        if self.tensor_mlp:
+        if self._peer_sum is not None:
+            self._peer_sum.launch(t, ctypes_stream(stream))
+        elif self.tensor_mlp:
             import torch.distributed as dist
             with torch.cuda.stream(stream):
                 dist.all_reduce(t, group=self.group)
@@ -703,6 +716,14 @@ class LlamaSparseDecoder:
             out[:, i].copy_(self.token)
         return out.cpu()
 
+    def all_reduce_error(self) -> bool:
+        """True when a peer all-reduce gave up waiting for a peer (tensor mode)."""
+        return self._peer_sum is not None and self._peer_sum.error()
+
     def close(self) -> None:
-        """Release the CUDA graph (before the process group is destroyed)."""
+        """Release the CUDA graph and the peer areas (before the process group is
+        destroyed; collective in tensor mode)."""
         self.graph = None
+        if self._peer_sum is not None:
+            self._peer_sum.close()
+            self._peer_sum = None

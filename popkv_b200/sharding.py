@@ -74,21 +74,16 @@ def gather_heads(local: torch.Tensor, group=None) -> torch.Tensor:
     return flat.view(world, batch, q_local, dim).permute(1, 0, 2, 3).reshape(batch, world * q_local, dim)
 
 
-class PeerGather:
-    """Merge fused with the all-gather over NVLink peer memory (popkv_attn_merge_gather).
+class _PeerArea:
+    """This rank's receive area in device memory, mapped by every peer of ``group``.
 
-    Every rank of ``group`` constructs one, collectively: each allocates its
-    receive area (popkv_peer_alloc), the 64-byte CUDA IPC
-    handles are exchanged with ``all_gather_object`` (any backend), and each
-    rank maps its peers' memory.  ``launch`` then merges this rank's ``rows``
-    split states and leaves all ranks' merged rows in ``output``
-    [world * rows, 128], rank-major.  Every rank must launch the same sequence
-    of steps; ``error()`` reports a wait for a peer that gave up.
+    Collective: each rank allocates ``nbytes`` (popkv_peer_alloc, zeroed), the
+    64-byte CUDA IPC handles are exchanged with ``all_gather_object`` (any
+    backend), and each rank maps its peers' areas.  ``ptrs`` holds every rank's
+    area base in rank order (a device int64 array), ``own`` this rank's.
     """
 
-    HEAD_DIM = 128
-
-    def __init__(self, rows: int, dtype: torch.dtype, device, group=None) -> None:
+    def __init__(self, nbytes: int, device, group=None) -> None:
         import ctypes
 
         import torch.distributed as dist
@@ -98,16 +93,13 @@ class PeerGather:
         self.group = group
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
-        self.rows = int(rows)
-        self.dtype = dtype
         self.device = torch.device(device)
         lib = _lib.lib()
-        recv_bytes = 2 * self.world * self.rows * self.HEAD_DIM * 8  # (value, epoch) words
         ptr = ctypes.c_void_p()
         handle = ctypes.create_string_buffer(64)
         with torch.cuda.device(self.device):
-            _lib.check(lib.popkv_peer_alloc(recv_bytes, ctypes.byref(ptr), handle))
-        self._own = ptr
+            _lib.check(lib.popkv_peer_alloc(int(nbytes), ctypes.byref(ptr), handle))
+        self.own = ptr
         self._opened: list = []
         handles: list = [None] * self.world
         dist.all_gather_object(handles, handle.raw, group=group)
@@ -121,18 +113,9 @@ class PeerGather:
                 _lib.check(lib.popkv_peer_open(h, ctypes.byref(p)))
                 self._opened.append(p)
                 bases.append(p.value)
-        self._recv_ptrs = torch.tensor(bases, dtype=torch.int64, device=self.device)
+        self.ptrs = torch.tensor(bases, dtype=torch.int64, device=self.device)
+        # Launch epoch, CTAs done in the launch, wait-gave-up flag.
         self.state = torch.zeros(4, dtype=torch.int32, device=self.device)
-        self.output = torch.empty((self.world * self.rows, self.HEAD_DIM), dtype=dtype, device=self.device)
-
-    def launch(self, partials: torch.Tensor, splits: int, stream) -> None:
-        """Merge ``partials`` [rows, splits, 130] and gather into ``output`` on ``stream``."""
-        import ctypes
-        lib, _lib = self._lib.lib(), self._lib
-        self._lib.check(lib.popkv_attn_merge_gather(
-            _lib.ptr(partials), self.rows, int(splits), self.HEAD_DIM, _lib.dtype_code(self.output),
-            self.rank, self.world, _lib.ptr(self._recv_ptrs), ctypes.c_void_p(self._own.value),
-            _lib.ptr(self.state), _lib.ptr(self.output), stream))
 
     def error(self) -> bool:
         return bool(int(self.state[2].item()))
@@ -147,6 +130,93 @@ class PeerGather:
             for p in self._opened:
                 self._lib.check(lib.popkv_peer_close(p))
             self._opened = []
-            if self._own is not None:
-                self._lib.check(lib.popkv_peer_free(self._own))
-                self._own = None
+            if self.own is not None:
+                self._lib.check(lib.popkv_peer_free(self.own))
+                self.own = None
+
+
+class PeerGather:
+    """Merge fused with the all-gather over NVLink peer memory (popkv_attn_merge_gather).
+
+    Every rank of ``group`` constructs one, collectively (a ``_PeerArea`` of
+    2 x world x rows x 128 (value, epoch) words).  ``launch`` then merges this
+    rank's ``rows`` split states and leaves all ranks' merged rows in
+    ``output`` [world * rows, 128], rank-major.  Every rank must launch the
+    same sequence of steps; ``error()`` reports a wait for a peer that gave up.
+    """
+
+    HEAD_DIM = 128
+
+    def __init__(self, rows: int, dtype: torch.dtype, device, group=None) -> None:
+        from . import _lib
+        self._lib = _lib
+        self.rows = int(rows)
+        self.dtype = dtype
+        self.device = torch.device(device)
+        import torch.distributed as dist
+        world = dist.get_world_size(group)
+        self.area = _PeerArea(2 * world * self.rows * self.HEAD_DIM * 8, self.device, group)
+        self.world, self.rank = self.area.world, self.area.rank
+        self.state = self.area.state
+        self.output = torch.empty((self.world * self.rows, self.HEAD_DIM), dtype=dtype, device=self.device)
+
+    def launch(self, partials: torch.Tensor, splits: int, stream) -> None:
+        """Merge ``partials`` [rows, splits, 130] and gather into ``output`` on ``stream``."""
+        import ctypes
+        lib, _lib = self._lib.lib(), self._lib
+        self._lib.check(lib.popkv_attn_merge_gather(
+            _lib.ptr(partials), self.rows, int(splits), self.HEAD_DIM, _lib.dtype_code(self.output),
+            self.rank, self.world, _lib.ptr(self.area.ptrs), ctypes.c_void_p(self.area.own.value),
+            _lib.ptr(self.state), _lib.ptr(self.output), stream))
+
+    def error(self) -> bool:
+        return self.area.error()
+
+    def close(self) -> None:
+        """Unmap the peers and free this rank's area (collective: all ranks call it)."""
+        self.area.close()
+
+
+class PeerSum:
+    """In-place all-reduce (sum) of short vectors over NVLink peer memory (popkv_peer_sum).
+
+    For the tensor-parallel decode's partial products: one launch, no NCCL
+    kernel, and the next kernel of the step may start filling its weight ring
+    while the words cross NVLink.  Constructed collectively for vectors of at
+    most ``count`` values of ``dtype``; every rank must launch the same
+    sequence of sums.  The sum is taken in fp32 in rank order and rounded
+    once, so all ranks hold identical bits.
+    """
+
+    def __init__(self, count: int, dtype: torch.dtype, device, group=None) -> None:
+        import torch.distributed as dist
+
+        from . import _lib
+        self._lib = _lib
+        self.count = int(count)
+        self.dtype = dtype
+        elem = torch.empty((), dtype=dtype).element_size()
+        if self.count <= 0 or (self.count * elem) % 4:
+            raise ValueError("count * element size must be a positive multiple of 4 bytes")
+        self.words = self.count * elem // 4
+        world = dist.get_world_size(group)
+        self.area = _PeerArea(2 * world * self.words * 8, device, group)
+        self.world, self.rank = self.area.world, self.area.rank
+        self.state = self.area.state
+
+    def launch(self, data: torch.Tensor, stream) -> None:
+        """Replace ``data`` (``count`` contiguous values) by the sum over ranks, on ``stream``."""
+        import ctypes
+        if data.dtype != self.dtype or data.numel() != self.count or not data.is_contiguous():
+            raise ValueError(f"PeerSum expects {self.count} contiguous {self.dtype} values")
+        lib, _lib = self._lib.lib(), self._lib
+        _lib.check(lib.popkv_peer_sum(
+            _lib.ptr(data), _lib.dtype_code(data), self.count, self.rank, self.world, _lib.ptr(self.area.ptrs),
+            ctypes.c_void_p(self.area.own.value), _lib.ptr(self.state), stream))
+
+    def error(self) -> bool:
+        return self.area.error()
+
+    def close(self) -> None:
+        """Unmap the peers and free this rank's area (collective: all ranks call it)."""
+        self.area.close()

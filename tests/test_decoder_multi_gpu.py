@@ -6,7 +6,8 @@
   same way, and the gathered rows are copies.
 * The tensor-parallel output projection and MLP (partial products summed by
   two all-reduces per layer) match it within bf16 tolerance: the partial sums
-  are rounded to bf16 before they are added.  Checked with dense layers, where
+  are rounded to bf16 before they are added.  The peer-memory all-reduce
+  (popkv_peer_sum) and NCCL's give the same bits at two ranks.  Checked with dense layers, where
   a last-bit difference in q cannot swap a near-tied token in the top-k.
 """
 from __future__ import annotations
@@ -51,17 +52,23 @@ def _worker(rank: int, port: int, method: str) -> None:
                                    world=WORLD)
         tensor = LlamaSparseDecoder(weights, method=method, retrieval=retrieval, max_context=170, rank=rank,
                                     world=WORLD, mlp_parallel="tensor")
-        decoders = [single, shard, tensor]
+        tensor_nccl = LlamaSparseDecoder(weights, method=method, retrieval=retrieval, max_context=170,
+                                         rank=rank, world=WORLD, mlp_parallel="tensor", all_reduce="nccl")
+        decoders = [single, shard, tensor, tensor_nccl]
         for d in decoders:
             d.prefill(ids)
         for _ in range(8):
             tok = single.token.clone()
             shard.token.copy_(tok)
             tensor.token.copy_(tok)
+            tensor_nccl.token.copy_(tok)
             want = single.decode().clone()
             got = shard.decode().clone()
             assert torch.equal(got, want), "replicated-MLP shard differs from the single-GPU decode"
             tp = tensor.decode().clone()
+            assert not tensor.all_reduce_error()
+            # Two ranks: both all-reduces round the exact sum of two bf16 values once.
+            assert torch.equal(tp, tensor_nccl.decode()), "peer all-reduce differs from NCCL's"
             if method == "full":
                 rel = float((tp - want).norm() / want.norm())
                 assert rel < 1e-2, rel

@@ -1,10 +1,12 @@
-"""Merge fused with the cross-GPU all-gather over peer memory (needs 2 GPUs).
+"""Merge fused with the cross-GPU all-gather, and the one-shot all-reduce, over
+peer memory (needs 2 GPUs).
 
 Two processes, one per GPU, exchange CUDA IPC handles over a gloo group.  The
 gathered output must equal every rank's popkv_attn_merge of its own rows, bit
 for bit, over several launches (both receive-buffer parities), eagerly and
 inside a replayed CUDA graph; and a KV-head-sharded decode step must equal the
-unsharded step.
+unsharded step.  popkv_peer_sum must equal the fp32 rank-order sum rounded
+once, eagerly and as two sums per replayed graph.
 """
 from __future__ import annotations
 
@@ -117,6 +119,55 @@ def _step_worker(rank: int, port: int) -> None:
         dist.destroy_process_group()
 
 
+def _sum_worker(rank: int, port: int, count: int, dtype_name: str) -> None:
+    import torch.distributed as dist
+
+    from popkv_b200 import _lib
+    from popkv_b200.sharding import PeerSum
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("gloo", rank=rank, world_size=WORLD,
+                            timeout=__import__("datetime").timedelta(seconds=60))
+    dtype = getattr(torch, dtype_name)
+    try:
+        def vec(r: int, step: int) -> torch.Tensor:
+            gen = torch.Generator().manual_seed(100 * step + r)
+            return (torch.randn(count, generator=gen) * (1 + r)).to(dtype)
+
+        peer = PeerSum(count, dtype, dev)
+        data = torch.empty(count, dtype=dtype, device=dev)
+        stream = _lib.stream_of(dev)
+        # Eager: three launches (both receive parities); the sum over ranks in
+        # fp32, rank order, rounded once to the vector's type.
+        for step in range(3):
+            data.copy_(vec(rank, step))
+            peer.launch(data, stream)
+            torch.cuda.synchronize(dev)
+            assert not peer.error()
+            want = sum((vec(r, step).float() for r in range(WORLD)), torch.zeros(count)).to(dtype)
+            assert torch.equal(data.cpu(), want), "eager peer sum differs"
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=side):
+            peer.launch(data, _lib.stream_of(dev))
+            peer.launch(data, _lib.stream_of(dev))  # two sums per replay, as a decode layer issues
+        for step in range(3, 6):
+            data.copy_(vec(rank, step))
+            graph.replay()
+            torch.cuda.synchronize(dev)
+            assert not peer.error()
+            once = sum((vec(r, step).float() for r in range(WORLD)), torch.zeros(count)).to(dtype)
+            want = (once.float() * WORLD).to(dtype)  # every rank holds `once`, summed again
+            assert torch.equal(data.cpu(), want), "graph peer sum differs"
+        del graph
+        peer.close()
+    finally:
+        dist.destroy_process_group()
+
+
 def _need_two_gpus():
     if not torch.cuda.is_available() or torch.cuda.device_count() < WORLD:
         pytest.skip("needs 2 GPUs")
@@ -133,3 +184,11 @@ def test_sharded_step_with_peer_gather_equals_unsharded_step():
     _need_two_gpus()
     import torch.multiprocessing as mp
     mp.spawn(_step_worker, args=(_free_port(),), nprocs=WORLD, join=True)
+
+
+@pytest.mark.parametrize("count,dtype_name", [(4096, "bfloat16"), (16384, "bfloat16"), (2, "float16"),
+                                              (1000, "float32")])
+def test_peer_sum_equals_rank_order_sum(count, dtype_name):
+    _need_two_gpus()
+    import torch.multiprocessing as mp
+    mp.spawn(_sum_worker, args=(_free_port(), count, dtype_name), nprocs=WORLD, join=True)
