@@ -95,6 +95,28 @@ def test_attention_validation_messages(lib):
     assert s == 1 and "shape mismatch" in msg
 
 
+def test_peer_sum_validation_messages(lib):
+    p = ctypes.c_void_p(16)
+    s, msg = _status_and_message(lib, lib.popkv_peer_sum(p, 2, 3, 0, 2, p, p, p, None))  # 3 bf16: 6 bytes
+    assert s == 1 and "whole 4-byte words" in msg
+    s, msg = _status_and_message(lib, lib.popkv_peer_sum(p, 2, 4096, 2, 2, p, p, p, None))
+    assert s == 1 and "invalid rank/world" in msg
+    s, msg = _status_and_message(lib, lib.popkv_peer_sum(p, 7, 4096, 0, 2, p, p, p, None))
+    assert s == 1 and "fp32/fp16/bf16" in msg
+    s, msg = _status_and_message(lib, lib.popkv_peer_sum(ctypes.c_void_p(18), 2, 4096, 0, 2, p, p, p, None))
+    assert s == 1 and "aligned" in msg
+    s, msg = _status_and_message(lib, lib.popkv_peer_sum(None, 2, 4096, 0, 2, p, p, p, None))
+    assert s == 1 and "null pointer" in msg
+
+
+def test_peer_sum_rejects_partial_words_before_any_collective():
+    import torch
+
+    from popkv_b200.sharding import PeerSum
+    with pytest.raises(ValueError, match="multiple of 4 bytes"):
+        PeerSum(3, torch.bfloat16, "cpu")
+
+
 def test_python_surface_validation_without_gpu():
     """The drop-in wrappers raise the reference's ValueErrors before touching CUDA."""
     import torch
