@@ -136,11 +136,32 @@ POPKV_API int popkv_score_encoded(const int32_t* q_sign, const int32_t* q_mag, c
  * head_dim 128 the scores are fp16 (scores_dtype must be POPKV_DTYPE_F16);
  * otherwise fp32 (POPKV_DTYPE_F32).
  *
+ * head_dim 128 with at most 8 query heads per KV head and 16-byte aligned
+ * tile rows (capacity * 2 * 128/dim_group_size bytes a multiple of 16) runs
+ * the fp8 tensor-core scorer: the four counts per representative group are
+ * exact products of +-1/0 fp8 vectors (mma.sync e4m3, fp32 accumulate) and
+ * the fp32 reconstruction is the reference's, so the scores are bit-identical
+ * to the popcount path.  Other shapes run the popcount scorer.
+ *
  * Replaces ext.score and ext.score_dim (csrc/popkv_ext.cu:1208-1313), reached
  * from popkv_cuda.score (popkv_cuda.py:190).
  */
 POPKV_API int popkv_score(const void* queries, int queries_dtype, int64_t batch, int64_t q_heads,
                 int64_t head_dim, const int32_t* k_sign, const int32_t* k_mag,
+                const uint16_t* k_low, const uint16_t* k_delta, int64_t kv_heads,
+                int64_t capacity, const int64_t* head_to_kv, int64_t tokens,
+                int64_t dim_group_size, void* scores, int scores_dtype, void* stream);
+
+/*
+ * popkv_score on the popcount scorer only (one token per thread, __popc per
+ * count), whatever the shape; bit-identical to popkv_score.  Kept for
+ * comparison with the fp8 tensor-core scorer.
+ *
+ * Same interface and reference functions as popkv_score (ext.score,
+ * csrc/popkv_ext.cu:1208-1313, via popkv_cuda.score, popkv_cuda.py:190).
+ */
+POPKV_API int popkv_score_popcount(const void* queries, int queries_dtype, int64_t batch,
+                int64_t q_heads, int64_t head_dim, const int32_t* k_sign, const int32_t* k_mag,
                 const uint16_t* k_low, const uint16_t* k_delta, int64_t kv_heads,
                 int64_t capacity, const int64_t* head_to_kv, int64_t tokens,
                 int64_t dim_group_size, void* scores, int scores_dtype, void* stream);
@@ -347,13 +368,17 @@ POPKV_API int popkv_stage(const void* src, void* dst, int64_t bytes, void* strea
  * export it: `handle` receives the 64-byte CUDA IPC handle.  popkv_peer_open
  * maps another process's handle on the current device (peer access enabled
  * lazily); popkv_peer_close unmaps it; popkv_peer_free frees an allocation of
- * popkv_peer_alloc.  A process cannot open its own handle.
+ * popkv_peer_alloc.  A process cannot open its own handle.  popkv_peer_clear
+ * zeroes `bytes` of this process's area on `stream` (asynchronous): after a
+ * wait for a peer gave up, every rank clears its area and its state words with
+ * no launch in flight on any rank, then all ranks continue from epoch 0.
  *
  * No counterpart in the reference, which gathers with NCCL.
  */
 POPKV_API int popkv_peer_alloc(int64_t bytes, void** ptr, unsigned char* handle);
 POPKV_API int popkv_peer_open(const unsigned char* handle, void** ptr);
 POPKV_API int popkv_peer_close(void* ptr);
+POPKV_API int popkv_peer_clear(void* ptr, int64_t bytes, void* stream);
 POPKV_API int popkv_peer_free(void* ptr);
 
 /*
@@ -370,8 +395,10 @@ POPKV_API int popkv_peer_free(void* ptr);
  * - peer_recv: device array [world] of each rank's receive area. An area is
  *   2 x world x rows x 128 uint64, zero at setup, 8-byte aligned.
  * - own_recv: this rank's area.
- * - state: 3 uint32 in this rank's memory, zero at setup. state[2] becomes 1
- *   when a wait for a peer gave up (the output is then incomplete).
+ * - state: 4 uint32 in this rank's memory, zero at setup. state[0] counts
+ *   launches, state[1] is scratch, state[2] becomes 1 when a wait for a peer
+ *   gave up (the output is then incomplete; sticky until cleared), state[3]
+ *   overrides the poll limit of each wait when nonzero (0: about a second).
  *
  * Every rank must issue the same sequence of these calls on one set of
  * buffers.
@@ -395,8 +422,7 @@ POPKV_API int popkv_attn_merge_gather(const float* partials, int64_t rows, int64
  * - data: count values, 4-byte aligned; count * element size a multiple of 4.
  * - peer_recv / own_recv: as popkv_attn_merge_gather, areas of
  *   2 x world x (count * element size / 4) uint64, zero at setup.
- * - state: 3 uint32 in this rank's memory, zero at setup; state[2] becomes 1
- *   when a wait for a peer gave up.
+ * - state: 4 uint32 in this rank's memory, as popkv_attn_merge_gather.
  *
  * Every rank must issue the same sequence of these calls on one set of
  * buffers.  The reference decodes on one GPU and has no counterpart; this

@@ -29,6 +29,7 @@ _SIGNATURES = {
     "popkv_query_encode": ([_P, _I, _L, _L, _L, _P, _P, _P, _P, _P], _I),
     "popkv_score_encoded": ([_P, _P, _P, _P, _L, _L, _P, _P, _P, _P, _L, _L, _P, _L, _L, _P, _P], _I),
     "popkv_score": ([_P, _I, _L, _L, _L, _P, _P, _P, _P, _L, _L, _P, _L, _L, _P, _I, _P], _I),
+    "popkv_score_popcount": ([_P, _I, _L, _L, _L, _P, _P, _P, _P, _L, _L, _P, _L, _L, _P, _I, _P], _I),
     "popkv_score_tc": ([_P, _I, _L, _L, _L, _P, _P, _P, _P, _L, _L, _P, _L, _L, _P, _I, _P], _I),
     "popkv_topk": ([_P, _I, _L, _L, _L, _L, _L, _P, _L, _P], _I),
     "popkv_score_hist": ([_P, _I, _L, _L, _P, _P, _P, _P, _L, _L, _P, _L, _L, _P, _P, _P], _I),
@@ -45,6 +46,7 @@ _SIGNATURES = {
     "popkv_peer_alloc": ([_L, ctypes.POINTER(ctypes.c_void_p), ctypes.c_char_p], _I),
     "popkv_peer_open": ([ctypes.c_char_p, ctypes.POINTER(ctypes.c_void_p)], _I),
     "popkv_peer_close": ([_P], _I),
+    "popkv_peer_clear": ([_P, _L, _P], _I),
     "popkv_peer_free": ([_P], _I),
     "popkv_attn_merge_gather": ([_P, _L, _L, _L, _I, _L, _L, _P, _P, _P, _P, _P], _I),
     "popkv_peer_sum": ([_P, _I, _L, _L, _L, _P, _P, _P, _P], _I),

@@ -11,6 +11,7 @@ import os
 import shutil
 import subprocess
 import sys
+from concurrent.futures import ThreadPoolExecutor
 from pathlib import Path
 
 PACKAGE = Path(__file__).resolve().parent
@@ -53,18 +54,28 @@ def build(force: bool = False, verbose: bool = False) -> Path:
     obj_dir.mkdir(exist_ok=True)
     LIB_DIR.mkdir(exist_ok=True)
     compiler = nvcc()
-    objects = []
+    objects, commands = [], []
     for source in SOURCES:
         src = CSRC / source
         obj = obj_dir / (src.stem + ".o")
         deps = [src] + list(CSRC.glob("*.cuh")) + list(INCLUDE.glob("*.h"))
         if force or not obj.exists() or any(d.stat().st_mtime > obj.stat().st_mtime for d in deps):
-            cmd = [compiler, *NVCC_FLAGS, "-I", str(INCLUDE), "-I", str(CSRC), "-c", str(src),
-                   "-o", str(obj)]
+            commands.append([compiler, *NVCC_FLAGS, "-I", str(INCLUDE), "-I", str(CSRC), "-c", str(src),
+                             "-o", str(obj)])
+        objects.append(str(obj))
+    # Translation units are independent: compile them in parallel.
+    workers = max(1, min(len(commands), os.cpu_count() or 1))
+    with ThreadPoolExecutor(max_workers=workers) as pool:
+        for cmd in commands:
             if verbose:
                 print(" ".join(cmd), flush=True)
-            subprocess.run(cmd, check=True)
-        objects.append(str(obj))
+        for result in pool.map(lambda c: subprocess.run(c, capture_output=True, text=True), commands):
+            if result.stdout:
+                print(result.stdout, end="", flush=True)
+            if result.stderr:
+                print(result.stderr, end="", file=sys.stderr, flush=True)
+            if result.returncode != 0:
+                raise subprocess.CalledProcessError(result.returncode, result.args)
     tmp = LIB_PATH.with_suffix(".so.tmp")
     cmd = [compiler, "-shared", "-gencode", "arch=compute_100a,code=sm_100a", *objects,
            "-o", str(tmp)]

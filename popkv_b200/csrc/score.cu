@@ -24,6 +24,7 @@
 #include <cstdint>
 
 #include "common.cuh"
+#include "score_tc8.cuh"
 #include "score_impl.cuh"
 #include "score_mma.cuh"
 
@@ -243,8 +244,14 @@ int launch_score128(const void* queries, const int32_t* q_sign, const int32_t* q
                     const uint16_t* k_delta, int64_t kv_heads, int64_t capacity,
                     const int64_t* head_to_kv, int64_t tokens, uint16_t* scores,
                     cudaStream_t stream, int64_t score_stride = -1,
-                    const int64_t* dyn_tokens = nullptr) {
+                    const int64_t* dyn_tokens = nullptr, bool popcount_only = false) {
     const int group_heads = static_cast<int>(q_heads / kv_heads);
+    if (!popcount_only && score_tc8_eligible(G, capacity, group_heads)) {
+        return launch_score128_tc8<G, QT, RAW>(
+            static_cast<const QT*>(queries), q_sign, q_mag, q_low, q_delta, batch, q_heads, k_sign, k_mag,
+            k_low, k_delta, kv_heads, capacity, head_to_kv, tokens, scores, stream,
+            score_stride < 0 ? tokens : score_stride, dyn_tokens);
+    }
     const int64_t tiles = (tokens + kScoreTile - 1) / kScoreTile;
     dim3 grid(static_cast<unsigned>(tiles), static_cast<unsigned>(batch * kv_heads));
     const cudaError_t err = launch_pdl(
@@ -263,21 +270,40 @@ int dispatch_score128(int64_t g, const void* queries, const int32_t* q_sign, con
                       const int32_t* k_sign, const int32_t* k_mag, const uint16_t* k_low,
                       const uint16_t* k_delta, int64_t kv_heads, int64_t capacity,
                       const int64_t* head_to_kv, int64_t tokens, uint16_t* scores,
-                      cudaStream_t stream) {
+                      cudaStream_t stream, bool popcount_only = false) {
     if (g == 16)
         return launch_score128<16, QT, RAW>(queries, q_sign, q_mag, q_low, q_delta, batch, q_heads,
                                             k_sign, k_mag, k_low, k_delta, kv_heads, capacity,
-                                            head_to_kv, tokens, scores, stream);
+                                            head_to_kv, tokens, scores, stream, -1, nullptr,
+                                            popcount_only);
     if (g == 32)
         return launch_score128<32, QT, RAW>(queries, q_sign, q_mag, q_low, q_delta, batch, q_heads,
                                             k_sign, k_mag, k_low, k_delta, kv_heads, capacity,
-                                            head_to_kv, tokens, scores, stream);
+                                            head_to_kv, tokens, scores, stream, -1, nullptr,
+                                            popcount_only);
     return launch_score128<64, QT, RAW>(queries, q_sign, q_mag, q_low, q_delta, batch, q_heads,
                                         k_sign, k_mag, k_low, k_delta, kv_heads, capacity,
-                                        head_to_kv, tokens, scores, stream);
+                                        head_to_kv, tokens, scores, stream, -1, nullptr, popcount_only);
 }
 
 }  // namespace
+
+int score_sm_count() {
+    static int cached[64] = {0};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+    if (!cached[dev]) {
+        int n = 0;
+        if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+        cached[dev] = n;
+    }
+    return cached[dev];
+}
+
+int read_score_tc8_timeouts(uint32_t* count) {
+    const cudaError_t e = cudaMemcpyFromSymbol(count, g_score_tc8_timeouts, sizeof(uint32_t));
+    return e == cudaSuccess ? POPKV_OK : fail(POPKV_ERR_CUDA, "score timeouts: %s", cudaGetErrorString(e));
+}
 
 int check_score_common(int64_t batch, int64_t q_heads, int64_t kv_heads, int64_t capacity,
                        int64_t tokens, int64_t g, const void* head_to_kv) {
@@ -361,12 +387,13 @@ extern "C" int popkv_score_encoded(const int32_t* q_sign, const int32_t* q_mag, 
                                            static_cast<cudaStream_t>(stream));
 }
 
-extern "C" int popkv_score(const void* queries, int queries_dtype, int64_t batch, int64_t q_heads,
-                           int64_t head_dim, const int32_t* k_sign, const int32_t* k_mag,
-                           const uint16_t* k_low, const uint16_t* k_delta, int64_t kv_heads,
-                           int64_t capacity, const int64_t* head_to_kv, int64_t tokens,
-                           int64_t dim_group_size, void* scores, int scores_dtype, void* stream) {
-    using namespace popkv;
+namespace popkv {
+static int score_entry(const void* queries, int queries_dtype, int64_t batch, int64_t q_heads,
+                       int64_t head_dim, const int32_t* k_sign, const int32_t* k_mag,
+                       const uint16_t* k_low, const uint16_t* k_delta, int64_t kv_heads,
+                       int64_t capacity, const int64_t* head_to_kv, int64_t tokens,
+                       int64_t dim_group_size, void* scores, int scores_dtype, void* stream,
+                       bool popcount_only) {
     if (!valid_dtype(queries_dtype)) return fail(POPKV_ERR_INVALID, "queries must be fp32/fp16/bf16");
     int st = check_score_common(batch, q_heads, kv_heads, capacity, tokens, dim_group_size, head_to_kv);
     if (st != POPKV_OK) return st;
@@ -390,16 +417,16 @@ extern "C" int popkv_score(const void* queries, int queries_dtype, int64_t batch
             return dispatch_score128<float, true>(dim_group_size, queries, nullptr, nullptr, nullptr,
                                                   nullptr, batch, q_heads, k_sign, k_mag, k_low,
                                                   k_delta, kv_heads, capacity, head_to_kv, tokens,
-                                                  out, s);
+                                                  out, s, popcount_only);
         if (queries_dtype == POPKV_DTYPE_F16)
             return dispatch_score128<__half, true>(dim_group_size, queries, nullptr, nullptr, nullptr,
                                                    nullptr, batch, q_heads, k_sign, k_mag, k_low,
                                                    k_delta, kv_heads, capacity, head_to_kv, tokens,
-                                                   out, s);
+                                                   out, s, popcount_only);
         return dispatch_score128<__nv_bfloat16, true>(dim_group_size, queries, nullptr, nullptr,
                                                       nullptr, nullptr, batch, q_heads, k_sign,
                                                       k_mag, k_low, k_delta, kv_heads, capacity,
-                                                      head_to_kv, tokens, out, s);
+                                                      head_to_kv, tokens, out, s, popcount_only);
     }
     if (scores_dtype != POPKV_DTYPE_F32)
         return fail(POPKV_ERR_INVALID, "scores for head_dim != 128 are fp32");
@@ -431,6 +458,27 @@ extern "C" int popkv_score(const void* queries, int queries_dtype, int64_t batch
 #undef POPKV_GEN_T
 #undef POPKV_GEN
     return check_launch("popkv_score");
+}
+}  // namespace popkv
+
+extern "C" int popkv_score(const void* queries, int queries_dtype, int64_t batch, int64_t q_heads,
+                           int64_t head_dim, const int32_t* k_sign, const int32_t* k_mag,
+                           const uint16_t* k_low, const uint16_t* k_delta, int64_t kv_heads,
+                           int64_t capacity, const int64_t* head_to_kv, int64_t tokens,
+                           int64_t dim_group_size, void* scores, int scores_dtype, void* stream) {
+    return popkv::score_entry(queries, queries_dtype, batch, q_heads, head_dim, k_sign, k_mag, k_low,
+                              k_delta, kv_heads, capacity, head_to_kv, tokens, dim_group_size, scores,
+                              scores_dtype, stream, false);
+}
+
+extern "C" int popkv_score_popcount(const void* queries, int queries_dtype, int64_t batch, int64_t q_heads,
+                                    int64_t head_dim, const int32_t* k_sign, const int32_t* k_mag,
+                                    const uint16_t* k_low, const uint16_t* k_delta, int64_t kv_heads,
+                                    int64_t capacity, const int64_t* head_to_kv, int64_t tokens,
+                                    int64_t dim_group_size, void* scores, int scores_dtype, void* stream) {
+    return popkv::score_entry(queries, queries_dtype, batch, q_heads, head_dim, k_sign, k_mag, k_low,
+                              k_delta, kv_heads, capacity, head_to_kv, tokens, dim_group_size, scores,
+                              scores_dtype, stream, true);
 }
 
 extern "C" int popkv_score_hist(const void* queries, int queries_dtype, int64_t batch, int64_t q_heads,

@@ -532,7 +532,11 @@ extern "C" int popkv_score_tc(const void* queries, int queries_dtype, int64_t ba
 extern "C" int popkv_score_tc_timeouts(uint32_t* count) {
     using namespace popkv;
     if (!count) return fail(POPKV_ERR_INVALID, "popkv_score_tc_timeouts: null pointer");
-    const cudaError_t e = cudaMemcpyFromSymbol(count, g_score_tc_timeouts, sizeof(uint32_t));
+    uint32_t tc = 0, f8 = 0;
+    const cudaError_t e = cudaMemcpyFromSymbol(&tc, g_score_tc_timeouts, sizeof(uint32_t));
     if (e != cudaSuccess) return fail(POPKV_ERR_CUDA, "popkv_score_tc_timeouts: %s", cudaGetErrorString(e));
+    const int st = read_score_tc8_timeouts(&f8);
+    if (st != POPKV_OK) return st;
+    *count = tc + f8;
     return POPKV_OK;
 }

@@ -23,4 +23,7 @@ int launch_score_mma(const void* queries, int queries_dtype, int64_t batch, int6
                      const int64_t* head_to_kv, int64_t tokens, int64_t dim_group_size, uint16_t* scores,
                      cudaStream_t stream);
 
+// Bounded waits of the fp8 tensor-core scorer (score_tc8.cuh) that gave up since load.
+int read_score_tc8_timeouts(uint32_t* count);
+
 }  // namespace popkv

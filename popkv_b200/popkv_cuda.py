@@ -258,15 +258,18 @@ def score_encoded(
 
 def score(
     queries: torch.Tensor, packed, *, head_to_kv: torch.Tensor, tokens: int,
-    dim_group_size: int = 32, dim_kernel: str | None = None, kernel: str = "popcount",
+    dim_group_size: int = 32, dim_kernel: str | None = None, kernel: str = "auto",
 ) -> torch.Tensor:
     """Return approximate QK scores; the head-dim-128 fast path emits FP16, others FP32.
 
-    ``kernel="tensor_core"`` (head_dim 128, <= 4 query heads per KV head) forms
-    the counts with tcgen05 int8 matrix products; the scores are identical.
+    ``kernel="auto"`` takes the fp8 tensor-core scorer (mma.sync e4m3 counts)
+    where it applies (head_dim 128, <= 8 query heads per KV head) and the
+    popcount scorer elsewhere; ``"popcount"`` forces the popcount scorer and
+    ``"tensor_core"`` (<= 4 query heads per KV head) forms the counts with
+    tcgen05 int8 matrix products.  The scores are identical for all three.
     """
-    if kernel not in ("popcount", "tensor_core"):
-        raise ValueError("kernel must be 'popcount' or 'tensor_core'")
+    if kernel not in ("auto", "popcount", "tensor_core"):
+        raise ValueError("kernel must be 'auto', 'popcount' or 'tensor_core'")
     if queries.ndim != 3 or not queries.is_cuda or not queries.is_contiguous():
         raise ValueError("queries must be contiguous CUDA [batch, query heads, head dim]")
     dim_group_size = _validate_dim_group_size(dim_group_size)
@@ -281,7 +284,8 @@ def score(
     out_dtype = torch.float16 if head_dim == 128 else torch.float32
     scores = torch.empty((batch, q_heads, int(tokens)), device=queries.device, dtype=out_dtype)
     with torch.cuda.device(queries.device):
-        entry = _lib.lib().popkv_score_tc if kernel == "tensor_core" else _lib.lib().popkv_score
+        entry = {"auto": _lib.lib().popkv_score, "popcount": _lib.lib().popkv_score_popcount,
+                 "tensor_core": _lib.lib().popkv_score_tc}[kernel]
         _lib.check(entry(
             _lib.ptr(queries), _lib.dtype_code(queries), batch, q_heads, head_dim,
             *(_lib.ptr(t) for t in packed), kv_heads, capacity, _lib.ptr(mapping), int(tokens),

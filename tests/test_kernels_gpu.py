@@ -217,6 +217,60 @@ def test_tensor_core_score_matches_popcount_kernel(cuda_device, g, batch, tokens
         np.testing.assert_array_equal(bits(mma), want)
 
 
+@pytest.mark.parametrize("g", GROUPS)
+@pytest.mark.parametrize("batch,tokens,group_heads,qdtype,capacity", [
+    (1, 1, 4, torch.bfloat16, 128), (1, 127, 4, torch.bfloat16, 132), (1, 129, 4, torch.float16, 256),
+    (2, 300, 2, torch.float32, 304), (1, 777, 1, torch.bfloat16, 780), (3, 1000, 4, torch.bfloat16, 1024),
+    (1, 515, 5, torch.bfloat16, 520), (2, 260, 8, torch.float16, 264), (1, 1500, 3, torch.bfloat16, 1504),
+    (1, 32768, 4, torch.bfloat16, 32768)])
+def test_fp8_score_matches_popcount_kernel_and_oracle(cuda_device, g, batch, tokens, group_heads, qdtype,
+                                                      capacity):
+    """popkv_score (fp8 tensor-core counts, every capacity here 16-byte aligned per row)
+    == popkv_score_popcount == popkv_score_encoded, bit for bit, and == the oracle."""
+    kv_heads = 2
+    keys, q, mapping, packed = _score_case(cuda_device, g, batch, tokens, q_heads=kv_heads * group_heads,
+                                           kv_heads=kv_heads, seed=tokens + 11 * g + group_heads,
+                                           qdtype=qdtype, capacity=capacity)
+    f8 = C.score(q, packed, head_to_kv=mapping, tokens=tokens, dim_group_size=g)
+    popc = C.score(q, packed, head_to_kv=mapping, tokens=tokens, dim_group_size=g, kernel="popcount")
+    enc = C.query_encode(q, dim_group_size=g)
+    f8_enc = C.score_encoded(enc, packed, head_to_kv=mapping, tokens=tokens, dim_group_size=g)
+    assert torch.equal(f8.view(torch.int16), popc.view(torch.int16))
+    assert torch.equal(f8_enc.view(torch.int16), popc.view(torch.int16))
+    import ctypes
+    from popkv_b200 import _lib
+    timeouts = ctypes.c_uint32(0)
+    _lib.check(_lib.lib().popkv_score_tc_timeouts(ctypes.byref(timeouts)))
+    assert timeouts.value == 0
+    if tokens <= 1500:
+        arr, tag = to_oracle(q)
+        penc = oracle.query_encode(arr, tag, dim_group_size=g)
+        _, want = oracle.score(penc, planes_to_numpy(packed), head_to_kv=mapping.cpu().numpy(),
+                               tokens=tokens, dim_group_size=g, head_dim=128)
+        np.testing.assert_array_equal(bits(f8), want)
+
+
+def test_fp8_score_special_planes(cuda_device):
+    """All-sign, no-sign, all-magnitude and empty-bucket planes (counts at +-16/32/64)."""
+    for g in GROUPS:
+        keys = torch.zeros(2, 256, 128, dtype=torch.bfloat16, device=cuda_device)
+        keys[0, 0::4] = 1.0
+        keys[0, 1::4] = -1.0
+        keys[1, 2::4] = torch.linspace(-3, 3, 128, device=cuda_device).to(torch.bfloat16)
+        keys[1, 3::4, ::2] = 4.0
+        q = torch.zeros(1, 8, 128, dtype=torch.bfloat16, device=cuda_device)
+        q[0, 0] = 1.0
+        q[0, 1] = -1.0
+        q[0, 2, ::3] = 2.0
+        q[0, 3] = torch.linspace(-1, 1, 128, device=cuda_device).to(torch.bfloat16)
+        q[0, 4:] = torch.randn(4, 128, generator=torch.Generator().manual_seed(g)).to(torch.bfloat16).to(cuda_device)
+        mapping = torch.arange(8, device=cuda_device) // 4
+        packed = C.pack_keys(keys, dim_group_size=g, token_capacity=256)
+        f8 = C.score(q, packed, head_to_kv=mapping, tokens=256, dim_group_size=g)
+        popc = C.score(q, packed, head_to_kv=mapping, tokens=256, dim_group_size=g, kernel="popcount")
+        assert torch.equal(f8.view(torch.int16), popc.view(torch.int16)), g
+
+
 def test_tensor_core_score_rejects_unsupported(cuda_device):
     keys, q, mapping, packed = _score_case(cuda_device, 16, 1, 64, q_heads=16, kv_heads=2, seed=1)
     with pytest.raises(RuntimeError, match="at most 4 query heads"):
@@ -463,3 +517,17 @@ def test_score_hist_and_topk_hist_match_separate_kernels(cuda_device, g, tokens,
         assert torch.equal(scores, want_scores)
         assert torch.equal(idx, want_idx)
         assert int(hist.abs().sum()) == 0
+
+
+def test_experimental_topk_hook_shape_and_selection(cuda_device):
+    """popkv.topk as LlamaSparseDecoder.experimental_topk (popkv.py:1091-1093): fp16 [B, QH, T]
+    -> int64 [B, QH, k], the same tokens as select_tokens without its current slot."""
+    gen = torch.Generator().manual_seed(5)
+    scores = torch.randn(1, 32, 5000, generator=gen).to(torch.float16).to(cuda_device)
+    k = 511
+    got = P.topk(scores, k)
+    assert got.dtype == torch.int64 and tuple(got.shape) == (1, 32, k)
+    with_current = P.select_tokens(scores, budget=k + 1, prefix_tokens=5000)
+    assert torch.equal(got[0], with_current[0, :, :k])
+    # The reference then indexes [0] and appends the current slot itself.
+    assert torch.equal(P._append_current(got[0], 5001), with_current[0])  # num_tokens = prefix + 1
