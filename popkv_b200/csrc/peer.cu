@@ -30,6 +30,13 @@ constexpr int kGatherThreads = 128;      // one thread per output element (head_
 constexpr int kGatherMaxSplits = 1024;
 constexpr long long kPolls = 1ll << 20;  // bounded wait for a peer's word (about a second)
 
+// Poll limit of a launch: state[3] when nonzero (a test can make waits run out
+// quickly), else kPolls.
+__device__ __forceinline__ long long poll_limit(const unsigned int* state) {
+    const unsigned int v = state[3];
+    return v ? static_cast<long long>(v) : kPolls;
+}
+
 __device__ __forceinline__ unsigned long long load_relaxed_sys(const unsigned long long* p) {
     unsigned long long v;
     asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
@@ -56,7 +63,10 @@ __device__ __forceinline__ OT from_bits(uint32_t b) {
 
 // Receive area of each rank: [2 parities][world source ranks][rows][128] words.
 // state[0]: launches completed (the epoch), state[1]: CTAs done in this launch,
-// state[2]: set to 1 when a wait for a peer gave up.
+// state[2]: set to 1 when a wait for a peer gave up (sticky), state[3]: poll
+// limit override (0: about a second).  After a wait gave up the ranks' epochs
+// may disagree; every rank must then reset its area and state together
+// (sharding._PeerArea.reset) before the next launch.
 template <typename OT>
 __global__ void __launch_bounds__(kGatherThreads) merge_gather_kernel(
     const float* __restrict__ partials, int64_t splits, int rows, int rank, int world,
@@ -69,6 +79,7 @@ __global__ void __launch_bounds__(kGatherThreads) merge_gather_kernel(
     pdl_wait();
     const unsigned int epoch = state[0] + 1u;
     const int64_t par = epoch & 1u;
+    const long long limit = poll_limit(state);
 
     // Log-sum-exp merge of row `blockIdx.x`, in the order of attn_merge_kernel.
     const int64_t row = blockIdx.x;
@@ -139,7 +150,7 @@ __global__ void __launch_bounds__(kGatherThreads) merge_gather_kernel(
         unsigned long long w = load_relaxed_sys(src);
         long long polls = 0;
         while (static_cast<unsigned int>(w >> 32) != epoch) {
-            if (++polls > kPolls) {
+            if (++polls > limit) {
                 ok = false;
                 break;
             }
@@ -181,6 +192,7 @@ __global__ void __launch_bounds__(kSumThreads) peer_sum_kernel(
     __syncthreads();
     const unsigned int epoch = state[0] + 1u;
     const int64_t par = epoch & 1u;
+    const long long limit = poll_limit(state);
     const int64_t i = static_cast<int64_t>(blockIdx.x) * kSumThreads + threadIdx.x;
     if (i < words) {
         const uint32_t mine = data[i];
@@ -199,7 +211,7 @@ __global__ void __launch_bounds__(kSumThreads) peer_sum_kernel(
                 unsigned long long w = load_relaxed_sys(src);
                 long long polls = 0;
                 while (static_cast<unsigned int>(w >> 32) != epoch) {
-                    if (++polls > kPolls) {
+                    if (++polls > limit) {
                         ok = false;
                         break;
                     }
@@ -266,6 +278,14 @@ extern "C" int popkv_peer_close(void* ptr) {
     using namespace popkv;
     const cudaError_t e = cudaIpcCloseMemHandle(ptr);
     if (e != cudaSuccess) return fail(POPKV_ERR_CUDA, "popkv_peer_close: %s", cudaGetErrorString(e));
+    return POPKV_OK;
+}
+
+extern "C" int popkv_peer_clear(void* ptr, int64_t bytes, void* stream) {
+    using namespace popkv;
+    if (!ptr || bytes <= 0) return fail(POPKV_ERR_INVALID, "popkv_peer_clear: invalid arguments");
+    const cudaError_t e = cudaMemsetAsync(ptr, 0, static_cast<size_t>(bytes), static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return fail(POPKV_ERR_CUDA, "popkv_peer_clear: %s", cudaGetErrorString(e));
     return POPKV_OK;
 }
 

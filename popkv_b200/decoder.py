@@ -558,6 +558,12 @@ class LlamaSparseDecoder:
         with torch.cuda.device(self.device):
             side = torch.cuda.Stream(self.device)
             self.position.zero_()
+            if self.world > 1:
+                # Every rank reaches the eager warm-up together, so no peer
+                # all-reduce of it waits on a rank that is still building.
+                import torch.distributed as dist
+                torch.cuda.synchronize(self.device)
+                dist.barrier(group=self.group)
             side.wait_stream(torch.cuda.current_stream(self.device))
             self._launch(side)  # sets kernel attributes, cuBLAS workspaces
             side.synchronize()
@@ -703,6 +709,7 @@ class LlamaSparseDecoder:
             self.token.copy_(ids)
         self.step()
         self.logits_f32.copy_(self.logits)
+        self._check_collectives()
         return self.logits_f32
 
     def generate(self, steps: int) -> torch.Tensor:
@@ -714,11 +721,29 @@ class LlamaSparseDecoder:
         for i in range(steps):
             self.step()
             out[:, i].copy_(self.token)
-        return out.cpu()
+        tokens = out.cpu()
+        self._check_collectives()
+        return tokens
 
     def all_reduce_error(self) -> bool:
         """True when a peer all-reduce gave up waiting for a peer (tensor mode)."""
         return self._peer_sum is not None and self._peer_sum.error()
+
+    def _check_collectives(self) -> None:
+        if self.all_reduce_error():
+            raise RuntimeError(
+                "a peer all-reduce gave up waiting for another rank: this step's outputs are invalid; "
+                "call reset_collectives() on every rank before decoding again")
+
+    def reset_collectives(self) -> None:
+        """Clear the peer all-reduce's areas and launch state on every rank (collective).
+
+        After ``all_reduce_error()`` the ranks' launch epochs may disagree, so
+        every later all-reduce would give up too; all ranks call this with no
+        step in flight, then decode again.
+        """
+        if self._peer_sum is not None:
+            self._peer_sum.reset()
 
     def close(self) -> None:
         """Release the CUDA graph and the peer areas (before the process group is

@@ -95,6 +95,7 @@ class _PeerArea:
         self.rank = dist.get_rank(group)
         self.device = torch.device(device)
         lib = _lib.lib()
+        self.nbytes = int(nbytes)
         ptr = ctypes.c_void_p()
         handle = ctypes.create_string_buffer(64)
         with torch.cuda.device(self.device):
@@ -114,11 +115,30 @@ class _PeerArea:
                 self._opened.append(p)
                 bases.append(p.value)
         self.ptrs = torch.tensor(bases, dtype=torch.int64, device=self.device)
-        # Launch epoch, CTAs done in the launch, wait-gave-up flag.
+        # Launch epoch, CTAs done in the launch, wait-gave-up flag, poll limit
+        # override (0: the kernels' default of about a second).
         self.state = torch.zeros(4, dtype=torch.int32, device=self.device)
 
     def error(self) -> bool:
         return bool(int(self.state[2].item()))
+
+    def reset(self) -> None:
+        """Zero this rank's area and launch state, in step with every peer (collective).
+
+        After a wait gave up (``error()``), the ranks' launch epochs may differ
+        and every later exchange would time out; all ranks call ``reset`` with
+        no launch in flight to start again from epoch 0.
+        """
+        import torch.distributed as dist
+        import ctypes
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)  # no peer still writes into this area
+        with torch.cuda.device(self.device):
+            self._lib.check(self._lib.lib().popkv_peer_clear(
+                ctypes.c_void_p(self.own.value), self.nbytes, self._lib.stream_of(self.device)))
+            self.state[:3].zero_()
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)  # every area is clean before any rank launches again
 
     def close(self) -> None:
         """Unmap the peers and free this rank's area (collective: all ranks call it)."""
@@ -172,6 +192,10 @@ class PeerGather:
     def error(self) -> bool:
         return self.area.error()
 
+    def reset(self) -> None:
+        """Clear the area and launch state on every rank together (collective), after ``error()``."""
+        self.area.reset()
+
     def close(self) -> None:
         """Unmap the peers and free this rank's area (collective: all ranks call it)."""
         self.area.close()
@@ -182,8 +206,8 @@ class PeerSum:
 
     For the tensor-parallel decode's partial products: one launch, no NCCL
     kernel, and the next kernel of the step may start filling its weight ring
-    while the words cross NVLink.  Constructed collectively for vectors of at
-    most ``count`` values of ``dtype``; every rank must launch the same
+    while the words cross NVLink.  Constructed collectively for vectors of
+    exactly ``count`` values of ``dtype``; every rank must launch the same
     sequence of sums.  The sum is taken in fp32 in rank order and rounded
     once, so all ranks hold identical bits.
     """
@@ -216,6 +240,10 @@ class PeerSum:
 
     def error(self) -> bool:
         return self.area.error()
+
+    def reset(self) -> None:
+        """Clear the area and launch state on every rank together (collective), after ``error()``."""
+        self.area.reset()
 
     def close(self) -> None:
         """Unmap the peers and free this rank's area (collective: all ranks call it)."""

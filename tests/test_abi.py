@@ -175,3 +175,18 @@ def test_ctypes_signatures_match_the_header():
         count = 0 if params in ("", "void") else params.count(",") + 1
         assert name in _lib._SIGNATURES, name
         assert len(_lib._SIGNATURES[name][0]) == count, name
+
+
+def test_reference_hooks_bind():
+    """The hook callables accept the reference decoder's exact calls (popkv.py:1083-1092)."""
+    import inspect
+
+    from popkv_b200 import popkv as P
+    from popkv_b200 import popkv_cuda as C
+    # scorer(encoded_query, packed, head_to_kv=..., tokens=..., dim_group_size=..., dim_kernel=...)
+    inspect.signature(C.score_encoded).bind(
+        object(), object(), head_to_kv=object(), tokens=1, dim_group_size=16, dim_kernel="g16")
+    # experimental_topk(scores, k), positional
+    inspect.signature(P.topk).bind(object(), 7)
+    with pytest.raises(TypeError):
+        inspect.signature(P.topk).bind(object())

@@ -13,10 +13,12 @@ from popkv_b200.workloads import decode_inputs, head_to_kv
 pytestmark = pytest.mark.gpu
 
 
+@pytest.mark.parametrize("host_io", [False, True])
 @pytest.mark.parametrize("select", ["hist", "radix"])
 @pytest.mark.parametrize("preset,context,budget", [("popkv-q", 2048, 256), ("popkv-s", 3000, 700),
-                                                   ("popkv-normal", 777, 1000)])
-def test_graph_step_matches_oracle(cuda_device, preset, context, budget, select):
+                                                   ("popkv-normal", 777, 1000),
+                                                   ("popkv-q", 32768, 4096)])  # the benchmark's step
+def test_graph_step_matches_oracle(cuda_device, preset, context, budget, select, host_io):
     tg, g = P.POPKV_PRESETS[preset]
     x = decode_inputs(context=context, seed=11, dtype="bf16")
     dev = cuda_device
@@ -24,14 +26,18 @@ def test_graph_step_matches_oracle(cuda_device, preset, context, budget, select)
     keys, values = to(x.keys[0]), to(x.values[0])
     cache = P.build_popkv_cache(keys, group_size=tg, dim_group_size=g, reserve_tokens=8)
     mapping = torch.from_numpy(head_to_kv(32, 8)).to(dev)
-    step = SparseAttentionStep(cache, keys, values, mapping, budget=budget, select=select)
+    step = SparseAttentionStep(cache, keys, values, mapping, budget=budget, select=select, host_io=host_io)
     assert step.select == select
     q_host = to(x.queries).cpu().pin_memory()
     k_host = to(x.current_keys[0]).cpu().pin_memory()
     v_host = to(x.current_values[0]).cpu().pin_memory()
-    out = step(q_host, k_host, v_host).clone()
-    again = step(q_host, k_host, v_host).clone()
-    assert torch.equal(out, again)
+    out = step(q_host, k_host, v_host)
+    torch.cuda.current_stream(dev).synchronize()  # host_io: the result lands in pinned host memory
+    out = out.clone()
+    again = step(q_host, k_host, v_host)
+    torch.cuda.current_stream(dev).synchronize()
+    assert torch.equal(out, again.clone())
+    out = out.to(dev)
     eager = P.popkv_attention(to(x.queries[0]), keys, values, to(x.current_keys[0]),
                               to(x.current_values[0]), cache, mapping, budget=budget)
     # The graph's attention kernels sum in another order than the eager chain:

@@ -6,7 +6,9 @@ gathered output must equal every rank's popkv_attn_merge of its own rows, bit
 for bit, over several launches (both receive-buffer parities), eagerly and
 inside a replayed CUDA graph; and a KV-head-sharded decode step must equal the
 unsharded step.  popkv_peer_sum must equal the fp32 rank-order sum rounded
-once, eagerly and as two sums per replayed graph.
+once, eagerly, as two sums per replayed graph, and after a collective reset.
+On one GPU, both kernels' bounded waits are made to run out (a peer area that
+nobody writes) and must report it and return.
 """
 from __future__ import annotations
 
@@ -163,6 +165,17 @@ def _sum_worker(rank: int, port: int, count: int, dtype_name: str) -> None:
             want = (once.float() * WORLD).to(dtype)  # every rank holds `once`, summed again
             assert torch.equal(data.cpu(), want), "graph peer sum differs"
         del graph
+        # A collective reset returns both ranks to epoch 0 with clean areas; the
+        # next sums are exact again.
+        peer.reset()
+        assert peer.state.tolist()[:3] == [0, 0, 0]
+        for step in range(6, 8):
+            data.copy_(vec(rank, step))
+            peer.launch(data, stream)
+            torch.cuda.synchronize(dev)
+            assert not peer.error()
+            want = sum((vec(r, step).float() for r in range(WORLD)), torch.zeros(count)).to(dtype)
+            assert torch.equal(data.cpu(), want), "peer sum after reset differs"
         peer.close()
     finally:
         dist.destroy_process_group()
@@ -192,3 +205,66 @@ def test_peer_sum_equals_rank_order_sum(count, dtype_name):
     _need_two_gpus()
     import torch.multiprocessing as mp
     mp.spawn(_sum_worker, args=(_free_port(), count, dtype_name), nprocs=WORLD, join=True)
+
+
+# ---------------------------------------------------------------------------
+# Bounded waits that run out, on one GPU.  Rank 0 of a world of 2 whose "peer"
+# area is a second local buffer that nobody writes: every poll of the peer's
+# words fails, the waits give up after the poll limit in state[3], the kernel
+# sets state[2] and returns, and the stream stays usable.  No GPU fault or hang
+# is involved: the waits are bounded and the status is read on the host.
+# ---------------------------------------------------------------------------
+
+def _lonely_areas(dev, words_per_rank: int, poll_limit: int):
+    own = torch.zeros(2 * WORLD * words_per_rank, dtype=torch.int64, device=dev)
+    silent_peer = torch.zeros_like(own)
+    ptrs = torch.tensor([own.data_ptr(), silent_peer.data_ptr()], dtype=torch.int64, device=dev)
+    state = torch.tensor([0, 0, 0, poll_limit], dtype=torch.int32, device=dev)
+    return own, silent_peer, ptrs, state
+
+
+def test_peer_sum_wait_runs_out_and_reports(cuda_device):
+    import ctypes
+
+    from popkv_b200 import _lib
+    lib, dev = _lib.lib(), cuda_device
+    count = 4096
+    data = torch.randn(count, device=dev).to(torch.bfloat16)
+    own, silent_peer, ptrs, state = _lonely_areas(dev, count // 2, poll_limit=2000)
+    _lib.check(lib.popkv_peer_sum(_lib.ptr(data), _lib.BF16, count, 0, WORLD, _lib.ptr(ptrs),
+                                  ctypes.c_void_p(own.data_ptr()), _lib.ptr(state), _lib.stream_of(dev)))
+    torch.cuda.synchronize(dev)
+    assert state.tolist()[:3] == [1, 0, 1]  # the launch ended, its epoch advanced, the flag is set
+    # This rank's words went out to the silent peer's area with epoch 1.
+    assert int((silent_peer.view(2, WORLD, -1)[1, 0] >> 32).eq(1).sum()) == count // 2
+    # The stream and the context still work: a one-rank sum is the identity.
+    again = data.clone()
+    solo_state = torch.zeros(4, dtype=torch.int32, device=dev)
+    solo_ptrs = torch.tensor([own.data_ptr()], dtype=torch.int64, device=dev)
+    _lib.check(lib.popkv_peer_sum(_lib.ptr(again), _lib.BF16, count, 0, 1, _lib.ptr(solo_ptrs),
+                                  ctypes.c_void_p(own.data_ptr()), _lib.ptr(solo_state), _lib.stream_of(dev)))
+    torch.cuda.synchronize(dev)
+    assert torch.equal(again, data) and solo_state.tolist()[:3] == [1, 0, 0]
+
+
+def test_merge_gather_wait_runs_out_and_reports(cuda_device):
+    import ctypes
+
+    from popkv_b200 import _lib
+    lib, dev = _lib.lib(), cuda_device
+    rows, splits = 8, 4
+    partials = _partials(0, rows, splits).to(dev)
+    own, silent_peer, ptrs, state = _lonely_areas(dev, rows * 128, poll_limit=2000)
+    out = torch.empty(WORLD * rows, 128, dtype=torch.bfloat16, device=dev)
+    for launch in (1, 2):  # both receive parities
+        _lib.check(lib.popkv_attn_merge_gather(_lib.ptr(partials), rows, splits, 128, _lib.BF16, 0, WORLD,
+                                               _lib.ptr(ptrs), ctypes.c_void_p(own.data_ptr()), _lib.ptr(state),
+                                               _lib.ptr(out), _lib.stream_of(dev)))
+        torch.cuda.synchronize(dev)
+        assert state.tolist()[:3] == [launch, 0, 1]
+    # The rank's own rows are still merged correctly.
+    want = torch.empty(rows, 128, dtype=torch.bfloat16, device=dev)
+    _lib.check(lib.popkv_attn_merge(_lib.ptr(partials), rows, splits, 128, _lib.ptr(want), _lib.BF16,
+                                    _lib.stream_of(dev)))
+    torch.cuda.synchronize(dev)
+    assert torch.equal(out[:rows], want)
