@@ -827,7 +827,129 @@ def run_reference(args, world, rank):
                                    "source that cannot travel to this host)"},
         "e2e": {"value": round(ms, 3), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
+    result["reference_gpu"] = reference_gpu_stages(args)
     print(json.dumps(result), flush=True)
+
+
+def reference_gpu_stages(args) -> dict:
+    """The reference's own CUDA kernels on this GPU, beside this package's, timed the same way.
+
+    The reference's extension (csrc/popkv_ext.cu, compiled from its sources by
+    oracle/build_ref.py with its own flags) runs the decode branch's GPU
+    stages as the reference launches them (popkv.py:1078-1099): eager calls,
+    device time from CUDA events over back-to-back calls, cycling over 8 copies
+    of the keys and planes (more than L2).  The split attention is Triton
+    source (sparse_kernels.py:237-318) that does not travel to the GPU host.
+    """
+    try:
+        import torch
+        from oracle.build_ref import load_reference_extension
+        if not torch.cuda.is_available():
+            return {"unavailable": "no CUDA device"}
+        ref = load_reference_extension()
+    except Exception as exc:  # noqa: BLE001  (a missing or stale build is reported, not fatal)
+        return {"unavailable": f"reference extension failed to load: {exc}"}
+    if ref is None:
+        return {"unavailable": "reference extension not built (the package was built without a reference checkout)"}
+    from popkv_b200 import popkv as P
+    from popkv_b200 import popkv_cuda as C
+    from popkv_b200.workloads import decode_inputs, head_to_kv
+    dev = torch.device("cuda", 0)
+    tg, g = P.POPKV_PRESETS[args.preset]
+    T, k, copies = args.context, min(args.budget - 1, args.context), 8
+    x = decode_inputs(batch=1, context=T, seed=0, dtype="bf16")
+    keys = [torch.from_numpy(x.keys[0]).to(torch.bfloat16).to(dev).contiguous() for _ in range(copies)]
+    q = torch.from_numpy(x.queries).to(torch.bfloat16).to(dev).contiguous()
+    mapping = torch.from_numpy(head_to_kv(32, 8)).to(dev)
+    pack = (lambda kk: ref.pack(kk, T, tg)) if g == 32 else (lambda kk: ref.pack_dim(kk, T, g, tg))
+    r_planes = [pack(kk) for kk in keys]
+    r_enc = (torch.empty((1, 32, 4), dtype=torch.int32, device=dev), torch.empty((1, 32, 4), dtype=torch.int32, device=dev),
+             torch.empty((1, 32, 128 // g), device=dev), torch.empty((1, 32, 128 // g), device=dev))
+    ref.query_encode_out(q, *r_enc, g)
+    r_scores = [ref.score_encoded(*r_enc, *pl, mapping, T, g) for pl in r_planes]
+    o_planes = [C.pack_keys(kk, token_capacity=T, token_group_size=tg, dim_group_size=g) for kk in keys]
+    o_enc = C.query_encode(q, dim_group_size=g)
+    o_scores = [C.score_encoded(o_enc, pl, head_to_kv=mapping, tokens=T, dim_group_size=g) for pl in o_planes]
+    torch.cuda.synchronize(dev)
+
+    def timed(fn, reps=60):
+        for i in range(5):
+            fn(i)
+        torch.cuda.synchronize(dev)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for i in range(reps):
+            fn(i)
+        b.record()
+        torch.cuda.synchronize(dev)
+        return round(a.elapsed_time(b) * 1e3 / reps, 2)
+
+    def r_chain(i):
+        ref.query_encode_out(q, *r_enc, g)
+        sc = ref.score_encoded(*r_enc, *r_planes[i % copies], mapping, T, g)
+        torch.topk(sc, k, dim=-1, sorted=False)
+
+    def o_chain(i):
+        enc = C.query_encode(q, dim_group_size=g)
+        sc = C.score_encoded(enc, o_planes[i % copies], head_to_kv=mapping, tokens=T, dim_group_size=g)
+        P.topk(sc, k)
+
+    def graph_timed(fn, reps=20, replays=10):
+        """Device time per call with `reps` calls captured in one CUDA graph (no host gaps)."""
+        for i in range(3):
+            fn(i)
+        torch.cuda.synchronize(dev)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            for i in range(reps):
+                fn(i)
+        graph.replay()
+        torch.cuda.synchronize(dev)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(replays):
+            graph.replay()
+        b.record()
+        torch.cuda.synchronize(dev)
+        return round(a.elapsed_time(b) * 1e3 / (replays * reps), 2)
+
+    reference_graph = {
+        "query_encode": graph_timed(lambda i: ref.query_encode_out(q, *r_enc, g)),
+        "score_encoded": graph_timed(lambda i: ref.score_encoded(*r_enc, *r_planes[i % copies], mapping, T, g)),
+        "topk": graph_timed(lambda i: torch.topk(r_scores[i % copies], k, dim=-1, sorted=False)),
+        "encode_score_topk": graph_timed(r_chain),
+    }
+    ours_graph = {
+        "query_encode": graph_timed(lambda i: C.query_encode(q, dim_group_size=g)),
+        "score_encoded": graph_timed(lambda i: C.score_encoded(o_enc, o_planes[i % copies], head_to_kv=mapping,
+                                                               tokens=T, dim_group_size=g)),
+        "topk": graph_timed(lambda i: P.topk(o_scores[i % copies], k)),
+        "encode_score_topk": graph_timed(o_chain),
+    }
+    reference = {
+        "prepack": timed(lambda i: pack(keys[i % copies]), reps=20),
+        "query_encode": timed(lambda i: ref.query_encode_out(q, *r_enc, g)),
+        "score_encoded": timed(lambda i: ref.score_encoded(*r_enc, *r_planes[i % copies], mapping, T, g)),
+        "topk": timed(lambda i: torch.topk(r_scores[i % copies], k, dim=-1, sorted=False)),
+        "encode_score_topk": timed(r_chain),
+    }
+    ours = {
+        "prepack": timed(lambda i: C.pack_keys(keys[i % copies], token_capacity=T, token_group_size=tg,
+                                               dim_group_size=g), reps=20),
+        "query_encode": timed(lambda i: C.query_encode(q, dim_group_size=g)),
+        "score_encoded": timed(lambda i: C.score_encoded(o_enc, o_planes[i % copies], head_to_kv=mapping, tokens=T,
+                                                         dim_group_size=g)),
+        "topk": timed(lambda i: P.topk(o_scores[i % copies], k)),
+        "encode_score_topk": timed(o_chain),
+    }
+    return {"unit": "us per call (CUDA events, 8 copies > L2)", "preset": args.preset, "context": T,
+            "budget": args.budget, "reference_eager": reference, "ours_eager": ours,
+            "reference_graph": reference_graph, "ours_graph": ours_graph,
+            "timing": "eager: back-to-back calls as the reference launches them (host overhead included when the "
+                      "GPU waits for it); graph: the same calls captured in a CUDA graph (device time)",
+            "attention": "unavailable: the reference's split attention is Triton source (sparse_kernels.py:237-318) "
+                         "that does not travel to the GPU host",
+            "build": "oracle/build_ref.py: csrc/popkv_ext.cu + popkv_ext.cpp, -O3 --use_fast_math, sm_100a"}
 
 
 # ---------------------------------------------------------------------------

@@ -81,6 +81,8 @@ def build(reference: str | os.PathLike | None = None, verbose: bool = False) -> 
     res = subprocess.run(link, capture_output=True, text=True)
     if res.returncode != 0:
         raise RuntimeError(f"reference extension link failed:\n{res.stderr[-4000:]}")
+    for obj in (cu_obj, cpp_obj):  # only the module travels to the GPU host
+        obj.unlink(missing_ok=True)
     return out
 
 
