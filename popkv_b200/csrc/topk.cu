@@ -776,23 +776,35 @@ __global__ void __launch_bounds__(kHistThreads) topk_hist_kernel(
 }
 
 // ---------------------------------------------------------------------------
-// fp16 top-k, one thread-block cluster of CPR CTAs per row, three cluster
+// fp16 top-k, one thread-block cluster of CPR CTAs per row, two cluster
 // barriers in all.
 //
 // Thread t of rank r owns the contiguous keys [r*S + t*PER, r*S + (t+1)*PER),
-// S = 512*PER, held in registers two to a word.  (1) Every CTA counts its keys'
-// top 11 bits in shared memory; barrier A; every CTA then reads all CPR
-// histograms (one 16-byte DSMEM load per rank and thread: thread t sums the
-// four bins at descending positions 4t..4t+3) and scans them itself, so all
-// CTAs pick the same digit b1 without a further exchange.  (2) The keys of
-// digit b1 are counted by their low 5 bits into a 32-bin histogram; barrier B;
-// warp 0 of every CTA reads the CPR small histograms and picks the threshold
-// key and how many keys equal to it are taken.  (3) A block scan of each
-// thread's (greater, equal) counts gives positions inside the CTA; each CTA
-// stores its totals into the higher ranks' shared memory; barrier C; each CTA
-// adds the totals of the lower ranks and writes its winners in ascending
-// index order.  No DSMEM access follows barrier C, so CTAs exit freely.
+// S = 512*PER, held in registers two to a word.
+// (1) Every CTA counts its keys' top 11 bits in shared memory; barrier A.
+//     Every CTA then reads all CPR histograms (one 16-byte DSMEM load per rank
+//     and thread: thread t sums the four bins at descending positions
+//     4t..4t+3) and scans them itself, so all CTAs pick the same digit b1.
+// (2) Each CTA counts its keys above b1 and, by their low 5 bits, its keys in
+//     b1 (a 32-bin histogram), and stores both into every CTA's shared memory
+//     (its own row of `hist2_all`); barrier B.  Warp 0 of every CTA then
+//     reads its local copy of the CPR rows, picks the threshold key and how
+//     many keys equal to it are taken, and sums how many keys above and equal
+//     to the threshold the lower ranks hold: the CTA's output offset, with no
+//     further exchange.
+// (3) A block scan of each thread's (greater, equal) counts gives positions
+//     inside the CTA.  The CTA's winners fill one contiguous range of the
+//     output; they are staged in shared memory by position and written out
+//     with coalesced stores.
+// Every DSMEM access (the reads of the 11-bit histograms, the stores of the
+// small ones) comes before barrier B, the last cluster-wide wait, so no CTA
+// exits while a peer may still touch its shared memory.
 // ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t popcount_mask(uint32_t m) { return static_cast<uint32_t>(__popc(m)); }
+__device__ __forceinline__ uint32_t popcount_mask(unsigned long long m) { return static_cast<uint32_t>(__popcll(m)); }
+__device__ __forceinline__ int lowest_bit(uint32_t m) { return __ffs(m) - 1; }
+__device__ __forceinline__ int lowest_bit(unsigned long long m) { return __ffsll(m) - 1; }
+
 __device__ __forceinline__ uint32_t cta_exclusive_scan32(uint32_t x, uint32_t* warp_sums, uint32_t& total) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     uint32_t incl = x;
@@ -821,17 +833,24 @@ __device__ __forceinline__ uint32_t cta_exclusive_scan32(uint32_t x, uint32_t* w
 }
 
 template <int CPR, int PER>
-__global__ void __launch_bounds__(kClusterThreads) topk16_cluster_kernel(
+__global__ void __launch_bounds__(kClusterThreads, PER <= 16 ? 4 : 1) topk16_cluster_kernel(
     const uint16_t* __restrict__ scores, int64_t tokens, int64_t row_stride, int64_t k,
     int64_t current_index, int64_t* __restrict__ out, int64_t out_stride, bool vec_ok,
     const int64_t* __restrict__ dyn_tokens) {
     static_assert(PER % 8 == 0 && PER <= 64, "PER keys per thread, whole uint4 loads");
+    static_assert(CPR <= 8, "at most 8 ranks per cluster");
     constexpr int64_t kSlice = static_cast<int64_t>(kClusterThreads) * PER;
+    // Winners staged by output position for coalesced stores (32 KiB at 32 keys
+    // per thread); with 64 keys per thread they are stored directly.
+    constexpr bool kStaged = PER <= 32;
+    constexpr int kStageSlots = kStaged ? kClusterThreads * PER : 1;
+    constexpr int kRow2 = 33;
     __shared__ __align__(16) uint32_t hist[kHistBins];
-    __shared__ uint32_t hist2[32];
+    __shared__ __align__(16) uint16_t stage[kStageSlots];
+    __shared__ uint32_t hist2[kRow2];  // bins 0..31: keys in digit b1 by low 5 bits; [32]: keys above b1
+    __shared__ uint32_t hist2_all[CPR * kRow2];  // row c: rank c's `hist2`
     __shared__ uint32_t warp_sums[kClusterWarps + 1];
-    __shared__ uint32_t lower_totals[CPR];  // packed (gt << 16) | eq of each lower rank
-    __shared__ uint32_t sel_b1, sel_above, sel_thr, sel_need;
+    __shared__ uint32_t sel_b1, sel_above, sel_thr, sel_need, sel_gt_before, sel_eq_before;
 
     POPKV_TOPK_PHASE(0);
     pdl_wait();
@@ -854,16 +873,18 @@ __global__ void __launch_bounds__(kClusterThreads) topk16_cluster_kernel(
     const uint32_t kk = static_cast<uint32_t>(k);
 
     for (int b = tid; b < kHistBins; b += kClusterThreads) hist[b] = 0;
-    if (tid < 32) hist2[tid] = 0;
-    if (tid < CPR) lower_totals[tid] = 0;
+    if (tid < kRow2) hist2[tid] = 0;
     if (tid == 0) {  // defaults; the scans below always overwrite them when k <= tokens
         sel_b1 = 0;
         sel_above = 0;
         sel_thr = 0;
         sel_need = 0;
+        sel_gt_before = 0;
+        sel_eq_before = 0;
     }
 
-    const int64_t base = static_cast<int64_t>(rank) * kSlice + static_cast<int64_t>(tid) * PER;
+    const int64_t cta_base = static_cast<int64_t>(rank) * kSlice;
+    const int64_t base = cta_base + static_cast<int64_t>(tid) * PER;
     const uint16_t* src = scores + row * row_stride + base;
     const int64_t left = tokens - base;
     const int lim = left <= 0 ? 0 : (left >= PER ? PER : static_cast<int>(left));
@@ -926,68 +947,108 @@ __global__ void __launch_bounds__(kClusterThreads) topk16_cluster_kernel(
     const uint32_t b1 = sel_b1;
     POPKV_TOPK_PHASE(4);
 
-    // (2) low 5 bits of the keys in digit b1.
+    // (2) keys above digit b1, and the low 5 bits of the keys in it.
+    uint32_t above_b1 = 0;
 #pragma unroll
-    for (int e = 0; e < PER; ++e)
-        if (e < lim && (key_of(e) >> 5) == b1) atomicAdd(&hist2[key_of(e) & 31u], 1u);
-    cluster.sync();  // B: every CTA's small histogram is complete
+    for (int e = 0; e < PER; ++e) {
+        if (e < lim) {
+            above_b1 += (key_of(e) >> 5) > b1;
+            if ((key_of(e) >> 5) == b1) atomicAdd(&hist2[key_of(e) & 31u], 1u);
+        }
+    }
+    above_b1 = __reduce_add_sync(0xFFFFFFFFu, above_b1);
+    if ((tid & 31) == 0 && above_b1) atomicAdd(&hist2[32], above_b1);
+    __syncthreads();
+    if (tid < CPR * kRow2)  // thread (c, i): entry i into rank c's copy
+        cluster.map_shared_rank(hist2_all, tid / kRow2)[rank * kRow2 + tid % kRow2] = hist2[tid % kRow2];
+    cluster.sync();  // B: every rank's row has arrived in every CTA
     if (tid < 32) {
-        uint32_t v[CPR];
+        // Lane i: bin 31 - i, over all ranks and over the lower ranks.
+        uint32_t c2 = 0, low = 0, low_above = 0;
 #pragma unroll
-        for (int c = 0; c < CPR; ++c) v[c] = cluster.map_shared_rank(hist2, c)[31 - tid];
-        uint32_t c2 = 0;
-#pragma unroll
-        for (int c = 0; c < CPR; ++c) c2 += v[c];
-        uint32_t incl = c2;
+        for (int c = 0; c < CPR; ++c) {
+            const uint32_t h = hist2_all[c * kRow2 + 31 - tid];
+            c2 += h;
+            if (c < rank) {
+                low += h;
+                low_above += hist2_all[c * kRow2 + 32];
+            }
+        }
+        uint32_t incl = c2, low_incl = low;
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
             const uint32_t y = __shfl_up_sync(0xFFFFFFFFu, incl, o);
-            if (tid >= o) incl += y;
+            const uint32_t z = __shfl_up_sync(0xFFFFFFFFu, low_incl, o);
+            if (tid >= o) {
+                incl += y;
+                low_incl += z;
+            }
         }
         const uint32_t remaining = kk - sel_above;
-        const uint32_t excl = incl - c2;
-        if (excl < remaining && incl >= remaining) {
+        if (incl - c2 < remaining && incl >= remaining) {
             sel_thr = (b1 << 5) | (31u - static_cast<uint32_t>(tid));
-            sel_need = remaining - excl;
+            sel_need = remaining - (incl - c2);
+            // Keys of lower ranks above the threshold: above digit b1, or in b1
+            // with a higher low part; equal to it: this lane's bin.
+            sel_gt_before = low_above + (low_incl - low);
+            sel_eq_before = low;
         }
     }
     __syncthreads();
     const uint32_t thr = sel_thr, need = sel_need;
     POPKV_TOPK_PHASE(5);
 
-    // (3) positions.
-    uint32_t gt = 0, eq = 0;
+    // (3) positions.  Bit e of `gtm` / `eqm`: key e is above / equal to the
+    // threshold; the counts come from their population counts.
+    using Mask = typename std::conditional<(PER > 32), unsigned long long, uint32_t>::type;
+    Mask gtm = 0, eqm = 0;
 #pragma unroll
     for (int e = 0; e < PER; ++e) {
         if (e < lim) {
-            gt += key_of(e) > thr;
-            eq += key_of(e) == thr;
+            gtm |= static_cast<Mask>(key_of(e) > thr) << e;
+            eqm |= static_cast<Mask>(key_of(e) == thr) << e;
         }
     }
+    const uint32_t gt = popcount_mask(gtm), eq = popcount_mask(eqm);
     uint32_t cta_total;
     const uint32_t excl = cta_exclusive_scan32((gt << 16) | eq, warp_sums, cta_total);
-    if (tid > rank && tid < CPR) *cluster.map_shared_rank(&lower_totals[rank], tid) = cta_total;
-    cluster.sync();  // C: lower ranks' totals have arrived; no DSMEM access after this
+    const uint32_t rank_gt = sel_gt_before, rank_eq = sel_eq_before;
+    const uint32_t gt_before = rank_gt + (excl >> 16), eq_before = rank_eq + (excl & 0xFFFFu);
+    // The CTA's winners: output positions [first, first + count).
+    const uint32_t first = rank_gt + min(rank_eq, need);
+    const uint32_t cta_eq = cta_total & 0xFFFFu;
+    const uint32_t eq_taken = need > rank_eq ? min(need - rank_eq, cta_eq) : 0u;
+    const uint32_t count = (cta_total >> 16) + eq_taken;
     POPKV_TOPK_PHASE(6);
-    uint32_t gt_before = excl >> 16, eq_before = excl & 0xFFFFu;
-#pragma unroll
-    for (int c = 0; c < CPR; ++c) {  // zero for c >= rank; fields summed apart (no carry between them)
-        gt_before += lower_totals[c] >> 16;
-        eq_before += lower_totals[c] & 0xFFFFu;
+    // This thread's winners: every key above the threshold and its first
+    // `take` keys equal to it, at consecutive positions from `pos` on (the
+    // winners before them: all keys above, and the equal keys taken, of the
+    // lower threads and ranks).
+    Mask win = gtm, rest = eqm;
+    const uint32_t take = need > eq_before ? min(need - eq_before, eq) : 0u;
+    for (uint32_t i = 0; i < take; ++i) {
+        win |= rest & (~rest + 1);  // lowest remaining equal key
+        rest &= rest - 1;
     }
-#pragma unroll
-    for (int e = 0; e < PER; ++e) {
-        if (e >= lim) continue;
-        const uint32_t key = key_of(e);
-        if (key > thr) {
-            const uint32_t pos = gt_before + min(eq_before, need);
-            if (pos < kk) dst[pos] = base + e;
-            ++gt_before;
-        } else if (key == thr) {
-            const uint32_t pos = gt_before + eq_before;
-            if (eq_before < need && pos < kk) dst[pos] = base + e;
-            ++eq_before;
+    uint32_t pos = gt_before + min(eq_before, need);
+    while (win) {
+        const int e = lowest_bit(win);
+        win &= win - 1;
+        if (pos < kk) {
+            if constexpr (kStaged) {
+                const uint32_t slot = pos - first;  // in [0, count) by construction
+                if (slot < static_cast<uint32_t>(kStageSlots)) stage[slot] = static_cast<uint16_t>(tid * PER + e);
+            } else {
+                dst[pos] = base + e;
+            }
         }
+        ++pos;
+    }
+    if constexpr (kStaged) {
+        __syncthreads();
+        const uint32_t n = min(count, static_cast<uint32_t>(kStageSlots));
+        for (uint32_t j = tid; j < n; j += kClusterThreads)
+            if (first + j < kk) dst[first + j] = cta_base + stage[j];
     }
     POPKV_TOPK_PHASE(7);
 }
