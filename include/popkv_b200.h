@@ -200,8 +200,9 @@ POPKV_API int popkv_score_hist(const void* queries, int queries_dtype, int64_t b
 
 /*
  * popkv_topk for fp16 scores whose first-pass histogram popkv_score_hist has
- * already produced (rows of `tokens` <= 65536 scores).  Same output contract
- * as popkv_topk; resets the rows of `hist` it reads to zero.
+ * already produced (rows of up to 262144 scores; `hist` 16-byte aligned).
+ * Same output contract as popkv_topk; resets the rows of `hist` it reads to
+ * zero, also when k is 0.
  */
 POPKV_API int popkv_topk_hist(const uint16_t* scores, uint32_t* hist, int64_t rows, int64_t tokens,
                               int64_t row_stride, int64_t k, int64_t current_index, int64_t* out,

@@ -223,6 +223,11 @@ int launch_score128_hist(const void* queries, int64_t batch, int64_t q_heads, co
                          int64_t kv_heads, int64_t capacity, const int64_t* head_to_kv,
                          int64_t tokens, uint16_t* scores, uint32_t* hist, cudaStream_t stream) {
     const int group_heads = static_cast<int>(q_heads / kv_heads);
+    if (score_tc8_eligible(G, capacity, group_heads)) {
+        return launch_score128_tc8<G, QT, RAW, true>(
+            static_cast<const QT*>(queries), nullptr, nullptr, nullptr, nullptr, batch, q_heads, k_sign, k_mag,
+            k_low, k_delta, kv_heads, capacity, head_to_kv, tokens, scores, stream, tokens, nullptr, hist);
+    }
     const int64_t tiles = (tokens + kScoreTile - 1) / kScoreTile;
     dim3 grid(static_cast<unsigned>(tiles), static_cast<unsigned>(batch * kv_heads));
     const size_t smem = sizeof(uint32_t) * kHistBins11 * group_heads;

@@ -69,10 +69,14 @@ struct Layout {
     static constexpr int kBBlockBytes = N * 32;               // one K-block of B
     static constexpr int kRingBytes = kStages * kStageBytes;
     static constexpr int kUsedBytes = kRingBytes + 4 * kBBlockBytes;  // ring + B (offset 1024-aligned)
+    // Optional first-pass top-k histograms: 2048 bins per query head.
+    static constexpr int kHistOffset = kUsedBytes;
+    static constexpr int kHistBytes = kMaxHeads * 2048 * 4;
     // Padded so that at most two CTAs share an SM: a third CTA's 256-column
     // tensor-memory allocation would wait for one of them to finish.
-    static constexpr int kSmemBytes = kUsedBytes > 80 * 1024 ? kUsedBytes : 80 * 1024;
+    static constexpr int kSmemBytes = 80 * 1024;
     static_assert(kRingBytes % 1024 == 0, "B must start 1024-aligned");
+    static_assert(kHistOffset % 16 == 0 && kHistOffset + kHistBytes <= kSmemBytes, "histograms fit the padding");
 };
 
 // Sign-replicated bytes: byte e of the result is 0xFF if bit 8e+7 of x is set, else 0.
@@ -194,19 +198,23 @@ __device__ __forceinline__ void tc8_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // Grid: x = chunks of one (batch, GQA group)'s tiles, y = batch * groups; at
-// most kMaxHeads query heads per KV head.
-template <int G, typename QT, bool RAW>
+// most kMaxHeads query heads per KV head.  With HIST the kernel also counts
+// every score's top 11 key bits (order_key16 >> 5) per query row into `hist`
+// [rows][2048] (zeros on entry): per-CTA shared-memory histograms, flushed with
+// one global atomic per non-empty bin (the top-k's first radix pass).
+template <int G, typename QT, bool RAW, bool HIST>
 __global__ void __launch_bounds__(tc8::kThreads, 2) score128_tc8_kernel(
     const QT* __restrict__ queries, const int32_t* __restrict__ q_sign, const int32_t* __restrict__ q_mag,
     const float* __restrict__ q_low, const float* __restrict__ q_delta, const int32_t* __restrict__ k_sign,
     const int32_t* __restrict__ k_mag, const uint16_t* __restrict__ k_low, const uint16_t* __restrict__ k_delta,
     const int64_t* __restrict__ head_to_kv, uint16_t* __restrict__ scores, int q_heads, int group_heads,
     int64_t capacity, int64_t tokens, float scale, int64_t score_stride, const int64_t* __restrict__ dyn_tokens,
-    int chunks) {
+    int chunks, uint32_t* __restrict__ hist) {
     using L = tc8::Layout<G>;
     constexpr int R = L::R, N = L::N, S = tc8::kStages;
     extern __shared__ __align__(1024) unsigned char tc8_smem[];
     unsigned char* sB = tc8_smem + L::kRingBytes;
+    uint32_t* shist = reinterpret_cast<uint32_t*>(tc8_smem + L::kHistOffset);  // [head][2048], with `hist`
     __shared__ QueryState<G> states[tc8::kMaxHeads];
     __shared__ float enc_scratch[tc8::kMaxHeads][2 * 32 * 4];
     __shared__ float4 qdq[tc8::kMaxHeads][R / 2];  // {ql_r, ql_r+1, dq_r, dq_r+1}
@@ -263,6 +271,11 @@ __global__ void __launch_bounds__(tc8::kThreads, 2) score128_tc8_kernel(
         for (int s = 0; s < S; ++s) mbar_init(&full_bar[s], 1);
         mbar_init(&mma_bar, 1);
         for (int i = 0; i < ntiles && i < S; ++i) issue(i);
+    }
+
+    if constexpr (HIST) {
+        for (int i = threadIdx.x; i < group_heads * 512; i += tc8::kThreads)
+            reinterpret_cast<uint4*>(shist)[i] = make_uint4(0u, 0u, 0u, 0u);
     }
 
     // ---- query side: states, then B (K-major fp8) and the {ql, dq} pairs ----
@@ -387,8 +400,11 @@ __global__ void __launch_bounds__(tc8::kThreads, 2) score128_tc8_kernel(
                                                   vs[p], vs[R / 2 + p], vm[p], vm[R / 2 + p]);
                 total = __fadd_rn(__fadd_rn(total, ch.x), ch.y);  // groups in order
             }
-            if (tok < tokens)
-                scores[(row0 + h) * score_stride + tok] = float_to_half_bits(__fmul_rn(total, scale));
+            if (tok < tokens) {
+                const uint16_t bits = float_to_half_bits(__fmul_rn(total, scale));
+                scores[(row0 + h) * score_stride + tok] = bits;
+                if constexpr (HIST) atomicAdd(&shist[h * 2048 + (order_key16(bits) >> 5)], 1u);
+            }
         }
     };
 
@@ -429,6 +445,14 @@ __global__ void __launch_bounds__(tc8::kThreads, 2) score128_tc8_kernel(
     }
     if (warp == 0)
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" :: "r"(tmem), "r"(tc8::kTmemCols) : "memory");
+    if constexpr (HIST) {
+        // Every epilogue count landed before the loop's last block barrier:
+        // one global atomic per non-empty bin.
+        for (int i = threadIdx.x; i < group_heads * 2048; i += tc8::kThreads) {
+            const uint32_t c = shist[i];
+            if (c) atomicAdd(&hist[(row0 + (i >> 11)) * 2048 + (i & 2047)], c);
+        }
+    }
     pdl_launch_dependents();
 }
 
@@ -441,12 +465,13 @@ inline bool score_tc8_eligible(int G, int64_t capacity, int group_heads) {
 
 int score_sm_count();
 
-template <int G, typename QT, bool RAW>
+template <int G, typename QT, bool RAW, bool HIST = false>
 int launch_score128_tc8(const QT* queries, const int32_t* q_sign, const int32_t* q_mag, const float* q_low,
                         const float* q_delta, int64_t batch, int64_t q_heads, const int32_t* k_sign,
                         const int32_t* k_mag, const uint16_t* k_low, const uint16_t* k_delta, int64_t kv_heads,
                         int64_t capacity, const int64_t* head_to_kv, int64_t tokens, uint16_t* scores,
-                        cudaStream_t stream, int64_t score_stride, const int64_t* dyn_tokens) {
+                        cudaStream_t stream, int64_t score_stride, const int64_t* dyn_tokens,
+                        uint32_t* hist = nullptr) {
     const int group_heads = static_cast<int>(q_heads / kv_heads);
     const int64_t rows = batch * kv_heads;
     const int64_t tiles = (tokens + tc8::kTile - 1) / tc8::kTile;
@@ -457,13 +482,13 @@ int launch_score128_tc8(const QT* queries, const int32_t* q_sign, const int32_t*
     if (chunks < 1) chunks = 1;
     const dim3 grid(static_cast<unsigned>(chunks), static_cast<unsigned>(rows));
     constexpr int smem = tc8::Layout<G>::kSmemBytes;
-    auto kernel = score128_tc8_kernel<G, QT, RAW>;
+    auto kernel = score128_tc8_kernel<G, QT, RAW, HIST>;
     const int st = allow_dynamic_smem(kernel, smem);
     if (st != POPKV_OK) return st;
     const cudaError_t err = launch_pdl(kernel, grid, dim3(tc8::kThreads), smem, stream, 1, queries, q_sign, q_mag,
                                        q_low, q_delta, k_sign, k_mag, k_low, k_delta, head_to_kv, scores,
                                        static_cast<int>(q_heads), group_heads, capacity, tokens, score_scale_for(128),
-                                       score_stride, dyn_tokens, static_cast<int>(chunks));
+                                       score_stride, dyn_tokens, static_cast<int>(chunks), hist);
     if (err != cudaSuccess) return fail(POPKV_ERR_CUDA, "popkv_score: %s", cudaGetErrorString(err));
     return check_launch("popkv_score");
 }

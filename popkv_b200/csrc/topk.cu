@@ -50,11 +50,8 @@ constexpr int kTopkWarps = kTopkThreads / 32;
 constexpr int kHistBins = 2048;
 constexpr size_t kStageBytes = 96 * 1024;
 
-__device__ __forceinline__ uint32_t key16(uint16_t h) {
-    if ((h & 0x7FFFu) == 0) h = 0;  // -0 == +0
-    if ((h & 0x7C00u) == 0x7C00u && (h & 0x3FFu)) return 0xFFFFu;  // NaN ranks highest
-    return (h & 0x8000u) ? (~static_cast<uint32_t>(h) & 0xFFFFu) : (static_cast<uint32_t>(h) | 0x8000u);
-}
+// -0 == +0, NaN ranks highest (the key the score kernels' histograms use).
+__device__ __forceinline__ uint32_t key16(uint16_t h) { return order_key16(h); }
 
 __device__ __forceinline__ uint32_t key32(uint32_t u) {
     if ((u & 0x7FFFFFFFu) == 0) u = 0;
@@ -836,7 +833,7 @@ template <int CPR, int PER>
 __global__ void __launch_bounds__(kClusterThreads, PER <= 16 ? 4 : 1) topk16_cluster_kernel(
     const uint16_t* __restrict__ scores, int64_t tokens, int64_t row_stride, int64_t k,
     int64_t current_index, int64_t* __restrict__ out, int64_t out_stride, bool vec_ok,
-    const int64_t* __restrict__ dyn_tokens) {
+    const int64_t* __restrict__ dyn_tokens, uint32_t* __restrict__ ghist) {
     static_assert(PER % 8 == 0 && PER <= 64, "PER keys per thread, whole uint4 loads");
     static_assert(CPR <= 8, "at most 8 ranks per cluster");
     constexpr int64_t kSlice = static_cast<int64_t>(kClusterThreads) * PER;
@@ -869,10 +866,18 @@ __global__ void __launch_bounds__(kClusterThreads, PER <= 16 ? 4 : 1) topk16_clu
     const int tid = threadIdx.x;
     int64_t* dst = out + row * out_stride;
     if (current_index >= 0 && tid == 0 && rank == 0) dst[k] = current_index;
-    if (k <= 0) return;  // uniform across the cluster: no CTA reaches a cluster barrier
+    uint32_t* grow = ghist ? ghist + row * kHistBins : nullptr;  // the row's first-pass histogram, if given
+    if (k <= 0) {  // uniform across the cluster: no CTA reaches a cluster barrier
+        if (grow && rank == 0)
+            reinterpret_cast<uint4*>(grow)[tid] = make_uint4(0u, 0u, 0u, 0u);  // leave zeros for the next call
+        return;
+    }
     const uint32_t kk = static_cast<uint32_t>(k);
+    uint4 gbins = make_uint4(0u, 0u, 0u, 0u);
+    if (grow) gbins = __ldcg(reinterpret_cast<const uint4*>(grow) + (kHistBins / 4 - 1) - tid);  // 2047-4t..2044-4t
 
-    for (int b = tid; b < kHistBins; b += kClusterThreads) hist[b] = 0;
+    if (!grow)
+        for (int b = tid; b < kHistBins; b += kClusterThreads) hist[b] = 0;
     if (tid < kRow2) hist2[tid] = 0;
     if (tid == 0) {  // defaults; the scans below always overwrite them when k <= tokens
         sel_b1 = 0;
@@ -910,15 +915,15 @@ __global__ void __launch_bounds__(kClusterThreads, PER <= 16 ? 4 : 1) topk16_clu
     POPKV_TOPK_PHASE(1);
     __syncthreads();  // histograms zeroed
 
-    // (1) top 11 bits.
+    // (1) top 11 bits: counted here, or by the kernel that wrote the scores.
+    uint32_t cnt[4] = {gbins.w, gbins.z, gbins.y, gbins.x};  // bins 2047 - 4t - q
+    if (!grow) {
 #pragma unroll
-    for (int e = 0; e < PER; ++e)
-        if (e < lim) atomicAdd(&hist[key_of(e) >> 5], 1u);
-    POPKV_TOPK_PHASE(2);
-    cluster.sync();  // A: every CTA's histogram is complete
-    POPKV_TOPK_PHASE(3);
-    uint32_t cnt[4] = {0u, 0u, 0u, 0u};
-    {
+        for (int e = 0; e < PER; ++e)
+            if (e < lim) atomicAdd(&hist[key_of(e) >> 5], 1u);
+        POPKV_TOPK_PHASE(2);
+        cluster.sync();  // A: every CTA's histogram is complete
+        POPKV_TOPK_PHASE(3);
         uint4 v[CPR];
 #pragma unroll
         for (int c = 0; c < CPR; ++c)  // all loads in flight at once
@@ -962,6 +967,8 @@ __global__ void __launch_bounds__(kClusterThreads, PER <= 16 ? 4 : 1) topk16_clu
     if (tid < CPR * kRow2)  // thread (c, i): entry i into rank c's copy
         cluster.map_shared_rank(hist2_all, tid / kRow2)[rank * kRow2 + tid % kRow2] = hist2[tid % kRow2];
     cluster.sync();  // B: every rank's row has arrived in every CTA
+    if (grow && rank == 0)  // every CTA read the row's histogram before B: leave zeros for the next call
+        reinterpret_cast<uint4*>(grow)[tid] = make_uint4(0u, 0u, 0u, 0u);
     if (tid < 32) {
         // Lane i: bin 31 - i, over all ranks and over the lower ranks.
         uint32_t c2 = 0, low = 0, low_above = 0;
@@ -1056,11 +1063,12 @@ __global__ void __launch_bounds__(kClusterThreads, PER <= 16 ? 4 : 1) topk16_clu
 template <int CPR, int PER>
 int launch_cluster16(const void* scores, int64_t rows, int64_t tokens, int64_t row_stride, int64_t k,
                      int64_t current_index, int64_t* out, int64_t out_stride, bool vec_ok,
-                     cudaStream_t stream, const int64_t* dyn_tokens) {
+                     cudaStream_t stream, const int64_t* dyn_tokens, uint32_t* ghist) {
     const cudaError_t err = launch_pdl(topk16_cluster_kernel<CPR, PER>,
                                        dim3(static_cast<unsigned>(rows * CPR)), dim3(kClusterThreads), 0,
                                        stream, CPR, static_cast<const uint16_t*>(scores), tokens,
-                                       row_stride, k, current_index, out, out_stride, vec_ok, dyn_tokens);
+                                       row_stride, k, current_index, out, out_stride, vec_ok, dyn_tokens,
+                                       ghist);
     if (err != cudaSuccess) return fail(POPKV_ERR_CUDA, "popkv_topk: %s", cudaGetErrorString(err));
     return check_launch("popkv_topk");
 }
@@ -1072,7 +1080,8 @@ int launch_cluster16(const void* scores, int64_t rows, int64_t tokens, int64_t r
 // thread that cover the row.  Returns -1 when the shape does not apply.
 int try_launch_cluster16(const void* scores, int64_t rows, int64_t tokens, int64_t row_stride,
                          int64_t k, int64_t current_index, int64_t* out, int64_t out_stride,
-                         bool vec_ok, cudaStream_t stream, const int64_t* dyn_tokens = nullptr) {
+                         bool vec_ok, cudaStream_t stream, const int64_t* dyn_tokens = nullptr,
+                         uint32_t* ghist = nullptr) {
     if (k <= 0 || k > tokens || rows > 0x7FFFFFF) return -1;
     // Up to 4 CTAs per row while the rows leave SMs idle (larger clusters cost
     // more in DSMEM reads and barrier latency than they save), more only when a
@@ -1102,7 +1111,7 @@ int try_launch_cluster16(const void* scores, int64_t rows, int64_t tokens, int64
 #define POPKV_C16(CPR_, PER_)                                                                      \
     if (cpr == CPR_ && per == PER_)                                                                \
         return launch_cluster16<CPR_, PER_>(scores, rows, tokens, row_stride, k, current_index, out, \
-                                            out_stride, vec_ok, stream, dyn_tokens);
+                                            out_stride, vec_ok, stream, dyn_tokens, ghist);
 #define POPKV_C16_CPR(CPR_) POPKV_C16(CPR_, 8) POPKV_C16(CPR_, 16) POPKV_C16(CPR_, 32)
     POPKV_C16_CPR(1)
     POPKV_C16_CPR(2)
@@ -1199,9 +1208,13 @@ extern "C" int popkv_topk_hist(const uint16_t* scores, uint32_t* hist, int64_t r
     if (!out || !hist || !scores) return fail(POPKV_ERR_INVALID, "popkv_topk_hist: null pointer");
     if (!aligned(hist, 16)) return fail(POPKV_ERR_INVALID, "popkv_topk_hist: hist must be 16-byte aligned");
     const bool vec_ok = aligned(scores, 16) && (row_stride * 2) % 16 == 0;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    // The cluster kernel finishes from the histogram when the row fits it.
+    const int st = try_launch_cluster16(scores, rows, tokens, row_stride, k, current_index, out, out_stride,
+                                        vec_ok, s, nullptr, hist);
+    if (st >= 0) return st;
     if (tokens > 64 * kHistThreads)
         return fail(POPKV_ERR_UNSUPPORTED, "popkv_topk_hist: at most %d tokens", 64 * kHistThreads);
-    cudaStream_t s = static_cast<cudaStream_t>(stream);
     const unsigned grid = static_cast<unsigned>(rows);
     if (tokens <= 8 * kHistThreads)
         topk_hist_kernel<8><<<grid, kHistThreads, 0, s>>>(scores, hist, tokens, row_stride, k, current_index, out, out_stride, vec_ok);

@@ -36,8 +36,8 @@ class SparseAttentionStep:
         q_dtype: dtype of the queries / outputs.
         select: "radix" (score, then the radix top-k: one thread-block
             cluster per row) or "hist" (the score kernel also builds the top-k's
-            first radix histogram and one CTA per row finishes the selection;
-            needs <= 4 query heads per KV head and <= 65536 tokens).  "auto" is
+            first radix histogram and the cluster top-k finishes from it;
+            needs <= 4 query heads per KV head and <= 262144 tokens).  "auto" is
             "radix", the faster of the two on B200 at 32K tokens (57.5 vs 62.5
             us per graph-captured step).
         host_io: keep pinned host staging buffers (``host_queries``,
@@ -141,11 +141,11 @@ class SparseAttentionStep:
         # fused=True: one popkv_retrieve launch (score, select, attention, merge in
         # one thread-block cluster per KV head); fused=False: the three-launch chain.
         self.fused = fused and batch == 1 and self.q_heads // self.kv_heads in (1, 2, 4)
-        hist_ok = self.q_heads // self.kv_heads <= 4 and self.prefix_tokens <= 65536
+        hist_ok = self.q_heads // self.kv_heads <= 4 and self.prefix_tokens <= 262144
         if select not in ("auto", "hist", "radix"):
             raise ValueError(f"unknown select {select!r}")
         if select == "hist" and not hist_ok:
-            raise ValueError("select='hist' needs <= 4 query heads per KV head and <= 65536 tokens")
+            raise ValueError("select='hist' needs <= 4 query heads per KV head and <= 262144 tokens")
         self.select = "radix" if select == "auto" else select
         if self.fused:
             self.kernels = ("retrieve",)

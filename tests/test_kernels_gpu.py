@@ -491,7 +491,7 @@ def test_partial_merge_single_launch_matches_two_launches(cuda_device, valid):
 
 @pytest.mark.parametrize("g", GROUPS)
 @pytest.mark.parametrize("tokens,budget", [(32768, 4096), (3000, 256), (100, 1000), (65536, 4096),
-                                           (777, 500)])
+                                           (777, 500), (131072, 4096), (5000, 1)])
 def test_score_hist_and_topk_hist_match_separate_kernels(cuda_device, g, tokens, budget):
     """popkv_score_hist + popkv_topk_hist == popkv_score + popkv_topk, and the histogram is re-zeroed."""
     from popkv_b200 import _lib
