@@ -27,6 +27,9 @@ from popkv_b200.workloads import decode_inputs, head_to_kv
 
 FIXTURE = Path(__file__).resolve().parent / "golden" / "reference_cuda.npz"
 CASES = ("config0", "config1", "popkv_normal")
+# The oracle runs on the CPU cases only: config 1's inputs are hundreds of MB of
+# arrays, which the CUDA-path test (on a GPU host) covers.
+CPU_CASES = ("config0", "popkv_normal")
 
 pytestmark = pytest.mark.skipif(not FIXTURE.exists(), reason="reference CUDA fixture not recorded")
 
@@ -89,7 +92,7 @@ def _boundary_check(name, selected_ref, selected_ours, scores_ours, kth_ref):
     return sym
 
 
-@pytest.mark.parametrize("name", CASES)
+@pytest.mark.parametrize("name", CPU_CASES)
 def test_oracle_planes_and_query_encoding_match_reference_cuda(fx, name):
     planes, enc, _, _, _ = _oracle_case(name, fx)
     digests = [str(d) for d in fx[f"{name}/digests"]]
@@ -116,7 +119,7 @@ def test_oracle_scorer_reproduces_reference_scores_bit_for_bit(fx):
     assert np.array_equal(scores, fx[f"{name}/scores"])
 
 
-@pytest.mark.parametrize("name", CASES)
+@pytest.mark.parametrize("name", CPU_CASES)
 def test_oracle_selection_matches_reference_cuda_at_the_boundary(fx, name):
     _, _, scores, selected, k = _oracle_case(name, fx)
     sym = _boundary_check(name, fx[f"{name}/selected"], selected[0], scores[0], fx[f"{name}/kth_score"])
