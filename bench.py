@@ -9,14 +9,19 @@ head_dim 128, context 32768, budget 4096, PopKV-Q preset (token group 128,
 dim group 16), bf16 K/V/Q, seeded synthetic inputs (popkv_b200.workloads).
 
 With N GPUs (torchrun) the KV heads -- cache, metadata, query heads -- are
-sharded across ranks and each step ends with one NCCL all-gather of the
-per-head attention outputs (the total work is fixed: strong scaling).
+sharded across ranks and each step ends with the merge fused with the
+all-gather over NVLink peer memory (``--gather nccl``: an NCCL all-gather);
+the total work is fixed: strong scaling.
 
 Timing: W warm-up steps, then exactly K steps between a barrier +
-synchronize; each step is bracketed by CUDA events on the launching stream
-and the per-step device times are summed; the max over ranks is reported.
-L2: steps cycle over enough copies of the layer (cache + metadata) that the
-working set of consecutive steps exceeds the 126 MB L2.
+synchronize.  The steps run as the layers of one decoded token do in the
+decoder's per-token graph: ``--chain`` (8) consecutive steps, each on the next
+layer copy, captured in one CUDA graph; each replay is bracketed by CUDA
+events on the launching stream, the device times are summed over K steps and
+the max over ranks is reported.  ``single_step_graph`` repeats the
+measurement with one graph launch per step.  L2: steps cycle over enough
+copies of the layer (cache + metadata) that the working set of consecutive
+steps exceeds the 126 MB L2.
 
 ``--impl reference`` times the reference's CPU implementation of the path
 (the C restatement in oracle/, OpenMP over all host cores) on the same
@@ -78,6 +83,10 @@ def parse_args(argv=None):
     p.add_argument("--split", type=int, default=256, help="selected slots per attention partial")
     p.add_argument("--chunks", type=int, default=1,
                    help="KV-head chunks pipelined on forked streams inside the step graph")
+    p.add_argument("--chain", type=int, default=8,
+                   help="layer steps per captured CUDA graph in the timed loop, each on the next layer copy "
+                        "(as the layers of one decoded token run in the decoder's graph); 1: one graph "
+                        "launch per step")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU baseline sample budget")
     p.add_argument("--stage-reps", type=int, default=50)
@@ -375,6 +384,33 @@ def run_ours(args, world, rank, local):
     for i in range(args.warmup):
         one_step(i)
     torch.cuda.synchronize(device)
+
+    # Chains: `chain` consecutive layer steps (each on the next layer copy)
+    # captured into one CUDA graph, as the layers of a decoded token are; the
+    # timed loop replays them so that exactly K steps run.
+    chain = max(1, min(args.chain, args.steps))
+    if args.no_graph or (dist is not None and peer is None) or args.chunks != 1:
+        chain = 1  # eager steps, or an NCCL all-gather after each replay
+
+    def capture_chain(n, offset):
+        g = torch.cuda.CUDAGraph()
+        side = torch.cuda.Stream(device)
+        side.wait_stream(stream)
+        with torch.cuda.graph(g, stream=side):
+            for j in range(n):
+                steps[(offset + j) % copies]._launch(side)
+        stream.wait_stream(side)
+        return g
+
+    full, rem = divmod(args.steps, chain)
+    if chain > 1:
+        chains = [capture_chain(chain, 0)] + ([capture_chain(rem, full * chain)] if rem else [])
+        plan = [(chains[0], chain)] * full + ([(chains[1], rem)] if rem else [])
+        for _ in range(max(1, math.ceil(args.warmup / chain))):
+            chains[0].replay()
+    else:
+        plan = [(None, 1)] * args.steps
+    torch.cuda.synchronize(device)
     sampler = ClockSampler(physical_gpu_index(local)).start()
     time.sleep(0.25)
     # Keep the GPU busy while the sampler warms up, then time exactly K steps.
@@ -383,12 +419,15 @@ def run_ours(args, world, rank, local):
     if dist is not None:
         dist.barrier()
     torch.cuda.synchronize(device)
-    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    starts = [torch.cuda.Event(enable_timing=True) for _ in plan]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in plan]
     t0 = time.time()
-    for i in range(args.steps):
+    for i, (g, _) in enumerate(plan):
         starts[i].record(stream)
-        one_step(i)
+        if g is None:
+            one_step(i)
+        else:
+            g.replay()
         ends[i].record(stream)
     torch.cuda.synchronize(device)
     if dist is not None:
@@ -396,12 +435,26 @@ def run_ours(args, world, rank, local):
     torch.cuda.synchronize(device)
     t1 = time.time()
     sampler.stop()
-    per_step = [s.elapsed_time(e) for s, e in zip(starts, ends)]
-    total_ms = sum(per_step)
-    total = torch.tensor([total_ms], device=device, dtype=torch.float64)
+    total_ms = sum(s.elapsed_time(e) for s, e in zip(starts, ends))
+    # The same steps with one graph launch per step (per-step events), for comparison.
+    single_n = min(args.steps, 400)
+    s_starts = [torch.cuda.Event(enable_timing=True) for _ in range(single_n)]
+    s_ends = [torch.cuda.Event(enable_timing=True) for _ in range(single_n)]
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize(device)
+    for i in range(single_n):
+        s_starts[i].record(stream)
+        one_step(i)
+        s_ends[i].record(stream)
+    torch.cuda.synchronize(device)
+    single_ms = sum(s.elapsed_time(e) for s, e in zip(s_starts, s_ends))
+    total = torch.tensor([total_ms, single_ms], device=device, dtype=torch.float64)
     if dist is not None:
         dist.all_reduce(total, op=dist.ReduceOp.MAX)
-    ms_per_step = float(total.item()) / args.steps
+    ms_per_step = float(total[0].item()) / args.steps
+    single_ms_per_step = float(total[1].item()) / single_n
+    chains = plan = None
 
     stages = stage_breakdown(args, layer, steps, device)
     e2e = end_to_end(args, layer, steps, device, dist, gathered, world, peer)
@@ -452,8 +505,13 @@ def run_ours(args, world, rank, local):
                     " + merge fused with the all-gather over NVLink peer memory" if peer is not None
                     else " + NCCL all-gather")),
                 "l2": f"steps cycle over {copies} layer copies ({copies * layer_bytes(args, layer) / 2**20:.0f} MiB) > L2",
-                "launch": "eager" if args.no_graph else "CUDA graph per layer step",
+                "launch": ("eager" if args.no_graph else
+                           "CUDA graph per layer step" if chain == 1 else
+                           f"{chain} layer steps per CUDA graph (each on the next layer copy, as the layers "
+                           f"of one decoded token), replays timed with CUDA events"),
             },
+            "single_step_graph": {"ms_per_step": round(single_ms_per_step, 5), "steps": single_n,
+                                  "timing": "one graph launch per step, CUDA events around each"},
             "roofline": {
                 "bound": "hbm", "kernel": dominant,
                 "achieved": dom.get("achieved_gbs"), "peak": peaks["hbm_gbs"], "unit": "GB/s",
