@@ -223,16 +223,30 @@ __global__ void __launch_bounds__(tc8::kThreads, 2) score128_tc8_kernel(
     __shared__ uint32_t tmem_base;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    pdl_wait();
-    if (dyn_tokens) {
-        const int64_t t = *dyn_tokens;
-        tokens = t < 0 ? 0 : (t < tokens ? t : tokens);
-    }
     const int groups = q_heads / group_heads;
     const int64_t b = blockIdx.y / groups;
     const int grp = blockIdx.y % groups;
     const int qh0 = grp * group_heads;
     const int64_t row0 = b * q_heads + qh0;
+
+    // Set-up that reads nothing a predecessor kernel writes runs before the
+    // dependency wait: the head mapping (a read-only argument) and the stage
+    // barriers.  Tensor memory is allocated only after the wait: a predecessor
+    // that triggers this launch before allocating its own columns must never
+    // find them taken by a CTA that is waiting for it.  Lane 0 of the last
+    // warp streams the plane tiles; it issues the first kStages after the wait
+    // while warps 0-3 encode the queries.
+    const bool streamer = threadIdx.x == (tc8::kWarps - 1) * 32;
+    const int64_t kvh = streamer ? head_to_kv[qh0] : 0;
+    if (streamer) {
+        for (int s = 0; s < S; ++s) mbar_init(&full_bar[s], 1);
+        mbar_init(&mma_bar, 1);
+    }
+    pdl_wait();
+    if (dyn_tokens) {
+        const int64_t t = *dyn_tokens;
+        tokens = t < 0 ? 0 : (t < tokens ? t : tokens);
+    }
     const int64_t tiles = (tokens + tc8::kTile - 1) / tc8::kTile;
     const int64_t tile_begin = static_cast<int64_t>(blockIdx.x) * tiles / chunks;
     const int64_t tile_end = static_cast<int64_t>(blockIdx.x + 1) * tiles / chunks;
@@ -241,11 +255,12 @@ __global__ void __launch_bounds__(tc8::kThreads, 2) score128_tc8_kernel(
         return;
     }
     const int ntiles = static_cast<int>(tile_end - tile_begin);
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
+                     :: "r"(smem_addr(&tmem_base)), "r"(tc8::kTmemCols) : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
 
-    // Lane 0 of the last warp streams the plane tiles: it sets up the barriers
-    // and issues the first kStages while warps 0-3 encode the queries.
-    const bool streamer = threadIdx.x == (tc8::kWarps - 1) * 32;
-    const int64_t kvh = streamer ? head_to_kv[qh0] : 0;
     const unsigned char* sign_src = reinterpret_cast<const unsigned char*>(k_sign) + kvh * capacity * 16;
     const unsigned char* mag_src = reinterpret_cast<const unsigned char*>(k_mag) + kvh * capacity * 16;
     const unsigned char* low_src = reinterpret_cast<const unsigned char*>(k_low) + kvh * capacity * 2 * R;
@@ -262,16 +277,8 @@ __global__ void __launch_bounds__(tc8::kThreads, 2) score128_tc8_kernel(
         bulk_copy_g2s(stage + tc8::kTile * 32, low_src + t0 * 2 * R, n * 2u * R, &full_bar[s]);
         bulk_copy_g2s(stage + tc8::kTile * (32 + 2 * R), delta_src + t0 * 2 * R, n * 2u * R, &full_bar[s]);
     };
-    if (warp == 0) {
-        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
-                     :: "r"(smem_addr(&tmem_base)), "r"(tc8::kTmemCols) : "memory");
-        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
-    }
-    if (streamer) {
-        for (int s = 0; s < S; ++s) mbar_init(&full_bar[s], 1);
-        mbar_init(&mma_bar, 1);
+    if (streamer)
         for (int i = 0; i < ntiles && i < S; ++i) issue(i);
-    }
 
     if constexpr (HIST) {
         for (int i = threadIdx.x; i < group_heads * 512; i += tc8::kThreads)
