@@ -247,6 +247,17 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_partial128_kernel(
 }
 
 // ---------------------------------------------------------------------------
+// Pairs of dims (2j, 2j+1) of one 16-byte unit as float2, for packed fp32 math.
+template <typename KT>
+__device__ __forceinline__ void unpack_unit2(const uint4& u, float2* f) {
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        if constexpr (std::is_same<KT, __nv_bfloat16>::value) f[j] = make_float2(bf16_lo(w[j]), bf16_hi(w[j]));
+        else f[j] = __half22float2(*reinterpret_cast<const __half2*>(&w[j]));
+    }
+}
+
 // Pipelined partial kernel (head_dim 128, 16-bit K/V).
 //
 // Thread t owns row group r = t / 8 and 16-byte units c and c + 8 of the
@@ -416,9 +427,15 @@ __global__ void __launch_bounds__(kAttnThreads, 4) attn_partial_pipe_kernel(
     }
 
     float m = -INFINITY, ssum = 0.0f;  // m in log2 units
-    float acc[16];
+    // Dims (2j, 2j+1) of this thread's 16 as pairs: the products and the
+    // accumulator updates run as packed fp32 operations (each element rounded
+    // as a single fma would round it).
+    float2 q2[8], acc2[8];
 #pragma unroll
-    for (int j = 0; j < 16; ++j) acc[j] = 0.0f;
+    for (int j = 0; j < 8; ++j) {
+        q2[j] = make_float2(q[2 * j], q[2 * j + 1]);
+        acc2[j] = make_float2(0.0f, 0.0f);
+    }
 
 #pragma unroll
     for (int i = 0; i < kPipeMaxSub; ++i) {
@@ -429,40 +446,49 @@ __global__ void __launch_bounds__(kAttnThreads, 4) attn_partial_pipe_kernel(
 #pragma unroll
         for (int h = 0; h < kPipeRowsPerGroup; ++h) {
             const int id = rid[i][h];  // uniform across the 8 lanes of the row group
-            float kf[16];
+            float2 kf[8];
             if (id != kSlotMasked) {
-                unpack_unit<KT>(*reinterpret_cast<const uint4*>(stage_k(st, h)), kf);
-                unpack_unit<KT>(*reinterpret_cast<const uint4*>(stage_k(st, h) + 128), kf + 8);
+                unpack_unit2<KT>(*reinterpret_cast<const uint4*>(stage_k(st, h)), kf);
+                unpack_unit2<KT>(*reinterpret_cast<const uint4*>(stage_k(st, h) + 128), kf + 4);
             } else {
 #pragma unroll
-                for (int j = 0; j < 16; ++j) kf[j] = 0.0f;
+                for (int j = 0; j < 8; ++j) kf[j] = make_float2(0.0f, 0.0f);
             }
-            float dot = 0.0f;
+            float2 d2 = make_float2(0.0f, 0.0f);
 #pragma unroll
-            for (int j = 0; j < 16; ++j) dot = __fmaf_rn(kf[j], q[j], dot);
+            for (int j = 0; j < 8; ++j) d2 = __ffma2_rn(kf[j], q2[j], d2);
+            float dot = d2.x + d2.y;
             dot += __shfl_xor_sync(0xFFFFFFFFu, dot, 4);
             dot += __shfl_xor_sync(0xFFFFFFFFu, dot, 2);
             dot += __shfl_xor_sync(0xFFFFFFFFu, dot, 1);
             if (id != kSlotMasked) {
-                float vf[16];
-                unpack_unit<KT>(*reinterpret_cast<const uint4*>(stage_v(st, h)), vf);
-                unpack_unit<KT>(*reinterpret_cast<const uint4*>(stage_v(st, h) + 128), vf + 8);
+                float2 vf[8];
+                unpack_unit2<KT>(*reinterpret_cast<const uint4*>(stage_v(st, h)), vf);
+                unpack_unit2<KT>(*reinterpret_cast<const uint4*>(stage_v(st, h) + 128), vf + 4);
                 if (dot > m) {  // new maximum: rescale what has been accumulated
                     const float alpha = exp2f(m - dot);  // 0 when m == -inf
                     ssum = __fmaf_rn(ssum, alpha, 1.0f);
+                    const float2 a2 = make_float2(alpha, alpha);
 #pragma unroll
-                    for (int j = 0; j < 16; ++j) acc[j] = __fmaf_rn(acc[j], alpha, vf[j]);
+                    for (int j = 0; j < 8; ++j) acc2[j] = __ffma2_rn(acc2[j], a2, vf[j]);
                     m = dot;
                 } else {
                     const float p = exp2f(dot - m);
                     ssum += p;
+                    const float2 p2 = make_float2(p, p);
 #pragma unroll
-                    for (int j = 0; j < 16; ++j) acc[j] = __fmaf_rn(p, vf[j], acc[j]);
+                    for (int j = 0; j < 8; ++j) acc2[j] = __ffma2_rn(p2, vf[j], acc2[j]);
                 }
             }
         }
     }
     cp_async_wait<0>();
+    float acc[16];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        acc[2 * j] = acc2[j].x;
+        acc[2 * j + 1] = acc2[j].y;
+    }
     POPKV_ATTN_PHASE(3);
 
     // Combine the 4 row groups of this warp (lanes with equal c), then the 8 warps.
