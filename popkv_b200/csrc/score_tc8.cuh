@@ -156,6 +156,11 @@ template <int X>
 __device__ __forceinline__ void tmem_ld(uint32_t taddr, float2 (&v)[X / 2]);
 
 template <>
+__device__ __forceinline__ void tmem_ld<2>(uint32_t taddr, float2 (&v)[1]) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x2.b32 {%0,%1}, [%2];"
+                 : "=f"(v[0].x), "=f"(v[0].y) : "r"(taddr));
+}
+template <>
 __device__ __forceinline__ void tmem_ld<4>(uint32_t taddr, float2 (&v)[2]) {
     asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0,%1,%2,%3}, [%4];"
                  : "=f"(v[0].x), "=f"(v[0].y), "=f"(v[1].x), "=f"(v[1].y) : "r"(taddr));
@@ -390,27 +395,51 @@ __global__ void __launch_bounds__(tc8::kThreads, 2) score128_tc8_kernel(
             dk[p].y = tc8::half_of(dw[p], 1);
         }
         const int64_t tok = (tile_begin + i) * tc8::kTile + row;
+        const int h0 = 2 * P, h1 = 2 * P + 1;
+        if (h0 >= group_heads) return;  // uniform over the warp
         __syncwarp();  // converged for the .aligned tensor-memory loads
+        // Both heads' chains interleaved (independent dependency chains); each
+        // head's groups are still summed in order.  Columns of head hh:
+        // [qt 0: groups 0..R-1][qt 1: groups 0..R-1] from kColD + P*4R + hh*2R.
+        // A missing second head (odd group) reads zero columns and is not stored.
+        const uint32_t c0 = t_lane + tc8::kColD + P * 4 * R, c1 = c0 + 2 * R;
+        float t0 = 0.0f, t1 = 0.0f;
+        constexpr int H = R == 8 ? 2 : 1;  // column halves (register budget)
+        constexpr int PP = R / 2 / H;      // group pairs per half
 #pragma unroll
-        for (int hh = 0; hh < 2; ++hh) {
-            const int h = 2 * P + hh;
-            if (h >= group_heads) continue;  // uniform over the warp
-            float2 vs[R], vm[R];             // [qt][group pair] of the sign and magnitude planes
-            tc8::tmem_ld<2 * R>(t_lane + tc8::kColD + P * 4 * R + hh * 2 * R, vs);
-            tc8::tmem_ld<2 * R>(t_lane + tc8::kColD + N + P * 4 * R + hh * 2 * R, vm);
+        for (int half = 0; half < H; ++half) {
+            // [head][plane][qt] pairs of the half's groups
+            float2 s0a[PP], s0b[PP], m0a[PP], m0b[PP], s1a[PP], s1b[PP], m1a[PP], m1b[PP];
+            const uint32_t off = half * 2 * PP;  // first column of the half
+            tc8::tmem_ld<2 * PP>(c0 + off, s0a);
+            tc8::tmem_ld<2 * PP>(c0 + R + off, s0b);
+            tc8::tmem_ld<2 * PP>(c0 + N + off, m0a);
+            tc8::tmem_ld<2 * PP>(c0 + N + R + off, m0b);
+            tc8::tmem_ld<2 * PP>(c1 + off, s1a);
+            tc8::tmem_ld<2 * PP>(c1 + R + off, s1b);
+            tc8::tmem_ld<2 * PP>(c1 + N + off, m1a);
+            tc8::tmem_ld<2 * PP>(c1 + N + R + off, m1b);
             tc8::tmem_wait_ld();
-            float total = 0.0f;
 #pragma unroll
-            for (int p = 0; p < R / 2; ++p) {
-                const float4 q = qdq[h][p];
-                const float2 ch = tc8::chain_pair(make_float2(q.x, q.y), make_float2(q.z, q.w), kl[p], dk[p],
-                                                  vs[p], vs[R / 2 + p], vm[p], vm[R / 2 + p]);
-                total = __fadd_rn(__fadd_rn(total, ch.x), ch.y);  // groups in order
+            for (int pp = 0; pp < PP; ++pp) {
+                const int p = half * PP + pp;
+                const float4 q0 = qdq[h0][p], q1 = qdq[h1][p];
+                const float2 ch0 = tc8::chain_pair(make_float2(q0.x, q0.y), make_float2(q0.z, q0.w), kl[p], dk[p],
+                                                   s0a[pp], s0b[pp], m0a[pp], m0b[pp]);
+                const float2 ch1 = tc8::chain_pair(make_float2(q1.x, q1.y), make_float2(q1.z, q1.w), kl[p], dk[p],
+                                                   s1a[pp], s1b[pp], m1a[pp], m1b[pp]);
+                t0 = __fadd_rn(__fadd_rn(t0, ch0.x), ch0.y);  // groups in order
+                t1 = __fadd_rn(__fadd_rn(t1, ch1.x), ch1.y);
             }
-            if (tok < tokens) {
-                const uint16_t bits = float_to_half_bits(__fmul_rn(total, scale));
-                scores[(row0 + h) * score_stride + tok] = bits;
-                if constexpr (HIST) atomicAdd(&shist[h * 2048 + (order_key16(bits) >> 5)], 1u);
+        }
+        if (tok < tokens) {
+            const uint16_t b0 = float_to_half_bits(__fmul_rn(t0, scale));
+            scores[(row0 + h0) * score_stride + tok] = b0;
+            if constexpr (HIST) atomicAdd(&shist[h0 * 2048 + (order_key16(b0) >> 5)], 1u);
+            if (h1 < group_heads) {
+                const uint16_t b1 = float_to_half_bits(__fmul_rn(t1, scale));
+                scores[(row0 + h1) * score_stride + tok] = b1;
+                if constexpr (HIST) atomicAdd(&shist[h1 * 2048 + (order_key16(b1) >> 5)], 1u);
             }
         }
     };
@@ -482,9 +511,11 @@ int launch_score128_tc8(const QT* queries, const int32_t* q_sign, const int32_t*
     const int group_heads = static_cast<int>(q_heads / kv_heads);
     const int64_t rows = batch * kv_heads;
     const int64_t tiles = (tokens + tc8::kTile - 1) / tc8::kTile;
-    // Two CTAs per SM (two 256-column tensor-memory allocations fill an SM's 512).
+    // Two CTAs per SM (two 256-column tensor-memory allocations fill an SM's 512):
+    // at most one resident wave of chunks, since every CTA of a row runs the same
+    // number of tiles and a second wave would double the kernel's time.
     const int64_t target = static_cast<int64_t>(score_sm_count()) * 2;
-    int64_t chunks = (target + rows - 1) / rows;
+    int64_t chunks = target / rows;
     if (chunks > tiles) chunks = tiles;
     if (chunks < 1) chunks = 1;
     const dim3 grid(static_cast<unsigned>(chunks), static_cast<unsigned>(rows));
