@@ -57,8 +57,8 @@ PUBLISHED_MS_PER_LAYER = (1.365 + 1.814 + 3.600 + 0.143) / 30.0
 # kernel at config 1 (not measured by this script, which runs without ncu).
 NCU_TRAFFIC_CONFIG1 = {
     "score_fused": 16_829_952,
-    "attn_partial": 55_847_168 + 1_044_224,
-    "topk": 2_136_832,
+    "attn_partial": 55_847_680 + 448_768,
+    "topk": 2_134_016,
     "prepack": 67_169_024 + 4_106_752,
 }
 DEFAULT_WORKLOAD = {"context": 32768, "budget": 4096, "batch": 1, "preset": "popkv-q"}
