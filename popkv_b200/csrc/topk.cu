@@ -790,9 +790,10 @@ __global__ void __launch_bounds__(kHistThreads) topk_hist_kernel(
 //     to the threshold the lower ranks hold: the CTA's output offset, with no
 //     further exchange.
 // (3) A block scan of each thread's (greater, equal) counts gives positions
-//     inside the CTA.  The CTA's winners fill one contiguous range of the
-//     output; they are staged in shared memory by position and written out
-//     with coalesced stores.
+//     inside the CTA.  A thread's winners (from bit masks of its keys above and
+//     equal to the threshold) take consecutive output positions, so each
+//     thread stores its few winners directly; a warp's stores cover one short
+//     contiguous range.
 // Every DSMEM access (the reads of the 11-bit histograms, the stores of the
 // small ones) comes before barrier B, the last cluster-wide wait, so no CTA
 // exits while a peer may still touch its shared memory.
@@ -837,13 +838,8 @@ __global__ void __launch_bounds__(kClusterThreads, PER <= 16 ? 4 : 1) topk16_clu
     static_assert(PER % 8 == 0 && PER <= 64, "PER keys per thread, whole uint4 loads");
     static_assert(CPR <= 8, "at most 8 ranks per cluster");
     constexpr int64_t kSlice = static_cast<int64_t>(kClusterThreads) * PER;
-    // Winners staged by output position for coalesced stores (32 KiB at 32 keys
-    // per thread); with 64 keys per thread they are stored directly.
-    constexpr bool kStaged = PER <= 32;
-    constexpr int kStageSlots = kStaged ? kClusterThreads * PER : 1;
     constexpr int kRow2 = 33;
     __shared__ __align__(16) uint32_t hist[kHistBins];
-    __shared__ __align__(16) uint16_t stage[kStageSlots];
     __shared__ uint32_t hist2[kRow2];  // bins 0..31: keys in digit b1 by low 5 bits; [32]: keys above b1
     __shared__ uint32_t hist2_all[CPR * kRow2];  // row c: rank c's `hist2`
     __shared__ uint32_t warp_sums[kClusterWarps + 1];
@@ -888,8 +884,7 @@ __global__ void __launch_bounds__(kClusterThreads, PER <= 16 ? 4 : 1) topk16_clu
         sel_eq_before = 0;
     }
 
-    const int64_t cta_base = static_cast<int64_t>(rank) * kSlice;
-    const int64_t base = cta_base + static_cast<int64_t>(tid) * PER;
+    const int64_t base = static_cast<int64_t>(rank) * kSlice + static_cast<int64_t>(tid) * PER;
     const uint16_t* src = scores + row * row_stride + base;
     const int64_t left = tokens - base;
     const int lim = left <= 0 ? 0 : (left >= PER ? PER : static_cast<int>(left));
@@ -1021,11 +1016,6 @@ __global__ void __launch_bounds__(kClusterThreads, PER <= 16 ? 4 : 1) topk16_clu
     const uint32_t excl = cta_exclusive_scan32((gt << 16) | eq, warp_sums, cta_total);
     const uint32_t rank_gt = sel_gt_before, rank_eq = sel_eq_before;
     const uint32_t gt_before = rank_gt + (excl >> 16), eq_before = rank_eq + (excl & 0xFFFFu);
-    // The CTA's winners: output positions [first, first + count).
-    const uint32_t first = rank_gt + min(rank_eq, need);
-    const uint32_t cta_eq = cta_total & 0xFFFFu;
-    const uint32_t eq_taken = need > rank_eq ? min(need - rank_eq, cta_eq) : 0u;
-    const uint32_t count = (cta_total >> 16) + eq_taken;
     POPKV_TOPK_PHASE(6);
     // This thread's winners: every key above the threshold and its first
     // `take` keys equal to it, at consecutive positions from `pos` on (the
@@ -1041,21 +1031,8 @@ __global__ void __launch_bounds__(kClusterThreads, PER <= 16 ? 4 : 1) topk16_clu
     while (win) {
         const int e = lowest_bit(win);
         win &= win - 1;
-        if (pos < kk) {
-            if constexpr (kStaged) {
-                const uint32_t slot = pos - first;  // in [0, count) by construction
-                if (slot < static_cast<uint32_t>(kStageSlots)) stage[slot] = static_cast<uint16_t>(tid * PER + e);
-            } else {
-                dst[pos] = base + e;
-            }
-        }
+        if (pos < kk) dst[pos] = base + e;
         ++pos;
-    }
-    if constexpr (kStaged) {
-        __syncthreads();
-        const uint32_t n = min(count, static_cast<uint32_t>(kStageSlots));
-        for (uint32_t j = tid; j < n; j += kClusterThreads)
-            if (first + j < kk) dst[first + j] = cta_base + stage[j];
     }
     POPKV_TOPK_PHASE(7);
 }
