@@ -153,6 +153,19 @@ POPKV_API int popkv_score(const void* queries, int queries_dtype, int64_t batch,
                 int64_t dim_group_size, void* scores, int scores_dtype, void* stream);
 
 /*
+ * Which head_dim-128 scorer the score entry points (popkv_score,
+ * popkv_score_encoded, popkv_score_dyn, popkv_score_hist) use, for the whole
+ * process: 0 (default) the faster one for the shape -- the fp8 tensor-core
+ * scorer from about one 128-token tile per SM up (G16: 1024 tiles of
+ * batch x KV heads x tokens/128; G32/G64: 4096), the popcount scorer below --
+ * 1 always the popcount scorer, 2 the fp8 tensor-core scorer wherever it
+ * applies (at most 4 query heads per KV head, 16-byte aligned representative
+ * rows).  All give the same bits; this is a tuning and testing switch.
+ * No reference counterpart.
+ */
+POPKV_API int popkv_score_dispatch(int mode);
+
+/*
  * popkv_score on the popcount scorer only (one token per thread, __popc per
  * count), whatever the shape; bit-identical to popkv_score.  Kept for
  * comparison with the fp8 tensor-core scorer.

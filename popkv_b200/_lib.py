@@ -29,6 +29,7 @@ _SIGNATURES = {
     "popkv_query_encode": ([_P, _I, _L, _L, _L, _P, _P, _P, _P, _P], _I),
     "popkv_score_encoded": ([_P, _P, _P, _P, _L, _L, _P, _P, _P, _P, _L, _L, _P, _L, _L, _P, _P], _I),
     "popkv_score": ([_P, _I, _L, _L, _L, _P, _P, _P, _P, _L, _L, _P, _L, _L, _P, _I, _P], _I),
+    "popkv_score_dispatch": ([_I], _I),
     "popkv_score_popcount": ([_P, _I, _L, _L, _L, _P, _P, _P, _P, _L, _L, _P, _L, _L, _P, _I, _P], _I),
     "popkv_score_tc": ([_P, _I, _L, _L, _L, _P, _P, _P, _P, _L, _L, _P, _L, _L, _P, _I, _P], _I),
     "popkv_topk": ([_P, _I, _L, _L, _L, _L, _L, _P, _L, _P], _I),

@@ -21,6 +21,7 @@
 // count-to-float conversion uses the FP32 pipe (small_int_to_float) instead of
 // the slower integer-conversion unit, leaving the popcount unit as the only
 // narrow pipe.
+#include <atomic>
 #include <cstdint>
 
 #include "common.cuh"
@@ -217,13 +218,24 @@ __global__ void __launch_bounds__(kGenericThreads) score_generic_kernel(
 // Launchers.
 // ---------------------------------------------------------------------------
 
+// Scorer choice for head_dim 128 (popkv_score_dispatch): 0 picks the faster
+// kernel for the shape, 1 always the popcount kernel, 2 the fp8 tensor-core
+// kernel wherever it applies.  All three give the same bits.
+std::atomic<int> g_score_dispatch{0};
+
+inline bool use_tc8(int G, int64_t capacity, int group_heads, int64_t rows, int64_t tokens) {
+    const int mode = g_score_dispatch.load(std::memory_order_relaxed);
+    if (mode == 1 || !score_tc8_eligible(G, capacity, group_heads)) return false;
+    return mode == 2 || score_tc8_pays(G, rows, tokens);
+}
+
 template <int G, typename QT, bool RAW>
 int launch_score128_hist(const void* queries, int64_t batch, int64_t q_heads, const int32_t* k_sign,
                          const int32_t* k_mag, const uint16_t* k_low, const uint16_t* k_delta,
                          int64_t kv_heads, int64_t capacity, const int64_t* head_to_kv,
                          int64_t tokens, uint16_t* scores, uint32_t* hist, cudaStream_t stream) {
     const int group_heads = static_cast<int>(q_heads / kv_heads);
-    if (score_tc8_eligible(G, capacity, group_heads)) {
+    if (use_tc8(G, capacity, group_heads, batch * kv_heads, tokens)) {
         return launch_score128_tc8<G, QT, RAW, true>(
             static_cast<const QT*>(queries), nullptr, nullptr, nullptr, nullptr, batch, q_heads, k_sign, k_mag,
             k_low, k_delta, kv_heads, capacity, head_to_kv, tokens, scores, stream, tokens, nullptr, hist);
@@ -251,7 +263,7 @@ int launch_score128(const void* queries, const int32_t* q_sign, const int32_t* q
                     cudaStream_t stream, int64_t score_stride = -1,
                     const int64_t* dyn_tokens = nullptr, bool popcount_only = false) {
     const int group_heads = static_cast<int>(q_heads / kv_heads);
-    if (!popcount_only && score_tc8_eligible(G, capacity, group_heads)) {
+    if (!popcount_only && use_tc8(G, capacity, group_heads, batch * kv_heads, tokens)) {
         return launch_score128_tc8<G, QT, RAW>(
             static_cast<const QT*>(queries), q_sign, q_mag, q_low, q_delta, batch, q_heads, k_sign, k_mag,
             k_low, k_delta, kv_heads, capacity, head_to_kv, tokens, scores, stream,
@@ -484,6 +496,14 @@ extern "C" int popkv_score_popcount(const void* queries, int queries_dtype, int6
     return popkv::score_entry(queries, queries_dtype, batch, q_heads, head_dim, k_sign, k_mag, k_low,
                               k_delta, kv_heads, capacity, head_to_kv, tokens, dim_group_size, scores,
                               scores_dtype, stream, true);
+}
+
+extern "C" int popkv_score_dispatch(int mode) {
+    using namespace popkv;
+    if (mode < 0 || mode > 2)
+        return fail(POPKV_ERR_INVALID, "popkv_score_dispatch: mode must be 0 (auto), 1 (popcount) or 2 (fp8)");
+    g_score_dispatch.store(mode, std::memory_order_relaxed);
+    return POPKV_OK;
 }
 
 extern "C" int popkv_score_hist(const void* queries, int queries_dtype, int64_t batch, int64_t q_heads,

@@ -499,6 +499,18 @@ inline bool score_tc8_eligible(int G, int64_t capacity, int group_heads) {
     return group_heads <= tc8::kMaxHeads && (row_bytes % 16) == 0;
 }
 
+// Whether the tensor-core scorer is the faster of the two for `rows` (batch x
+// KV heads) rows of `tokens` keys.  Below about one 128-token tile per SM its
+// per-CTA prologue (query encoding, B operand, first plane tile) dominates and
+// the popcount kernel (4 CTAs per SM, lighter prologue) wins; the crossover is
+// later for the coarser groups, whose popcount kernel needs fewer popcounts.
+// Measured on B200 at head_dim 128, 4 query heads per KV head (both kernels
+// give the same bits): G16 from 1024 tiles, G32 and G64 from 4096 tiles.
+inline bool score_tc8_pays(int G, int64_t rows, int64_t tokens) {
+    const int64_t tiles = rows * ((tokens + tc8::kTile - 1) / tc8::kTile);
+    return tiles >= (G == 16 ? 1024 : 4096);
+}
+
 int score_sm_count();
 
 template <int G, typename QT, bool RAW, bool HIST = false>

@@ -256,17 +256,34 @@ def score_encoded(
     return scores
 
 
+_SCORE_DISPATCH = {"auto": 0, "popcount": 1, "fp8": 2}
+
+
+def set_score_dispatch(mode: str) -> None:
+    """Process-wide head_dim-128 scorer choice of every score entry point.
+
+    ``"auto"`` (default): the fp8 tensor-core scorer from about one 128-token
+    tile per SM up, the popcount scorer below; ``"popcount"``: always the
+    popcount scorer; ``"fp8"``: the tensor-core scorer wherever it applies.
+    The bits are the same; this is for tuning and testing.
+    """
+    if mode not in _SCORE_DISPATCH:
+        raise ValueError("mode must be 'auto', 'popcount' or 'fp8'")
+    _lib.check(_lib.lib().popkv_score_dispatch(_SCORE_DISPATCH[mode]))
+
+
 def score(
     queries: torch.Tensor, packed, *, head_to_kv: torch.Tensor, tokens: int,
     dim_group_size: int = 32, dim_kernel: str | None = None, kernel: str = "auto",
 ) -> torch.Tensor:
     """Return approximate QK scores; the head-dim-128 fast path emits FP16, others FP32.
 
-    ``kernel="auto"`` takes the fp8 tensor-core scorer (mma.sync e4m3 counts)
-    where it applies (head_dim 128, <= 8 query heads per KV head) and the
-    popcount scorer elsewhere; ``"popcount"`` forces the popcount scorer and
-    ``"tensor_core"`` (<= 4 query heads per KV head) forms the counts with
-    tcgen05 int8 matrix products.  The scores are identical for all three.
+    ``kernel="auto"`` takes the library's choice for head_dim 128 (see
+    ``set_score_dispatch``): the fp8 tensor-core scorer (tcgen05 e4m3 counts,
+    at most 4 query heads per KV head) when the shape is large enough for it to
+    win, the popcount scorer otherwise; ``"popcount"`` forces the popcount
+    scorer and ``"tensor_core"`` forms the counts with tcgen05 int8 matrix
+    products.  The scores are identical for all of them.
     """
     if kernel not in ("auto", "popcount", "tensor_core"):
         raise ValueError("kernel must be 'auto', 'popcount' or 'tensor_core'")

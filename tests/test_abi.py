@@ -190,3 +190,14 @@ def test_reference_hooks_bind():
     inspect.signature(P.topk).bind(object(), 7)
     with pytest.raises(TypeError):
         inspect.signature(P.topk).bind(object())
+
+
+def test_score_dispatch_switch_validation(lib):
+    """popkv_score_dispatch takes 0 (auto), 1 (popcount) or 2 (fp8) and rejects anything else."""
+    from popkv_b200 import popkv_cuda as C
+    status, message = _status_and_message(lib, lib.popkv_score_dispatch(3))
+    assert status == 1 and "mode must be" in message  # POPKV_ERR_INVALID
+    with pytest.raises(ValueError):
+        C.set_score_dispatch("tensor")
+    for mode in ("popcount", "fp8", "auto"):
+        C.set_score_dispatch(mode)

@@ -217,14 +217,23 @@ def test_tensor_core_score_matches_popcount_kernel(cuda_device, g, batch, tokens
         np.testing.assert_array_equal(bits(mma), want)
 
 
+@pytest.fixture
+def fp8_scorer():
+    """The fp8 tensor-core scorer for every shape it applies to (the automatic
+    choice takes the popcount scorer for small shapes), restored afterwards."""
+    C.set_score_dispatch("fp8")
+    yield
+    C.set_score_dispatch("auto")
+
+
 @pytest.mark.parametrize("g", GROUPS)
 @pytest.mark.parametrize("batch,tokens,group_heads,qdtype,capacity", [
     (1, 1, 4, torch.bfloat16, 128), (1, 127, 4, torch.bfloat16, 132), (1, 129, 4, torch.float16, 256),
     (2, 300, 2, torch.float32, 304), (1, 777, 1, torch.bfloat16, 780), (3, 1000, 4, torch.bfloat16, 1024),
     (1, 515, 5, torch.bfloat16, 520), (2, 260, 8, torch.float16, 264), (1, 1500, 3, torch.bfloat16, 1504),
     (1, 32768, 4, torch.bfloat16, 32768)])
-def test_fp8_score_matches_popcount_kernel_and_oracle(cuda_device, g, batch, tokens, group_heads, qdtype,
-                                                      capacity):
+def test_fp8_score_matches_popcount_kernel_and_oracle(fp8_scorer, cuda_device, g, batch, tokens, group_heads,
+                                                      qdtype, capacity):
     """popkv_score (fp8 tensor-core counts, every capacity here 16-byte aligned per row)
     == popkv_score_popcount == popkv_score_encoded, bit for bit, and == the oracle."""
     kv_heads = 2
@@ -250,7 +259,7 @@ def test_fp8_score_matches_popcount_kernel_and_oracle(cuda_device, g, batch, tok
         np.testing.assert_array_equal(bits(f8), want)
 
 
-def test_fp8_score_special_planes(cuda_device):
+def test_fp8_score_special_planes(fp8_scorer, cuda_device):
     """All-sign, no-sign, all-magnitude and empty-bucket planes (counts at +-16/32/64)."""
     for g in GROUPS:
         keys = torch.zeros(2, 256, 128, dtype=torch.bfloat16, device=cuda_device)
