@@ -319,7 +319,7 @@ def test_topk_matches_oracle(cuda_device, tokens, dtype):
 
 
 @pytest.mark.parametrize("rows,tokens", [(1, 131072), (3, 65536), (32, 32768), (32, 33024), (64, 8191),
-                                         (200, 777), (160, 70000)])
+                                         (200, 777), (160, 70000), (32, 40000), (48, 49152)])
 def test_topk_all_equal_and_row_counts(cuda_device, rows, tokens):
     """Every key equal (all winners are ties, taken in index order) and many cluster shapes."""
     gen = torch.Generator().manual_seed(rows)
@@ -327,6 +327,20 @@ def test_topk_all_equal_and_row_counts(cuda_device, rows, tokens):
     mixed = _tie_heavy_scores(gen, rows, tokens, levels=2).half().to(cuda_device)
     for scores in (flat, mixed):
         for k in sorted({1, tokens // 3, tokens - 1, tokens}):
+            got = C.topk(scores, k, current_index=tokens)
+            want = oracle.topk(bits(scores), k)
+            np.testing.assert_array_equal(got[:, :k].cpu().numpy(), want)
+            assert torch.all(got[:, k] == tokens)
+
+
+@pytest.mark.parametrize("rows,tokens", [(32, 32771), (32, 45000), (40, 49152)])
+def test_topk_rows_just_past_32k_keys(cuda_device, rows, tokens):
+    """The decoder's sparse layers (32 rows of a few tokens over 32768, 4 CTAs at
+    24 keys per thread): the budget's k and a tie-free and a tie-heavy row set."""
+    gen = torch.Generator().manual_seed(tokens)
+    for levels in (None, 4):
+        scores = _tie_heavy_scores(gen, rows, tokens, levels=levels).half().to(cuda_device)
+        for k in (4095, tokens - 1):
             got = C.topk(scores, k, current_index=tokens)
             want = oracle.topk(bits(scores), k)
             np.testing.assert_array_equal(got[:, :k].cpu().numpy(), want)
